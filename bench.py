@@ -1,0 +1,302 @@
+#!/usr/bin/env python
+"""Decode throughput of the device-resident llmdot path (BASELINE.json metric:
+decode tok/s at batch 1 / 32 on 1..8 B200, achieved HBM GB/s vs peak).
+
+Default workload: Llama-3.2-1B-shape synthetic Q4_K_M
+GGUF, batch 1, 512-token random prompt, greedy decode, fp16 KV of 4096
+positions.  A "step" is one greedy decode token for every session of the GPU.
+
+    python bench.py [--gpus N --steps K --warmup W] [--batch B] [--config NAME]
+    python bench.py --impl reference ...   # the reference's CPU algorithm (oracle port)
+
+Under torchrun each rank drives its own GPU with its own sessions (session
+data parallelism, no collective on the data path: weak scaling); rank 0 prints
+one JSON line with value = all ranks' tokens / the slowest rank's device time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from dotllm_b200 import synth  # noqa: E402
+
+WORKLOADS = {
+    "llama1b": "Llama-3.2-1B-shape synthetic Q4_K_M GGUF (16 layers, d2048, 32q/8kv heads, hd64, FFN 8192, "
+               "vocab 128256 tied; Q4_K, attn_v/ffn_down Q6_K), {prompt}-token random prompt, greedy decode, "
+               "{kv} KV cache of {ctx} positions, batch {batch} per GPU",
+    "tiny": "tiny LLaMA-like synthetic GGUF (6 layers, d512), {prompt}-token prompt, greedy decode, {kv} KV, batch {batch}",
+    "phi3mini": "Phi-3-mini-shape synthetic Q4_K_M GGUF, {prompt}-token prompt, greedy decode, {kv} KV, batch {batch}",
+    "gemma2b": "Gemma-2-2B-shape synthetic Q4_K_M GGUF, {prompt}-token prompt, greedy decode, {kv} KV, batch {batch}",
+    "llama8b": "Llama-3-8B-shape synthetic Q4_K_M GGUF, {prompt}-token prompt, greedy decode, {kv} KV, batch {batch}",
+}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=10)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = [r.split(",") for r in (getattr(self, "out", "") or "").strip().splitlines()]
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline_sample(path: str, cfg, threads: int, n_prompt: int, n_decode: int):
+    """Time the oracle (C restatement of the reference's managed CPU path) on a bounded sample:
+    n_prompt prefill tokens then n_decode greedy steps; returns decode tok/s."""
+    from oracle import oracle as O
+    O.set_threads(threads)
+    m = O.Model(path)
+    s = O.Session(m)
+    prompt = synth.prompt_tokens(cfg, n_prompt)
+    t0 = time.perf_counter()
+    logits = None
+    for i, t in enumerate(prompt):
+        logits = s.process_token(int(t), i)
+    t1 = time.perf_counter()
+    tok = int(np.argmax(logits))
+    for j in range(n_decode):
+        logits = s.process_token(tok, n_prompt + j)
+        tok = int(np.argmax(logits))
+    t2 = time.perf_counter()
+    s.close()
+    m.close()
+    return {"decode_tok_s": n_decode / (t2 - t1), "prefill_tok_s": n_prompt / (t1 - t0),
+            "decode_s_per_tok": (t2 - t1) / n_decode}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    cfg = synth.get(args.config)
+    path = synth.build_model(cfg)
+    from oracle import oracle as O
+    O.build()
+    threads = max(1, O.max_threads())
+    n_prompt = 8
+    # warm-up: W decode steps (bounded), then K decode steps sized to a few minutes of CPU time
+    probe = cpu_baseline_sample(path, cfg, threads, n_prompt, max(1, min(args.warmup, 3)))
+    budget_s = 120.0
+    k = max(1, min(args.steps, int(budget_s / max(probe["decode_s_per_tok"], 1e-6))))
+    res = cpu_baseline_sample(path, cfg, threads, n_prompt, k)
+    v = res["decode_tok_s"]
+    line = {
+        "impl": "reference", "metric": "decode tok/s", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": k, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.config, "batch": 1, "kv": "f32 (reference KvCache)"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"{n_prompt}-token prompt then {k} greedy decode steps of the {args.config} model "
+                                   f"(C restatement of llmdot's managed CPU path, row-parallel OpenMP, {threads} threads)"},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "prefill_tok_s": res["prefill_tok_s"],
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="llama1b")
+    ap.add_argument("--batch", type=int, default=1, help="sessions per GPU")
+    ap.add_argument("--prompt", type=int, default=None)
+    ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    cfg = synth.get(args.config)
+    n_prompt = args.prompt if args.prompt is not None else cfg.prompt_len
+    dist = None
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    # rank 0 writes the synthetic GGUF (spawned workers, before any CUDA work), the others reuse it
+    if rank == 0:
+        path = synth.build_model(cfg)
+    if dist:
+        dist.barrier()
+    path = synth.build_model(cfg)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # single-threaded, like the reference (no threading in its src/): ~10-30 s of CPU work
+        n_pre, n_dec = (2, 3) if cfg.hidden >= 2048 else (8, 16)
+        r = cpu_baseline_sample(path, cfg, 1, n_pre, n_dec)
+        cpu = {"value": r["decode_tok_s"], "unit": "tok/s", "cores": 1, "kind": "port",
+               "sample": f"{n_pre}-token prompt then {n_dec} greedy decode steps of the same model, C restatement of "
+                         f"llmdot's managed CPU path (oracle/), 1 thread"}
+
+    from dotllm_b200.engine import CudaModel, decode_batch, decode_steps
+    m = CudaModel.load(path, device=local)
+    ctx = min(cfg.context, 4096) if args.config == "llama1b" else cfg.context
+    B = args.batch
+    sessions = [m.session(max_ctx=ctx, kv=args.kv) for _ in range(B)]
+    prompts = [synth.prompt_tokens(cfg, n_prompt, session=rank * B + i) for i in range(B)]
+    t0 = time.perf_counter()
+    first = [s.prefill(p)[0] for s, p in zip(sessions, prompts)]
+    prefill_s = time.perf_counter() - t0
+    toks, _, _ = decode_steps(sessions, first, args.warmup)
+    cur = toks[-1]
+
+    if dist:
+        import torch
+        dist.barrier()
+        torch.cuda.synchronize()
+    gpu_index = local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            gpu_index = int(vis.split(",")[local])
+        except ValueError:
+            pass
+    with ClockSampler(gpu_index) as clk:
+        out, dev_ms, kps = decode_steps(sessions, cur, args.steps)
+    if dist:
+        import torch
+        t = torch.tensor([dev_ms], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms = float(t.item())
+    cur = out[-1]
+
+    # end to end through the public per-step API: host tokens in, host ids out, every step
+    if dist:
+        dist.barrier()
+    e2e_steps = args.steps
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        cur, _ = decode_batch(sessions, cur)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        import torch
+        t = torch.tensor([e2e_s], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    # roofline of the dominant kernel family: the quantised matvec launches of one step,
+    # each timed live with CUDA events (profile_matvec), aggregated over the step's launches
+    c = m.config
+    per_layer = ["attn_qkv"] if c["qkv_fused"] else ["attn_q", "attn_k", "attn_v"]
+    per_layer += ["attn_output", "ffn_gate", "ffn_up", "ffn_down"]
+    tot_ms, tot_bytes, launches = 0.0, 0, 0
+    for name in per_layer:
+        ms, nb = m.profile_matvec(f"blk.0.{name}.weight", B, 20)
+        tot_ms += ms * c["layers"]
+        tot_bytes += nb * c["layers"]
+        launches += c["layers"]
+    head = "token_embd.weight" if c["tied"] else "output.weight"
+    ms, nb = m.profile_matvec(head, B, 10)
+    tot_ms += ms
+    tot_bytes += nb
+    launches += 1
+    peak, peak_kind = peaks()
+    achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
+
+    K = args.steps
+    step_ms = dev_ms / K
+    layer_b, head_b = m.weight_bytes()
+    kv_bytes_per_elem = 2 if args.kv == "f16" else 4
+    kv_dim = c["heads_kv"] * c["head_dim"]
+    mean_pos = n_prompt + args.warmup + K / 2.0
+    kv_read = B * c["layers"] * 2 * kv_dim * kv_bytes_per_elem * mean_pos
+    step_bytes = layer_b + head_b + kv_read
+    value = B * K * world / (dev_ms * 1e-3)
+    line = {
+        "metric": f"decode tok/s (batch {B})", "value": value, "unit": "tok/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_K/Q6_K, uniform random prompt ids",
+        "config": {"workload": WORKLOADS.get(args.config, args.config).format(prompt=n_prompt, kv=args.kv, ctx=ctx,
+                                                                              batch=B),
+                   "model": args.config, "global_batch": B * world, "seq_len": n_prompt, "kv": args.kv,
+                   "parallelism": f"dp{world} (independent sessions per GPU)",
+                   "l2": f"weights ({(layer_b + head_b) / 1e6:.0f} MB) exceed L2 (126 MB): inputs larger than L2, no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "quantised matvec (all launches of one step)",
+                     "launches_per_step": launches, "bytes_per_step": tot_bytes,
+                     "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind},
+        "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (step_ms * 1e-3) / 1e9,
+                          "frac": step_bytes / (step_ms * 1e-3) / 1e9 / peak,
+                          "note": "quantised weights + KV reads at the mean position / device step time"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": B * e2e_steps * world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": B * (4 + 4 + 32),
+                "d2h_bytes_per_step": B * 4},
+        "gpu_launches": kps * K,
+        "kernels_per_step": kps,
+        "clocks": clk.summary(),
+        "prefill_tok_s": B * n_prompt / prefill_s,
+    }
+    for s in sessions:
+        s.close()
+    m.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

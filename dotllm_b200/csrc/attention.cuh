@@ -1,0 +1,37 @@
+// attention.cuh -- paged KV cache views and the decode-attention launchers.
+#pragma once
+#include "common.cuh"
+
+namespace llmdot {
+
+// Positions per KV page.  A page of one KV head holds KV_PAGE consecutive positions,
+// head_dim contiguous elements each, so one page is one contiguous run per head.
+constexpr int KV_PAGE = 64;
+
+// Device-side view of one session's cache (one entry per batch row).
+struct KvView {
+    void *k;              // base of the session's K pool, element type = kv_type
+    void *v;              // base of the V pool
+    const int32_t *pages; // logical page -> physical page
+    int64_t layer_stride; // elements per layer = n_pages * heads_kv * KV_PAGE * head_dim
+};
+
+struct AttnShape {
+    int heads, heads_kv, head_dim, max_ctx, sliding_window, has_cap;
+    float cap, inv_sqrt_hd;
+    int rope_half;
+};
+
+// RoPE of q (in place) and k, then k and v appended to the cache at pos[b].
+int launch_rope_append(float *q, int ldq, const float *k, const float *v, int ldkv, const int32_t *pos,
+                       const float *cos_t, const float *sin_t, const KvView *views, int layer, int kv_type,
+                       const AttnShape &sh, int batch, cudaStream_t st);
+
+// softmax(q K^T * 1/sqrt(hd), softcap) V over the window of every session, written to
+// out[b][h*hd + d].  Scratch: scores [batch][heads][max_ctx], part_o
+// [batch][heads][max_ctx/KV_PAGE][head_dim], part_m/part_s [batch][heads][max_ctx/KV_PAGE].
+int launch_attention_decode(const float *q, int ldq, const int32_t *pos, const KvView *views, int layer, int kv_type,
+                            const AttnShape &sh, int batch, float *scores, float *part_m, float *part_s, float *part_o,
+                            float *out, int ldo, cudaStream_t st);
+
+}  // namespace llmdot

@@ -1,0 +1,324 @@
+// engine.cu -- model upload, sessions, and the decode step (the device-resident
+// counterpart of InferenceEngine.ProcessToken, src/Llmdot.Core/Inference/InferenceEngine.cs:134-602).
+#include <math.h>
+#include <string.h>
+#include <strings.h>
+
+#include <algorithm>
+
+#include "engine.cuh"
+#include "gemv.cuh"
+#include "ops.cuh"
+
+namespace llmdot {
+
+static int dmalloc(std::vector<void *> &allocs, void **p, size_t bytes)
+{
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(LLMDOT_E_NOMEM, std::string("cudaMalloc(") + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    }
+    allocs.push_back(*p);
+    return LLMDOT_OK;
+}
+
+template <typename T> static int dalloc(std::vector<void *> &a, T **p, size_t n)
+{
+    return dmalloc(a, (void **)p, n * sizeof(T));
+}
+
+static const llmdot_tensor_desc *find_desc(const llmdot_tensor_desc *t, int n, const std::string &name)
+{
+    for (int i = 0; i < n; i++)
+        if (t[i].name && strcasecmp(t[i].name, name.c_str()) == 0) return &t[i];  // OrdinalIgnoreCase
+    return nullptr;
+}
+
+static int upload_mat(llmdot_model *m, const llmdot_tensor_desc *d, DevMat &out, int expect_cols, int expect_rows)
+{
+    if (!d) return LLMDOT_OK;
+    m->by_name[d->name] = &out;
+    if (d->n_dims < 2) return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": expected a 2-D weight");
+    out.type = d->type;
+    out.cols = (int)d->dims[0];
+    out.rows = (int)d->dims[1];
+    if (block_elems(out.type) == 0 || out.type == T_F16 || out.type == T_BF16)
+        return fail(LLMDOT_E_UNSUPPORTED, std::string(d->name) + ": weight type " + std::to_string(out.type) +
+                                              " is not supported by the device matvec");
+    if ((expect_cols > 0 && out.cols != expect_cols) || (expect_rows > 0 && out.rows != expect_rows))
+        return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": unexpected shape " + std::to_string(out.cols) + "x" +
+                                         std::to_string(out.rows));
+    if (out.cols % (int)block_elems(out.type) != 0)
+        return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": columns not a multiple of the block size");
+    out.rbytes = row_bytes(out.type, (uint64_t)out.cols);
+    uint64_t nb = out.rbytes * (uint64_t)out.rows;
+    if (!d->data || d->n_bytes < nb) return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": data too short");
+    // 256 zeroed bytes of slack: the Q3_K decoder reads one byte past each block
+    LLMDOT_TRY(dmalloc(m->allocs, (void **)&out.raw, nb + 256));
+    LLMDOT_CUDA_TRY(cudaMemsetAsync(out.raw + nb, 0, 256, m->stream));
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(out.raw, d->data, nb, cudaMemcpyHostToDevice, m->stream));
+    LLMDOT_TRY(prepare_tiled(m, out));
+    return LLMDOT_OK;
+}
+
+// LoadedModel.GetDequantizedWeights (LoadedModel.cs:63-75) for norm vectors.
+static int upload_vec(llmdot_model *m, const llmdot_tensor_desc *d, float **out, int n)
+{
+    if (!d) return LLMDOT_OK;
+    uint64_t elems = 1;
+    for (uint32_t i = 0; i < d->n_dims; i++) elems *= d->dims[i];
+    if ((int)elems != n) return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": unexpected length");
+    uint64_t nb = row_bytes(d->type, elems);
+    if (nb == 0) return fail(LLMDOT_E_UNSUPPORTED, std::string(d->name) + ": unsupported type");
+    if (!d->data || d->n_bytes < nb) return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": data too short");
+    LLMDOT_TRY(dalloc(m->allocs, out, (size_t)n));
+    if (d->type == T_F32) {
+        LLMDOT_CUDA_TRY(cudaMemcpyAsync(*out, d->data, nb, cudaMemcpyHostToDevice, m->stream));
+        return LLMDOT_OK;
+    }
+    uint8_t *tmp = nullptr;
+    LLMDOT_CUDA_TRY(cudaMalloc(&tmp, nb));
+    cudaMemcpyAsync(tmp, d->data, nb, cudaMemcpyHostToDevice, m->stream);
+    int rc = launch_dequant(tmp, *out, d->type, 1, n, m->stream);
+    cudaStreamSynchronize(m->stream);
+    cudaFree(tmp);
+    return rc;
+}
+
+int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc *t, int n, llmdot_model **out)
+{
+    *out = nullptr;
+    if (!cfg || !t || n <= 0) return fail(LLMDOT_E_INVALID, "model_load: null config or tensors");
+    const llmdot_config &c = *cfg;
+    if (c.template_id != 0 && c.template_id != 2)
+        return fail(LLMDOT_E_UNSUPPORTED, "model_load: only the LlamaLike and GemmaLike execution templates run on the device");
+    if (c.expert_count > 0) return fail(LLMDOT_E_UNSUPPORTED, "model_load: MoE models are not supported on the device");
+    if (!c.norm_is_rms) return fail(LLMDOT_E_UNSUPPORTED, "model_load: LayerNorm models are not supported on the device");
+    if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.heads_kv <= 0 || c.head_dim <= 0 || c.vocab <= 0 ||
+        c.context <= 0 || c.heads % c.heads_kv != 0)
+        return fail(LLMDOT_E_FORMAT, "model_load: invalid dimensions in config");
+    if (c.ffn_type == 0) return fail(LLMDOT_E_UNSUPPORTED, "model_load: non-gated FFN is not supported on the device");
+    int rd = c.rope_dim > 0 ? c.rope_dim : c.head_dim;
+    if (rd > c.head_dim || rd % 2) return fail(LLMDOT_E_FORMAT, "model_load: bad rope dimension");
+    if (c.head_dim % 8 != 0) return fail(LLMDOT_E_UNSUPPORTED, "model_load: head_dim must be a multiple of 8");
+
+    LLMDOT_CUDA_TRY(cudaSetDevice(device));
+    llmdot_model *m = new llmdot_model();
+    m->device = device;
+    m->cfg = c;
+    int rc = LLMDOT_OK;
+    auto bail = [&](int code) { model_destroy(m); return code; };
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(LLMDOT_E_CUDA, "stream create failed"));
+
+    const int qDim = c.heads * c.head_dim, kvDim = c.heads_kv * c.head_dim, H = c.hidden;
+    auto D = [&](const std::string &s) { return find_desc(t, n, s); };
+    const llmdot_tensor_desc *emb = D("token_embd.weight");
+    if (!emb) return bail(fail(LLMDOT_E_FORMAT, "token_embd.weight missing"));
+    if ((rc = upload_mat(m, emb, m->emb, H, c.vocab))) return bail(rc);
+    const llmdot_tensor_desc *outw = nullptr;
+    for (int i = 0; i < n; i++)
+        if (t[i].name && strcmp(t[i].name, "output.weight") == 0) outw = &t[i];
+    if (outw && (rc = upload_mat(m, outw, m->out, H, c.vocab))) return bail(rc);
+    const llmdot_tensor_desc *on = D("output_norm.weight");
+    if (!on) on = D("token_embd_norm.weight");
+    if (!on) return bail(fail(LLMDOT_E_FORMAT, "output_norm.weight missing"));
+    if ((rc = upload_vec(m, on, &m->out_norm, H))) return bail(rc);
+
+    m->layers.resize(c.layers);
+    for (int l = 0; l < c.layers; l++) {
+        LayerW &L = m->layers[l];
+        std::string p = "blk." + std::to_string(l) + ".";
+        if (D(p + "attn_q_norm.weight") || D(p + "attn_k_norm.weight"))
+            return bail(fail(LLMDOT_E_UNSUPPORTED, "q/k norm tensors are not supported on the device"));
+        if (!D(p + "attn_norm.weight")) return bail(fail(LLMDOT_E_FORMAT, p + "attn_norm.weight missing"));
+        if ((rc = upload_vec(m, D(p + "attn_norm.weight"), &L.attn_norm, H))) return bail(rc);
+        if ((rc = upload_vec(m, D(p + "ffn_norm.weight"), &L.ffn_norm, H))) return bail(rc);
+        if (c.template_id == 2 && c.has_post_norm) {
+            if ((rc = upload_vec(m, D(p + "post_attention_norm.weight"), &L.post_attn, H))) return bail(rc);
+            if ((rc = upload_vec(m, D(p + "post_ffw_norm.weight"), &L.post_ffw, H))) return bail(rc);
+        }
+        if (c.qkv_fused) {
+            if (!D(p + "attn_qkv.weight")) return bail(fail(LLMDOT_E_FORMAT, p + "attn_qkv.weight missing"));
+            if ((rc = upload_mat(m, D(p + "attn_qkv.weight"), L.qkv, H, qDim + 2 * kvDim))) return bail(rc);
+        } else {
+            if (!D(p + "attn_q.weight") || !D(p + "attn_k.weight") || !D(p + "attn_v.weight"))
+                return bail(fail(LLMDOT_E_FORMAT, p + "attn_q/k/v missing"));
+            if ((rc = upload_mat(m, D(p + "attn_q.weight"), L.q, H, qDim))) return bail(rc);
+            if ((rc = upload_mat(m, D(p + "attn_k.weight"), L.k, H, kvDim))) return bail(rc);
+            if ((rc = upload_mat(m, D(p + "attn_v.weight"), L.v, H, kvDim))) return bail(rc);
+        }
+        if (!D(p + "attn_output.weight") || !D(p + "ffn_gate.weight") || !D(p + "ffn_up.weight") ||
+            !D(p + "ffn_down.weight"))
+            return bail(fail(LLMDOT_E_FORMAT, p + "attention output / FFN tensors missing"));
+        if ((rc = upload_mat(m, D(p + "attn_output.weight"), L.o, qDim, H))) return bail(rc);
+        if ((rc = upload_mat(m, D(p + "ffn_gate.weight"), L.gate, H, c.ffn))) return bail(rc);
+        if ((rc = upload_mat(m, D(p + "ffn_up.weight"), L.up, H, c.ffn))) return bail(rc);
+        if ((rc = upload_mat(m, D(p + "ffn_down.weight"), L.down, c.ffn, H))) return bail(rc);
+        for (const DevMat *w : {&L.q, &L.k, &L.v, &L.qkv, &L.o, &L.gate, &L.up, &L.down})
+            if (w->valid()) m->layer_bytes += w->bytes();
+        m->layer_bytes += (uint64_t)H * 4 * (L.post_attn ? 4 : 2);
+    }
+    m->head_bytes = (m->out.valid() ? m->out.bytes() : m->emb.bytes()) + (uint64_t)H * 4;
+
+    // RoPE tables: PrecomputeRopeFrequencies (InferenceEngine.cs:57-72), then
+    // MathF.Cos/Sin of position*freq (TensorOps.cs:688-693), evaluated on the host
+    // with the same C runtime functions the reference calls.
+    m->rope_half = rd / 2;
+    m->max_ctx = (c.context + KV_PAGE - 1) / KV_PAGE * KV_PAGE;
+    {
+        std::vector<float> freq(m->rope_half), cs((size_t)m->max_ctx * m->rope_half), sn(cs.size());
+        for (int i = 0; i < m->rope_half; i++) {
+            float f = 1.0f / powf(c.rope_base, 2.0f * (float)i / (float)rd);
+            if (c.rope_scaling == 1 && c.rope_factor > 1.0f) f /= c.rope_factor;
+            freq[i] = f;
+        }
+        for (int p = 0; p < m->max_ctx; p++)
+            for (int i = 0; i < m->rope_half; i++) {
+                float a = (float)p * freq[i];
+                cs[(size_t)p * m->rope_half + i] = cosf(a);
+                sn[(size_t)p * m->rope_half + i] = sinf(a);
+            }
+        if ((rc = dalloc(m->allocs, &m->cos_t, cs.size())) || (rc = dalloc(m->allocs, &m->sin_t, sn.size())))
+            return bail(rc);
+        cudaMemcpy(m->cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(m->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+    }
+    if (cudaStreamSynchronize(m->stream) != cudaSuccess) return bail(cuda_fail(cudaGetLastError(), "model upload"));
+    if ((rc = ensure_workspace(m, 1))) return bail(rc);
+    *out = m;
+    return LLMDOT_OK;
+}
+
+void model_destroy(llmdot_model *m)
+{
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (void *p : m->ws.allocs) cudaFree(p);
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+int ensure_workspace(llmdot_model *m, int batch)
+{
+    Workspace &w = m->ws;
+    if (w.batch >= batch) return LLMDOT_OK;
+    cudaStreamSynchronize(m->stream);
+    for (void *p : w.allocs) cudaFree(p);
+    w = Workspace();
+    const llmdot_config &c = m->cfg;
+    const size_t B = (size_t)batch, qDim = (size_t)c.heads * c.head_dim, kvDim = (size_t)c.heads_kv * c.head_dim;
+    const size_t nchunk = (size_t)m->max_ctx / KV_PAGE;
+    auto &a = w.allocs;
+    LLMDOT_TRY(dalloc(a, &w.h, B * c.hidden));
+    LLMDOT_TRY(dalloc(a, &w.xn, B * c.hidden));
+    LLMDOT_TRY(dalloc(a, &w.q, B * qDim));
+    LLMDOT_TRY(dalloc(a, &w.k, B * kvDim));
+    LLMDOT_TRY(dalloc(a, &w.v, B * kvDim));
+    LLMDOT_TRY(dalloc(a, &w.qkv, B * (qDim + 2 * kvDim)));
+    LLMDOT_TRY(dalloc(a, &w.attn, B * qDim));
+    LLMDOT_TRY(dalloc(a, &w.gate, B * c.ffn));
+    LLMDOT_TRY(dalloc(a, &w.up, B * c.ffn));
+    LLMDOT_TRY(dalloc(a, &w.logits, B * c.vocab));
+    LLMDOT_TRY(dalloc(a, &w.scores, B * c.heads * (size_t)m->max_ctx));
+    LLMDOT_TRY(dalloc(a, &w.part_m, B * c.heads * nchunk));
+    LLMDOT_TRY(dalloc(a, &w.part_s, B * c.heads * nchunk));
+    LLMDOT_TRY(dalloc(a, &w.part_o, B * c.heads * nchunk * c.head_dim));
+    LLMDOT_TRY(dalloc(a, &w.keys, B));
+    LLMDOT_TRY(dalloc(a, &w.tokens, B));
+    LLMDOT_TRY(dalloc(a, &w.pos, B));
+    LLMDOT_TRY(dalloc(a, &w.next, B));
+    LLMDOT_TRY(dalloc(a, &w.views, B));
+    LLMDOT_TRY(dalloc(a, &w.err, 1));
+    LLMDOT_TRY(dalloc(a, &w.hist, (size_t)HIST_STEPS * B));
+    LLMDOT_TRY(dalloc(a, &w.hist_step, 1));
+    LLMDOT_CUDA_TRY(cudaMemset(w.err, 0, sizeof(int)));
+    LLMDOT_CUDA_TRY(cudaMemset(w.hist_step, 0, sizeof(int32_t)));
+    w.batch = batch;
+    return LLMDOT_OK;
+}
+
+int gemv(const DevMat &W, const float *x, int ldx, int nv, float *y, int ldy, bool accumulate, bool fast, cudaStream_t st)
+{
+    if (fast && W.tiled && gemv_fast_supported(W, nv)) return launch_gemv_fast(W, x, ldx, nv, y, ldy, accumulate, st);
+    return launch_gemv_ref(W.raw, W.type, W.rows, W.cols, x, ldx, nv, y, ldy, accumulate, st);
+}
+
+// ProcessToken (InferenceEngine.cs:134-146) for `batch` independent sessions at once.
+int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens, const int32_t *pos,
+                 const KvView *views, int32_t *next, cudaStream_t st)
+{
+    const llmdot_config &c = m->cfg;
+    Workspace &w = m->ws;
+    const int H = c.hidden, qDim = c.heads * c.head_dim, kvDim = c.heads_kv * c.head_dim;
+    const bool gemma = c.template_id == 2;
+    const bool fast = m->use_fast_gemv;
+    AttnShape sh;
+    sh.heads = c.heads;
+    sh.heads_kv = c.heads_kv;
+    sh.head_dim = c.head_dim;
+    sh.max_ctx = m->max_ctx;
+    sh.sliding_window = c.sliding_window;
+    sh.has_cap = c.has_attn_cap;
+    sh.cap = c.attn_cap;
+    sh.inv_sqrt_hd = 1.0f / sqrtf((float)c.head_dim);
+    sh.rope_half = m->rope_half;
+
+    // GetEmbedding + EmbeddingScale
+    LLMDOT_TRY(launch_embed(m->emb.raw, m->emb.type, H, c.vocab, tokens, batch, c.emb_scale, w.h, H, w.err, st));
+    for (int l = 0; l < c.layers; l++) {
+        const LayerW &L = m->layers[l];
+        // ApplyNorm(attn_norm) :544-562
+        LLMDOT_TRY(launch_rmsnorm(w.h, H, L.attn_norm, w.xn, H, H, batch, c.eps, st));
+        // Q/K/V projections :321-353
+        float *q, *k, *v;
+        int ldq, ldkv;
+        if (L.qkv.valid()) {
+            LLMDOT_TRY(gemv(L.qkv, w.xn, H, batch, w.qkv, qDim + 2 * kvDim, false, fast, st));
+            q = w.qkv;
+            k = w.qkv + qDim;
+            v = w.qkv + qDim + kvDim;
+            ldq = ldkv = qDim + 2 * kvDim;
+        } else {
+            LLMDOT_TRY(gemv(L.q, w.xn, H, batch, w.q, qDim, false, fast, st));
+            LLMDOT_TRY(gemv(L.k, w.xn, H, batch, w.k, kvDim, false, fast, st));
+            LLMDOT_TRY(gemv(L.v, w.xn, H, batch, w.v, kvDim, false, fast, st));
+            q = w.q;
+            k = w.k;
+            v = w.v;
+            ldq = qDim;
+            ldkv = kvDim;
+        }
+        // RoPE of q and k, K/V cache append :362-382
+        LLMDOT_TRY(launch_rope_append(q, ldq, k, v, ldkv, pos, m->cos_t, m->sin_t, views, l, kv_type, sh,
+                                      batch, st));
+        // attention :384-442
+        LLMDOT_TRY(launch_attention_decode(q, ldq, pos, views, l, kv_type, sh, batch, w.scores, w.part_m,
+                                           w.part_s, w.part_o, w.attn, qDim, st));
+        // attn_output matvec + residual add :444-449, :189
+        LLMDOT_TRY(gemv(L.o, w.attn, qDim, batch, w.h, H, true, fast, st));
+        if (gemma && L.post_attn) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_attn, w.h, H, H, batch, c.eps, st));
+        // ApplyNorm(ffn_norm ?? attn_norm)
+        LLMDOT_TRY(launch_rmsnorm(w.h, H, L.ffn_norm ? L.ffn_norm : L.attn_norm, w.xn, H, H, batch, c.eps, st));
+        // FfnForward :452-487: gate, act, up, mul, down + residual add
+        LLMDOT_TRY(gemv(L.gate, w.xn, H, batch, w.gate, c.ffn, false, fast, st));
+        LLMDOT_TRY(gemv(L.up, w.xn, H, batch, w.up, c.ffn, false, fast, st));
+        LLMDOT_TRY(launch_act_mul(c.ffn_type == 2, w.gate, w.up, w.gate, c.ffn, batch, st));
+        LLMDOT_TRY(gemv(L.down, w.gate, c.ffn, batch, w.h, H, true, fast, st));
+        if (gemma && L.post_ffw) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_ffw, w.h, H, H, batch, c.eps, st));
+    }
+    // ApplyFinalNorm :575-581, ComputeLogits :583-602
+    LLMDOT_TRY(launch_rmsnorm(w.h, H, m->out_norm, w.xn, H, H, batch, c.eps, st));
+    const DevMat &head = m->out.valid() ? m->out : m->emb;
+    LLMDOT_TRY(gemv(head, w.xn, H, batch, w.logits, c.vocab, false, fast, st));
+    // final softcap + greedy argmax (InferenceEngine.cs:105-108, Sampler.cs:26-27)
+    LLMDOT_TRY(launch_argmax(w.logits, c.vocab, c.vocab, batch, w.keys, next, c.has_final_cap != 0, c.final_cap,
+                             nullptr, st));
+    return LLMDOT_OK;
+}
+
+}  // namespace llmdot

@@ -1,0 +1,84 @@
+// engine.cuh -- device-resident model, sessions and the decode step.
+#pragma once
+#include <map>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+
+namespace llmdot {
+
+// One weight matrix on the device: `rows` output features of `cols` inputs, stored
+// exactly as GGUF holds it (row-major, quantised blocks), plus an optional copy
+// re-laid out in 16-row tiles for the tensor-core matvec (see gemv.cu).
+struct DevMat {
+    uint32_t type = 0;
+    int rows = 0, cols = 0;
+    uint64_t rbytes = 0;
+    uint8_t *raw = nullptr;
+    uint8_t *tiled = nullptr;
+    bool valid() const { return raw != nullptr; }
+    uint64_t bytes() const { return rbytes * (uint64_t)rows; }
+};
+
+struct LayerW {
+    DevMat q, k, v, qkv, o, gate, up, down;
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *post_attn = nullptr, *post_ffw = nullptr;
+};
+
+// Step scratch, sized for `batch` rows.
+struct Workspace {
+    int batch = 0;
+    float *h = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qkv = nullptr, *attn = nullptr;
+    float *gate = nullptr, *up = nullptr, *logits = nullptr;
+    float *scores = nullptr, *part_m = nullptr, *part_s = nullptr, *part_o = nullptr;
+    unsigned long long *keys = nullptr;
+    int32_t *tokens = nullptr, *pos = nullptr, *next = nullptr;
+    KvView *views = nullptr;
+    int *err = nullptr;
+    int32_t *hist = nullptr;   // [HIST_STEPS][batch] greedy ids recorded by captured steps
+    int32_t *hist_step = nullptr;
+    std::vector<void *> allocs;
+};
+constexpr int HIST_STEPS = 4096;
+
+}  // namespace llmdot
+
+struct llmdot_model {
+    int device = 0;
+    llmdot_config cfg{};
+    cudaStream_t stream = nullptr;
+    std::vector<llmdot::LayerW> layers;
+    llmdot::DevMat emb, out;
+    float *out_norm = nullptr;
+    float *cos_t = nullptr, *sin_t = nullptr;
+    int rope_half = 0;
+    int max_ctx = 0;  // context rounded up to whole KV pages
+    uint64_t layer_bytes = 0, head_bytes = 0;
+    std::vector<void *> allocs;
+    std::map<std::string, llmdot::DevMat *> by_name;
+    llmdot::Workspace ws;
+    bool use_fast_gemv = true;
+};
+
+struct llmdot_session {
+    llmdot_model *m = nullptr;
+    int max_ctx = 0, kv_type = 0, n_pages = 0, pos = 0;
+    void *k = nullptr, *v = nullptr;
+    int32_t *pages = nullptr;
+    llmdot::KvView view{};
+};
+
+namespace llmdot {
+int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc *t, int n, llmdot_model **out);
+void model_destroy(llmdot_model *m);
+int ensure_workspace(llmdot_model *m, int batch);
+// One forward step (ProcessToken) for `batch` rows: token ids, positions and KV views are
+// device arrays of `batch` entries.  Raw logits land in ws.logits, greedy ids in next.
+// tokens may alias next (the step reads its tokens before it writes the argmax).
+int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens, const int32_t *pos,
+                 const KvView *views, int32_t *next, cudaStream_t st);
+int gemv(const DevMat &W, const float *x, int ldx, int nv, float *y, int ldy, bool accumulate, bool fast,
+         cudaStream_t st);
+}  // namespace llmdot

@@ -1,0 +1,154 @@
+"""Device-resident decode/prefill over the C ABI (Tier B).
+
+Mirrors the reference's engine surface: ``LoadedModel.Load`` ->
+``CudaModel.load``; ``new InferenceEngine(model, backend)`` + ``Generate`` ->
+``CudaSession.generate`` (greedy, src/Llmdot.Core/Inference/InferenceEngine.cs:74-132);
+the per-token ``ProcessToken`` -> ``prefill`` / ``decode``.  Everything runs
+in the native library on the GPU; there is no CPU path here.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from .native import (KV_F16, KV_F32, LlmdotConfig, TensorDesc, VP, F32P, I32P, check, lib)
+
+
+class CudaModel:
+    def __init__(self, handle: int, device: int):
+        self._h = C.c_void_p(handle)
+        self.device = device
+        cfg = LlmdotConfig()
+        check(lib().llmdot_cuda_model_config(self._h, C.byref(cfg)))
+        self.config = cfg.as_dict()
+
+    @classmethod
+    def load(cls, path: str, device: int = 0) -> "CudaModel":
+        """LoadedModel.Load + upload: native GGUF parse, tensors streamed to the device."""
+        h = VP()
+        check(lib().llmdot_cuda_model_load_gguf(device, path.encode(), C.byref(h)))
+        return cls(h.value, device)
+
+    @classmethod
+    def from_tensors(cls, cfg: dict, tensors: Sequence[Tuple[str, int, Sequence[int], np.ndarray]],
+                     device: int = 0) -> "CudaModel":
+        """Upload tensors the host already holds (the .NET LoadedModel path)."""
+        c = LlmdotConfig(**{k: v for k, v in cfg.items() if k in dict(LlmdotConfig._fields_)})
+        keep = []
+        descs = (TensorDesc * len(tensors))()
+        for i, (name, gtype, dims, data) in enumerate(tensors):
+            data = np.ascontiguousarray(data)
+            nb = name.encode()
+            keep += [data, nb]
+            descs[i].name = nb
+            descs[i].type = gtype
+            descs[i].n_dims = len(dims)
+            for j, d in enumerate(dims):
+                descs[i].dims[j] = d
+            descs[i].data = data.ctypes.data
+            descs[i].n_bytes = data.nbytes
+        h = VP()
+        check(lib().llmdot_cuda_model_load(device, C.byref(c), descs, len(tensors), C.byref(h)))
+        return cls(h.value, device)
+
+    def profile_matvec(self, tensor: str, batch: int = 1, iters: int = 20) -> Tuple[float, int]:
+        """(average ms per launch, bytes per launch) of the matvec over one weight tensor."""
+        ms, nb = C.c_float(), C.c_uint64()
+        check(lib().llmdot_cuda_profile_matvec(self._h, tensor.encode(), batch, iters, C.byref(ms), C.byref(nb)))
+        return ms.value, nb.value
+
+    def weight_bytes(self) -> Tuple[int, int]:
+        a, b = C.c_uint64(), C.c_uint64()
+        check(lib().llmdot_cuda_model_weight_bytes(self._h, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
+    def session(self, max_ctx: int = 0, kv: str = "f16") -> "CudaSession":
+        return CudaSession(self, max_ctx, KV_F16 if kv == "f16" else KV_F32)
+
+    def close(self) -> None:
+        if self._h:
+            lib().llmdot_cuda_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CudaSession:
+    def __init__(self, model: CudaModel, max_ctx: int = 0, kv_type: int = KV_F16):
+        self.model = model
+        self._h = VP()
+        check(lib().llmdot_cuda_session_create(model._h, max_ctx, kv_type, C.byref(self._h)))
+
+    @property
+    def position(self) -> int:
+        p = C.c_int()
+        check(lib().llmdot_cuda_session_position(self._h, C.byref(p)))
+        return p.value
+
+    def reset(self) -> None:
+        check(lib().llmdot_cuda_session_reset(self._h))
+
+    def prefill(self, tokens, want_logits: bool = False):
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        V = self.model.config["vocab"]
+        logits = np.empty(V, dtype=np.float32) if want_logits else None
+        nxt = C.c_int32()
+        check(lib().llmdot_cuda_prefill(self._h, toks.ctypes.data_as(I32P), toks.size,
+                                        logits.ctypes.data_as(F32P) if logits is not None else None, C.byref(nxt)))
+        return nxt.value, logits
+
+    def decode(self, token: int, want_logits: bool = False):
+        nxt, lg = decode_batch([self], [token], want_logits)
+        return int(nxt[0]), (lg[0] if lg is not None else None)
+
+    def generate(self, prompt, max_tokens: int) -> np.ndarray:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(max_tokens, 1), dtype=np.int32)
+        n = C.c_int()
+        check(lib().llmdot_cuda_generate(self._h, p.ctypes.data_as(I32P), p.size, max_tokens,
+                                         out.ctypes.data_as(I32P), C.byref(n)))
+        return out[:n.value]
+
+    def close(self) -> None:
+        if self._h:
+            lib().llmdot_cuda_session_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def decode_steps(sessions: List[CudaSession], tokens, n_steps: int):
+    """Device-resident greedy decode of n_steps tokens for sessions in lockstep.
+    Returns (ids [n_steps, batch], device ms, kernel launches per step)."""
+    B = len(sessions)
+    arr = (VP * B)(*[s._h for s in sessions])
+    toks = np.ascontiguousarray(tokens, dtype=np.int32)
+    out = np.zeros((max(n_steps, 1), B), dtype=np.int32)
+    ms = C.c_float()
+    kps = C.c_int()
+    check(lib().llmdot_cuda_decode_steps(arr, B, toks.ctypes.data_as(I32P), n_steps, out.ctypes.data_as(I32P),
+                                         C.byref(ms), C.byref(kps)))
+    return out[:n_steps], ms.value, kps.value
+
+
+def decode_batch(sessions: List[CudaSession], tokens, want_logits: bool = False):
+    """One greedy step for several sessions of one model (batched decode)."""
+    B = len(sessions)
+    arr = (VP * B)(*[s._h for s in sessions])
+    toks = np.ascontiguousarray(tokens, dtype=np.int32)
+    nxt = np.zeros(B, dtype=np.int32)
+    V = sessions[0].model.config["vocab"]
+    logits = np.empty((B, V), dtype=np.float32) if want_logits else None
+    check(lib().llmdot_cuda_decode(arr, B, toks.ctypes.data_as(I32P), nxt.ctypes.data_as(I32P),
+                                   logits.ctypes.data_as(F32P) if logits is not None else None))
+    return nxt, logits

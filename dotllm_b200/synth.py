@@ -1,0 +1,287 @@
+"""Seeded synthetic GGUF models for the benchmark configurations.
+
+No checkpoints or datasets exist on these machines, so every model is random:
+weight matrices N(0, 0.02) quantised to the stated K-quant types with the
+reference-layout encoders in ``quant.py``; norm weights 1 + N(0, 0.01) stored
+as F32; prompts uniform token ids.  The metadata carries exactly the keys
+llmdot's ArchitectureResolver reads (src/Llmdot.Core/Loading/ArchitectureResolver.cs:14-112),
+plus ``tokenizer.ggml.tokens`` of length V (which sets the vocabulary) and an
+EOS id of -1 so the reference's Generate never stops early
+(src/Llmdot.Core/Inference/InferenceEngine.cs:114).
+
+Each tensor is generated from its own seed (config seed, tensor index), so a
+file is identical whatever order or process builds it.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+from dataclasses import dataclass, field, replace
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+
+from . import gguf
+from .gguf import (F32, I32, STR, U32, ARR, GGML_F32, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_Q8_0,
+                   Metadata, TensorInfo, write_gguf)
+from .quant import quantize
+
+GEN_VERSION = 3  # bump when the generator's output changes
+
+
+@dataclass(frozen=True)
+class SynthConfig:
+    name: str
+    arch: str
+    layers: int
+    hidden: int
+    heads: int
+    heads_kv: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    context: int
+    rope_base: float = 10000.0
+    eps: float = 1e-5
+    tied: bool = False
+    default_type: int = GGML_Q4_K
+    # tensor-name role -> ggml type ("token_embd", "output", "attn_q", "attn_k", "attn_v",
+    # "attn_qkv", "attn_output", "ffn_gate", "ffn_up", "ffn_down")
+    overrides: Tuple[Tuple[str, int], ...] = ()
+    qkv_fused: bool = False
+    post_norm: bool = False
+    attn_softcap: Optional[float] = None
+    final_softcap: Optional[float] = None
+    sliding_window: int = 0
+    seed: int = 1
+    # workload
+    prompt_len: int = 64
+    decode_len: int = 128
+    batch: int = 1
+
+    def type_of(self, role: str) -> int:
+        return dict(self.overrides).get(role, self.default_type)
+
+    @property
+    def q_dim(self) -> int:
+        return self.heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.heads_kv * self.head_dim
+
+
+Q6 = GGML_Q6_K
+
+# BASELINE.json configs[0..4]
+CONFIGS: Dict[str, SynthConfig] = {
+    "tiny": SynthConfig(
+        name="tiny", arch="llama", layers=6, hidden=512, heads=8, heads_kv=4, head_dim=64, ffn=1536,
+        vocab=32000, context=2048, rope_base=10000.0, tied=False,
+        overrides=(("token_embd", Q6), ("output", Q6)), seed=1001, prompt_len=64, decode_len=128),
+    "llama1b": SynthConfig(
+        name="llama1b", arch="llama", layers=16, hidden=2048, heads=32, heads_kv=8, head_dim=64, ffn=8192,
+        vocab=128256, context=4096, rope_base=500000.0, tied=True,
+        overrides=(("attn_v", Q6), ("ffn_down", Q6)), seed=2001, prompt_len=512, decode_len=256),
+    "phi3mini": SynthConfig(
+        name="phi3mini", arch="phi3", layers=32, hidden=3072, heads=32, heads_kv=32, head_dim=96, ffn=8192,
+        vocab=32064, context=4096, rope_base=10000.0, tied=False, qkv_fused=True,
+        overrides=(("output", Q6),), seed=3001, prompt_len=1024, decode_len=256, batch=32),
+    "gemma2b": SynthConfig(
+        name="gemma2b", arch="gemma2", layers=26, hidden=2304, heads=8, heads_kv=4, head_dim=256, ffn=9216,
+        vocab=256000, context=8192, rope_base=10000.0, eps=1e-6, tied=True, post_norm=True,
+        attn_softcap=50.0, final_softcap=30.0, sliding_window=4096,
+        overrides=(("token_embd", Q6), ("attn_v", Q6), ("ffn_down", Q6)), seed=4001,
+        prompt_len=6144, decode_len=256, batch=4),
+    "llama8b": SynthConfig(
+        name="llama8b", arch="llama", layers=32, hidden=4096, heads=32, heads_kv=8, head_dim=128, ffn=14336,
+        vocab=128256, context=8192, rope_base=500000.0, tied=False,
+        overrides=(("attn_v", Q6), ("ffn_down", Q6), ("output", Q6)), seed=5001,
+        prompt_len=2048, decode_len=256, batch=1),
+}
+
+# Small shapes for fast tests; they exercise the same features as the big configs.
+TEST_CONFIGS: Dict[str, SynthConfig] = {
+    "micro": SynthConfig(
+        name="micro", arch="llama", layers=2, hidden=256, heads=4, heads_kv=2, head_dim=64, ffn=512,
+        vocab=1000, context=256, tied=True, overrides=(("attn_v", Q6), ("ffn_down", Q6)), seed=11,
+        prompt_len=8, decode_len=16),
+    "micro-gemma": SynthConfig(
+        name="micro-gemma", arch="gemma2", layers=2, hidden=256, heads=4, heads_kv=2, head_dim=128, ffn=768,
+        vocab=1000, context=256, eps=1e-6, tied=True, post_norm=True, attn_softcap=50.0, final_softcap=30.0,
+        sliding_window=24, overrides=(("token_embd", Q6), ("attn_v", Q6), ("ffn_down", Q6)), seed=12,
+        prompt_len=20, decode_len=16),
+    "micro-phi3": SynthConfig(
+        name="micro-phi3", arch="phi3", layers=2, hidden=512, heads=8, heads_kv=8, head_dim=96, ffn=512,
+        vocab=1000, context=256, qkv_fused=True, overrides=(("output", Q6),), seed=13,
+        prompt_len=8, decode_len=16),
+    "micro-q5q8": SynthConfig(
+        name="micro-q5q8", arch="qwen2", layers=2, hidden=256, heads=4, heads_kv=1, head_dim=64, ffn=512,
+        vocab=1000, context=256, default_type=GGML_Q5_K,
+        overrides=(("attn_v", GGML_Q8_0), ("ffn_down", GGML_Q8_0), ("output", Q6)), seed=14,
+        prompt_len=8, decode_len=16),
+}
+
+ALL_CONFIGS = {**CONFIGS, **TEST_CONFIGS}
+
+
+def tensor_plan(cfg: SynthConfig) -> List[Tuple[TensorInfo, str]]:
+    """(TensorInfo, role) for every tensor, in file order.  Role "norm" = F32 norm vector."""
+    d, q, kv, f, V = cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.ffn, cfg.vocab
+    out: List[Tuple[TensorInfo, str]] = []
+
+    def add(name: str, dims: List[int], role: str):
+        t = GGML_F32 if role == "norm" else cfg.type_of(role)
+        out.append((TensorInfo(name, dims, t), role))
+
+    add("token_embd.weight", [d, V], "token_embd")
+    for l in range(cfg.layers):
+        p = f"blk.{l}."
+        add(p + "attn_norm.weight", [d], "norm")
+        if cfg.qkv_fused:
+            add(p + "attn_qkv.weight", [d, q + 2 * kv], "attn_qkv")
+        else:
+            add(p + "attn_q.weight", [d, q], "attn_q")
+            add(p + "attn_k.weight", [d, kv], "attn_k")
+            add(p + "attn_v.weight", [d, kv], "attn_v")
+        add(p + "attn_output.weight", [q, d], "attn_output")
+        if cfg.post_norm:
+            add(p + "post_attention_norm.weight", [d], "norm")
+        add(p + "ffn_norm.weight", [d], "norm")
+        add(p + "ffn_gate.weight", [d, f], "ffn_gate")
+        add(p + "ffn_up.weight", [d, f], "ffn_up")
+        add(p + "ffn_down.weight", [f, d], "ffn_down")
+        if cfg.post_norm:
+            add(p + "post_ffw_norm.weight", [d], "norm")
+    add("output_norm.weight", [d], "norm")
+    if not cfg.tied:
+        add("output.weight", [d, V], "output")
+    return out
+
+
+def metadata_for(cfg: SynthConfig) -> Metadata:
+    a = cfg.arch
+    md = Metadata()
+    md.add("general.architecture", STR, a)
+    md.add("general.name", STR, f"synthetic-{cfg.name}")
+    md.add(f"{a}.embedding_length", U32, cfg.hidden)
+    md.add(f"{a}.block_count", U32, cfg.layers)
+    md.add(f"{a}.context_length", U32, cfg.context)
+    md.add(f"{a}.feed_forward_length", U32, cfg.ffn)
+    md.add(f"{a}.attention.head_count", U32, cfg.heads)
+    md.add(f"{a}.attention.head_count_kv", U32, cfg.heads_kv)
+    md.add(f"{a}.attention.key_length", U32, cfg.head_dim)
+    md.add(f"{a}.attention.value_length", U32, cfg.head_dim)
+    md.add(f"{a}.attention.layer_norm_rms_epsilon", F32, cfg.eps)
+    md.add(f"{a}.rope.freq_base", F32, cfg.rope_base)
+    md.add(f"{a}.rope.dimension_count", U32, cfg.head_dim)
+    if cfg.sliding_window:
+        md.add(f"{a}.attention.sliding_window", U32, cfg.sliding_window)
+    if cfg.attn_softcap is not None:
+        md.add(f"{a}.attn_logit_softcapping", F32, cfg.attn_softcap)
+    if cfg.final_softcap is not None:
+        md.add(f"{a}.final_logit_softcapping", F32, cfg.final_softcap)
+    md.add("tokenizer.ggml.model", STR, "synthetic")
+    md.add("tokenizer.ggml.tokens", ARR, [f"<t{i}>" for i in range(cfg.vocab)], STR)
+    md.add("tokenizer.ggml.bos_token_id", U32, 1)
+    md.add("tokenizer.ggml.eos_token_id", I32, -1)
+    return md
+
+
+def _tensor_seed(cfg: SynthConfig, idx: int) -> int:
+    return (cfg.seed * 1_000_003 + idx * 7919) & 0x7FFFFFFF
+
+
+def tensor_bytes(cfg: SynthConfig, info: TensorInfo, role: str, idx: int) -> bytes:
+    rng = np.random.default_rng(_tensor_seed(cfg, idx))
+    if role == "norm":
+        w = 1.0 + 0.01 * rng.standard_normal(info.dims[0], dtype=np.float32)
+        return w.astype("<f4").tobytes()
+    cols, rows = info.dims[0], info.dims[1]
+    chunk = max(1, (1 << 24) // cols)
+    parts = []
+    for r0 in range(0, rows, chunk):
+        n = min(chunk, rows - r0)
+        x = rng.standard_normal((n, cols), dtype=np.float32) * np.float32(0.02)
+        parts.append(quantize(x, info.ggml_type).tobytes())
+    return b"".join(parts)
+
+
+def cache_dir() -> str:
+    d = os.environ.get("LLMDOT_SYNTH_DIR") or os.path.join(os.path.expanduser("~"), ".cache", "llmdot_synth")
+    os.makedirs(d, exist_ok=True)
+    return d
+
+
+def model_path(cfg: SynthConfig) -> str:
+    key = hashlib.sha1(repr((cfg, GEN_VERSION)).encode()).hexdigest()[:12]
+    return os.path.join(cache_dir(), f"{cfg.name}-{key}.gguf")
+
+
+def _tensor_job(args):
+    cfg, info, role, idx = args
+    return tensor_bytes(cfg, info, role, idx)
+
+
+def build_model(cfg: SynthConfig, path: Optional[str] = None, workers: Optional[int] = None) -> str:
+    """Write (or reuse) the synthetic GGUF for ``cfg`` and return its path.
+
+    Large models are generated by a pool of *spawned* worker processes (safe to
+    use in a process that already initialised CUDA); the file is identical to a
+    single-process build because every tensor has its own seed."""
+    path = path or model_path(cfg)
+    if os.path.exists(path):
+        return path
+    plan = tensor_plan(cfg)
+    infos = [t for t, _ in plan]
+    roles = {t.name: (r, i) for i, (t, r) in enumerate(plan)}
+    tmp = path + f".tmp{os.getpid()}"
+    total = sum(t.n_bytes for t in infos)
+    if workers is None:
+        workers = min(os.cpu_count() or 1, 24) if total > (64 << 20) else 1
+    if workers <= 1:
+        def produce(info: TensorInfo) -> bytes:
+            role, idx = roles[info.name]
+            return tensor_bytes(cfg, info, role, idx)
+
+        write_gguf(tmp, metadata_for(cfg), infos, produce)
+    else:
+        import multiprocessing as mp
+        ctx = mp.get_context("spawn")
+        jobs = [(cfg, t, r, i) for i, (t, r) in enumerate(plan)]
+        with ctx.Pool(workers) as pool:
+            it = pool.imap(_tensor_job, jobs, chunksize=1)
+            write_gguf(tmp, metadata_for(cfg), infos, lambda info: next(it))
+    os.replace(tmp, path)
+    return path
+
+
+def prompt_tokens(cfg: SynthConfig, n: Optional[int] = None, session: int = 0) -> np.ndarray:
+    """Uniform token ids in [0, V) seeded by (config seed, session)."""
+    n = cfg.prompt_len if n is None else n
+    rng = np.random.default_rng(cfg.seed * 1000 + 1 + session)
+    return rng.integers(0, cfg.vocab, size=n, dtype=np.int64).astype(np.int32)
+
+
+def weight_bytes(cfg: SynthConfig) -> Dict[str, int]:
+    """Quantised bytes read per decode step (embedding excluded: one row per session)."""
+    layer = 0
+    head = 0
+    for info, role in tensor_plan(cfg):
+        if role == "token_embd":
+            if cfg.tied:
+                head += info.n_bytes
+            continue
+        if role == "output":
+            head += info.n_bytes
+            continue
+        layer += info.n_bytes
+    return {"layers": layer, "logits": head}
+
+
+def get(name: str) -> SynthConfig:
+    return ALL_CONFIGS[name]
+
+
+def with_overrides(cfg: SynthConfig, **kw) -> SynthConfig:
+    return replace(cfg, **kw)

@@ -1,0 +1,48 @@
+"""The C-ABI library loads and exports every symbol include/llmdot_cuda.h
+declares; on a machine without a GPU its entry points fail with a status, never
+crash and never compute on the CPU."""
+import ctypes as C
+import subprocess
+
+import numpy as np
+import pytest
+
+from dotllm_b200 import native
+
+
+def test_library_exists_and_loads():
+    L = native.lib()
+    assert L.llmdot_cuda_version().decode().startswith("llmdot-cuda")
+
+
+def test_exports_every_header_function():
+    declared = native.header_functions()
+    assert len(declared) >= 35
+    out = subprocess.run(["nm", "-D", "--defined-only", native.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = [f for f in declared if f not in exported]
+    assert not missing, f"not exported: {missing}"
+    # nothing else leaks: internal symbols are hidden
+    extra = [s for s in exported if s.startswith("llmdot") and s not in declared]
+    assert not extra, f"undeclared exports: {extra}"
+
+
+def test_bindings_cover_header():
+    assert set(native.header_functions()) <= set(native._SIGS)
+
+
+def test_device_count_without_gpu_is_zero_or_more():
+    n = native.device_count()
+    assert n >= 0
+
+
+def test_no_cpu_fallback_without_device():
+    if native.device_count() > 0:
+        pytest.skip("a GPU is present; this checks the device-less error path")
+    h = C.c_void_p()
+    rc = native.lib().llmdot_cuda_create(0, C.byref(h))
+    assert rc == -3 and not h.value
+    assert "no CUDA device" in native.lib().llmdot_cuda_last_error().decode()
+    with pytest.raises(native.CudaBackendError):
+        from dotllm_b200.backend import CudaBackend
+        CudaBackend(0)
