@@ -249,21 +249,23 @@ extern "C" int llmdot_cuda_layernorm(llmdot_backend *h, const float *input, cons
 static int rope_common(llmdot_backend *h, float *query, int qLen, float *key, int kLen, int headDim, const float *cs,
                        const float *sn, int half)
 {
-    if (!query || !key || headDim <= 0 || half <= 0 || 2 * half > headDim)
+    if (!query || !key || half <= 0 || 2 * half > qLen || (key != query && 2 * half > kLen))
         return fail(LLMDOT_E_INVALID, "rope: bad arguments");
-    // The reference rotates the spans it is given (one head per call in InferenceEngine);
-    // spans longer than headDim are treated as consecutive heads.
+    (void)headDim;
+    // TensorOps.ApplyRoPECore (TensorOps.cs:699-743) rotates the pairs (i, i+half) of the
+    // first 2*half elements of each span and leaves the rest untouched, whatever the span
+    // length (InferenceEngine calls it once per head).
     void *tab;
     LLMDOT_TRY(scratch(h, 2, sizeof(float) * 2 * half, &tab));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(tab, cs, sizeof(float) * half, cudaMemcpyHostToDevice, h->st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync((float *)tab + half, sn, sizeof(float) * half, cudaMemcpyHostToDevice, h->st));
     void *q;
     LLMDOT_TRY(up(h, 0, query, sizeof(float) * qLen, &q));
-    LLMDOT_TRY(launch_rope((float *)q, qLen / headDim, headDim, (float *)tab, (float *)tab + half, half, h->st));
+    LLMDOT_TRY(launch_rope((float *)q, 1, 2 * half, (float *)tab, (float *)tab + half, half, h->st));
     if (key != query) {
         void *k;
         LLMDOT_TRY(up(h, 1, key, sizeof(float) * kLen, &k));
-        LLMDOT_TRY(launch_rope((float *)k, kLen / headDim, headDim, (float *)tab, (float *)tab + half, half, h->st));
+        LLMDOT_TRY(launch_rope((float *)k, 1, 2 * half, (float *)tab, (float *)tab + half, half, h->st));
         LLMDOT_CUDA_TRY(cudaMemcpyAsync(key, k, sizeof(float) * kLen, cudaMemcpyDeviceToHost, h->st));
     }
     return down(h, query, q, sizeof(float) * qLen);
