@@ -251,6 +251,24 @@ LLMDOT_API int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
 LLMDOT_API int llmdot_cuda_profile_matvec(llmdot_model *m, const char *tensor, int batch, int iters,
                                           float *avg_ms, uint64_t *bytes);
 
+/* Greedy argmax over logits that are already in device memory, without allocating any device
+ * memory.  No counterpart in the reference: it exists for hosts that own all device memory
+ * themselves (e.g. pools reserved at start-up for weights, KV pages and logits) and cannot let
+ * a library call cudaMalloc during the token loop, where it could fail or stall the device.
+ *   d_logits  device pointer, `rows` vectors of `n` floats, row r starting at d_logits + r*ld
+ *   d_index   device pointer, receives `rows` int32 results: first index of each row's maximum
+ *   stream    a cudaStream_t passed as a plain pointer (NULL = the legacy default stream)
+ * The only scratch is one fixed array inside the library: LLMDOT_ARGMAX_NOALLOC_MAX_ROWS 64-bit
+ * keys (32 KiB), which every GPU that loads the library holds until the process exits; more rows
+ * are rejected with LLMDOT_E_INVALID.  The call is asynchronous on `stream`.  All calls on a
+ * device share that array and it keeps the last call's contents (each call clears the rows it
+ * uses): calls that overlap on the GPU race and return wrong indices.  The first call on each
+ * device looks the array's address up (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture. */
+#define LLMDOT_ARGMAX_NOALLOC_MAX_ROWS 4096
+LLMDOT_API int llmdot_cuda_argmax_noalloc(const float *d_logits, int n, int rows, int ld, int32_t *d_index,
+                                          void *stream);
+
 #ifdef __cplusplus
 }
 #endif
