@@ -242,7 +242,7 @@ def main():
     per_layer += ["attn_output", "ffn_gate", "ffn_up", "ffn_down"]
     tot_ms, tot_bytes, launches = 0.0, 0, 0
     for name in per_layer:
-        ms, nb = m.profile_matvec(f"blk.0.{name}.weight", B, 20)
+        ms, nb = m.profile_matvec(f"blk.*.{name}.weight", B, 5)
         tot_ms += ms * c["layers"]
         tot_bytes += nb * c["layers"]
         launches += c["layers"]

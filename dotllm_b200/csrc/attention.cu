@@ -1,26 +1,32 @@
-// attention.cu -- RoPE + KV append and GQA decode attention over the paged cache.
+// attention.cu -- GQA decode attention over the paged KV cache, with RoPE and the KV append.
 //
 // Reference: InferenceEngine.AttentionForward (src/Llmdot.Core/Inference/InferenceEngine.cs:304-450)
 // with VectorMath.Softmax (src/Llmdot.Core/Tensors/Numeric/VectorMath.cs:215-258).
 // The reference's softmax evaluates ExpApprox(s - max) against the GLOBAL max of the
 // window (an approximation whose error is up to ~18 % for some arguments, so an
-// online/rescaled softmax would not reproduce it).  The device therefore works in
-// three passes over pages of KV_PAGE positions:
-//   1. scores: s = (q . k) * 1/sqrt(hd), softcap, per-page max;
-//   2. p = exp(s - M) with M the window max, per-page sum and sum p*V;
-//   3. combine the pages and scale by 1/sum.
+// online/rescaled softmax would not reproduce it).  The device therefore runs two kernels
+// over pages of KV_PAGE positions, one CTA per (page, kv head, session):
+//   1. scores: RoPE of q (and of the new k, which the CTA owning the current position appends
+//      to the cache together with v), s = (q . k) * 1/sqrt(hd), softcap, per-page max;
+//   2. p = exp(s - M) with M the window max, per-page sum and sum p*V; the last CTA of each
+//      (session, kv head) to finish combines the pages and scales by 1/sum.
 // "Vector lane" vs "tail" (ExpApprox/TanhApprox vs MathF.Exp/Tanh) is decided by the
 // position's index inside the window, exactly as the reference's 8-wide loops do.
+// Both kernels stage their KV page in shared memory before waiting on the previous kernel
+// (programmatic dependent launch): pages of earlier positions are constant during a step.
 #include "attention.cuh"
 
 namespace llmdot {
 
-template <typename T> __device__ __forceinline__ float ldf(const T *p);
-template <> __device__ __forceinline__ float ldf<float>(const float *p) { return *p; }
-template <> __device__ __forceinline__ float ldf<__half>(const __half *p) { return __half2float(*p); }
-template <typename T> __device__ __forceinline__ T stf(float v);
-template <> __device__ __forceinline__ float stf<float>(float v) { return v; }
-template <> __device__ __forceinline__ __half stf<__half>(float v) { return __float2half_rn(v); }
+template <typename T> struct KvT;
+template <> struct KvT<float> {
+    static __device__ __forceinline__ float ld(const float *p) { return *p; }
+    static __device__ __forceinline__ float st(float v) { return v; }
+};
+template <> struct KvT<__half> {
+    static __device__ __forceinline__ float ld(const __half *p) { return __half2float(*p); }
+    static __device__ __forceinline__ __half st(float v) { return __float2half_rn(v); }
+};
 
 __device__ __forceinline__ void window(int p, int sw, int &start, int &seq_len)
 {
@@ -28,198 +34,235 @@ __device__ __forceinline__ void window(int p, int sw, int &start, int &seq_len)
     start = sw > 0 ? max(0, seq_len - sw) : 0;
 }
 
-// ---------------------------------------------------------------- RoPE + append
+// Copy positions [j0, j1) of one page (KV_PAGE x hd elements, contiguous) into shared memory
+// rows of `stride` elements, 16 bytes at a time.
 template <typename T>
-__global__ void rope_append_kernel(float *__restrict__ q, int ldq, const float *__restrict__ k,
-                                   const float *__restrict__ v, int ldkv, const int32_t *__restrict__ pos,
-                                   const float *__restrict__ cos_t, const float *__restrict__ sin_t,
-                                   const KvView *__restrict__ views, int layer, AttnShape sh)
+__device__ __forceinline__ void stage_page(T *dst, const T *src, int hd, int stride, int j0, int j1)
 {
-    const int b = blockIdx.y, h = blockIdx.x, hd = sh.head_dim, half = sh.rope_half;
-    const int p = pos[b];
-    const float *cs = cos_t + (uint64_t)p * half, *sn = sin_t + (uint64_t)p * half;
-    if (h < sh.heads) {
-        float *x = q + (uint64_t)b * ldq + (uint64_t)h * hd;
-        for (int i = threadIdx.x; i < half; i += blockDim.x) {
-            float c = cs[i], s = sn[i], x0 = x[i], x1 = x[i + half];
-            x[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-            x[i + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-        }
-        return;
-    }
-    const int kh = h - sh.heads;
-    const KvView vw = views[b];
-    const int page = vw.pages[p / KV_PAGE], slot = p % KV_PAGE;
-    const uint64_t off = (uint64_t)layer * vw.layer_stride +
-                         (((uint64_t)page * sh.heads_kv + kh) * KV_PAGE + slot) * hd;
-    T *kd = (T *)vw.k + off;
-    T *vd = (T *)vw.v + off;
-    const float *ks = k + (uint64_t)b * ldkv + (uint64_t)kh * hd;
-    const float *vs = v + (uint64_t)b * ldkv + (uint64_t)kh * hd;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-        float r;
-        if (i < half) r = __fsub_rn(__fmul_rn(ks[i], cs[i]), __fmul_rn(ks[i + half], sn[i]));
-        else if (i < 2 * half) r = __fadd_rn(__fmul_rn(ks[i - half], sn[i - half]), __fmul_rn(ks[i], cs[i - half]));
-        else r = ks[i];
-        kd[i] = stf<T>(r);
-        vd[i] = stf<T>(vs[i]);
+    constexpr int E = 16 / sizeof(T);  // elements per 16 bytes
+    const int per_row = hd / E;
+    for (int i = threadIdx.x; i < (j1 - j0) * per_row; i += blockDim.x) {
+        const int j = j0 + i / per_row, c = (i % per_row) * E;
+        const uint4 v = *(const uint4 *)(src + (size_t)j * hd + c);
+        const T *pv = (const T *)&v;
+#pragma unroll
+        for (int e = 0; e < E; e++) dst[j * stride + c + e] = pv[e];
     }
 }
 
-int launch_rope_append(float *q, int ldq, const float *k, const float *v, int ldkv, const int32_t *pos,
-                       const float *cos_t, const float *sin_t, const KvView *views, int layer, int kv_type,
-                       const AttnShape &sh, int batch, cudaStream_t st)
-{
-    dim3 grid(sh.heads + sh.heads_kv, batch);
-    if (kv_type == LLMDOT_KV_F16)
-        rope_append_kernel<__half><<<grid, 128, 0, st>>>(q, ldq, k, v, ldkv, pos, cos_t, sin_t, views, layer, sh);
-    else
-        rope_append_kernel<float><<<grid, 128, 0, st>>>(q, ldq, k, v, ldkv, pos, cos_t, sin_t, views, layer, sh);
-    LLMDOT_CUDA_TRY(cudaGetLastError());
-    return LLMDOT_OK;
-}
-
-// ---------------------------------------------------------------- pass 1: scores
+// ---------------------------------------------------------------- kernel 1: RoPE, append, scores
 template <typename T>
-__global__ void __launch_bounds__(256) attn_scores_kernel(const float *__restrict__ q, int ldq,
+__global__ void __launch_bounds__(256) attn_scores_kernel(const float *__restrict__ q, int ldq, const float *__restrict__ k,
+                                                          const float *__restrict__ v, int ldkv,
                                                           const int32_t *__restrict__ pos,
+                                                          const float *__restrict__ cos_t, const float *__restrict__ sin_t,
                                                           const KvView *__restrict__ views, int layer, AttnShape sh,
                                                           float *__restrict__ scores, float *__restrict__ part_m)
 {
-    extern __shared__ float smem[];
+    extern __shared__ __align__(16) uint8_t smem_raw[];
     const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-    const int hd = sh.head_dim, G = sh.heads / sh.heads_kv, nchunk = sh.max_ctx / KV_PAGE;
+    const int hd = sh.head_dim, half = sh.rope_half, G = sh.heads / sh.heads_kv, nchunk = sh.max_ctx / KV_PAGE;
+    const int p = pos[b];  // positions change only between steps
     int start, seq_len;
-    window(pos[b], sh.sliding_window, start, seq_len);
+    window(p, sh.sliding_window, start, seq_len);
     const int s0 = chunk * KV_PAGE;
-    if (s0 >= seq_len || s0 + KV_PAGE <= start) return;
-    const int len = seq_len - start, nvec = len - len % 8;
-    float *qs = smem;                                // [G][hd]
-    uint32_t *mk = (uint32_t *)(smem + G * hd);      // [G]
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
-        qs[i] = q[(uint64_t)b * ldq + (uint64_t)(kvh * G) * hd + i];
-    for (int i = threadIdx.x; i < G; i += blockDim.x) mk[i] = 0u;
-    __syncthreads();
+    if (s0 >= seq_len || s0 + KV_PAGE <= start) {
+        pdl_launch();
+        return;
+    }
+    const int stride = hd + (sizeof(T) == 2 ? 2 : 1);  // odd word stride: no bank conflicts across positions
+    T *ks = (T *)smem_raw;                                            // [KV_PAGE][stride]
+    float *qs = (float *)(smem_raw + (size_t)KV_PAGE * stride * sizeof(T));  // [G][hd]
+    uint32_t *mk = (uint32_t *)(qs + G * hd);                         // [G]
     const KvView vw = views[b];
     const int page = vw.pages[chunk];
-    const T *kb = (const T *)vw.k + (uint64_t)layer * vw.layer_stride +
-                  ((uint64_t)page * sh.heads_kv + kvh) * KV_PAGE * hd;
+    const size_t head_off = ((size_t)page * sh.heads_kv + kvh) * KV_PAGE * hd;
+    T *kg = (T *)vw.k + (size_t)layer * vw.layer_stride + head_off;
+    T *vg = (T *)vw.v + (size_t)layer * vw.layer_stride + head_off;
+    const int jlo = max(start - s0, 0), jhi = min(seq_len - s0, KV_PAGE);
+    const bool has_new = p >= s0 && p < s0 + KV_PAGE;
+    // earlier positions of the page are constant: stage them before the dependency wait
+    stage_page<T>(ks, kg, hd, stride, jlo, has_new ? p - s0 : jhi);
+    pdl_launch();
+    pdl_wait();
+    const float *cs = cos_t + (size_t)p * half, *sn = sin_t + (size_t)p * half;
+    // RoPE of the G query heads (TensorOps.ApplyRoPE, half-split pairs)
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+        const int hg = i / hd, d = i % hd;
+        const float *x = q + (size_t)b * ldq + (size_t)(kvh * G + hg) * hd;
+        float r;
+        if (d < half) r = __fsub_rn(__fmul_rn(x[d], cs[d]), __fmul_rn(x[d + half], sn[d]));
+        else if (d < 2 * half) r = __fadd_rn(__fmul_rn(x[d - half], sn[d - half]), __fmul_rn(x[d], cs[d - half]));
+        else r = x[d];
+        qs[i] = r;
+    }
+    for (int i = threadIdx.x; i < G; i += blockDim.x) mk[i] = 0u;
+    if (has_new) {
+        // RoPE of the new key, then K/V cache append (InferenceEngine.cs:375-382)
+        const float *kx = k + (size_t)b * ldkv + (size_t)kvh * hd;
+        const float *vx = v + (size_t)b * ldkv + (size_t)kvh * hd;
+        const int slot = p - s0;
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+            float r;
+            if (d < half) r = __fsub_rn(__fmul_rn(kx[d], cs[d]), __fmul_rn(kx[d + half], sn[d]));
+            else if (d < 2 * half) r = __fadd_rn(__fmul_rn(kx[d - half], sn[d - half]), __fmul_rn(kx[d], cs[d - half]));
+            else r = kx[d];
+            const T kt = KvT<T>::st(r);
+            kg[(size_t)slot * hd + d] = kt;
+            ks[slot * stride + d] = kt;
+            vg[(size_t)slot * hd + d] = KvT<T>::st(vx[d]);
+        }
+    }
+    __syncthreads();
+    const int len = seq_len - start, nvec = len - len % 8;
     const float inv_cap = sh.has_cap ? __fdiv_rn(1.0f, sh.cap) : 0.0f;
     for (int idx = threadIdx.x; idx < G * KV_PAGE; idx += blockDim.x) {
         const int hg = idx / KV_PAGE, j = idx % KV_PAGE, s = s0 + j;
-        if (s < start || s >= seq_len) continue;
-        const T *kr = kb + (uint64_t)j * hd;
+        if (j < jlo || j >= jhi) continue;
+        const T *kr = ks + j * stride;
         const float *qh = qs + hg * hd;
         float dot = 0.0f;
-        for (int d = 0; d < hd; d++) dot = fmaf(qh[d], ldf<T>(kr + d), dot);
+        for (int d = 0; d < hd; d++) dot = fmaf(qh[d], KvT<T>::ld(kr + d), dot);
         float sc = __fmul_rn(dot, sh.inv_sqrt_hd);
         if (sh.has_cap) sc = softcap_ref(sc, sh.cap, inv_cap, (s - start) < nvec);
-        const int h = kvh * G + hg;
-        scores[((uint64_t)b * sh.heads + h) * sh.max_ctx + s] = sc;
+        scores[((size_t)b * sh.heads + kvh * G + hg) * sh.max_ctx + s] = sc;
         atomicMax(mk + hg, float_key(sc));
     }
     __syncthreads();
     for (int hg = threadIdx.x; hg < G; hg += blockDim.x)
-        part_m[((uint64_t)b * sh.heads + kvh * G + hg) * nchunk + chunk] = key_float(mk[hg]);
+        part_m[((size_t)b * sh.heads + kvh * G + hg) * nchunk + chunk] = key_float(mk[hg]);
 }
 
-// ---------------------------------------------------------------- pass 2: exp + PV
+// ---------------------------------------------------------------- kernel 2: exp, PV, combine
 template <typename T>
 __global__ void __launch_bounds__(256) attn_pv_kernel(const int32_t *__restrict__ pos, const KvView *__restrict__ views,
                                                       int layer, AttnShape sh, const float *__restrict__ scores,
                                                       const float *__restrict__ part_m, float *__restrict__ part_s,
-                                                      float *__restrict__ part_o)
+                                                      float *__restrict__ part_o, int *__restrict__ counters,
+                                                      float *__restrict__ out, int ldo)
 {
-    extern __shared__ float smem[];
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    __shared__ int last;
     const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int hd = sh.head_dim, G = sh.heads / sh.heads_kv, nchunk = sh.max_ctx / KV_PAGE;
+    const int p = pos[b];
     int start, seq_len;
-    window(pos[b], sh.sliding_window, start, seq_len);
+    window(p, sh.sliding_window, start, seq_len);
     const int s0 = chunk * KV_PAGE;
-    if (s0 >= seq_len || s0 + KV_PAGE <= start) return;
+    if (s0 >= seq_len || s0 + KV_PAGE <= start) {
+        pdl_launch();
+        return;
+    }
+    T *vs = (T *)smem_raw;                                                  // [KV_PAGE][hd]
+    float *ps = (float *)(smem_raw + (size_t)KV_PAGE * hd * sizeof(T));     // [G][KV_PAGE]
+    float *mx = ps + G * KV_PAGE;                                           // [G]
+    const KvView vw = views[b];
+    const int page = vw.pages[chunk];
+    const T *vg = (const T *)vw.v + (size_t)layer * vw.layer_stride + ((size_t)page * sh.heads_kv + kvh) * KV_PAGE * hd;
+    const int jlo = max(start - s0, 0), jhi = min(seq_len - s0, KV_PAGE);
+    const bool has_new = p >= s0 && p < s0 + KV_PAGE;
+    stage_page<T>(vs, vg, hd, hd, jlo, has_new ? p - s0 : jhi);
+    pdl_launch();
+    pdl_wait();
+    if (has_new) stage_page<T>(vs, vg, hd, hd, p - s0, p - s0 + 1);  // appended by kernel 1
     const int len = seq_len - start, nvec = len - len % 8;
     const int c0 = start / KV_PAGE, c1 = (seq_len - 1) / KV_PAGE;
-    float *ps = smem;                  // [G][KV_PAGE]
-    float *mx = smem + G * KV_PAGE;    // [G]
-    float *sm = mx + G;                // [G]
     for (int hg = threadIdx.x; hg < G; hg += blockDim.x) {
-        const float *pm = part_m + ((uint64_t)b * sh.heads + kvh * G + hg) * nchunk;
+        const float *pm = part_m + ((size_t)b * sh.heads + kvh * G + hg) * nchunk;
         float m = -INFINITY;
         for (int c = c0; c <= c1; c++) m = fmaxf(m, pm[c]);
         mx[hg] = m;
-        sm[hg] = 0.0f;
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < G * KV_PAGE; idx += blockDim.x) {
         const int hg = idx / KV_PAGE, j = idx % KV_PAGE, s = s0 + j;
-        float p = 0.0f;
-        if (s >= start && s < seq_len) {
-            const int h = kvh * G + hg;
-            float d = __fsub_rn(scores[((uint64_t)b * sh.heads + h) * sh.max_ctx + s], mx[hg]);
-            p = (s - start) < nvec ? exp_approx(d) : expf(d);
+        float pr = 0.0f;
+        if (j >= jlo && j < jhi) {
+            const float d = __fsub_rn(scores[((size_t)b * sh.heads + kvh * G + hg) * sh.max_ctx + s], mx[hg]);
+            pr = (s - start) < nvec ? exp_approx(d) : expf(d);
         }
-        ps[idx] = p;
+        ps[idx] = pr;
     }
     __syncthreads();
+    const size_t hbase = ((size_t)b * sh.heads + kvh * G) * nchunk;
     for (int hg = threadIdx.x >> 5; hg < G; hg += blockDim.x >> 5) {
         float t = 0.0f;
         for (int j = threadIdx.x & 31; j < KV_PAGE; j += 32) t += ps[hg * KV_PAGE + j];
         t = warp_sum(t);
-        if ((threadIdx.x & 31) == 0) part_s[((uint64_t)b * sh.heads + kvh * G + hg) * nchunk + chunk] = t;
+        if ((threadIdx.x & 31) == 0) part_s[hbase + (size_t)hg * nchunk + chunk] = t;
     }
-    const KvView vw = views[b];
-    const int page = vw.pages[chunk];
-    const T *vb = (const T *)vw.v + (uint64_t)layer * vw.layer_stride +
-                  ((uint64_t)page * sh.heads_kv + kvh) * KV_PAGE * hd;
-    const int jlo = max(start - s0, 0), jhi = min(seq_len - s0, KV_PAGE);
     for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
         const int hg = idx / hd, d = idx % hd;
-        const float *p = ps + hg * KV_PAGE;
+        const float *pp = ps + hg * KV_PAGE;
         float acc = 0.0f;
-        for (int j = jlo; j < jhi; j++) acc = fmaf(p[j], ldf<T>(vb + (uint64_t)j * hd + d), acc);
-        part_o[(((uint64_t)b * sh.heads + kvh * G + hg) * nchunk + chunk) * hd + d] = acc;
+        for (int j = jlo; j < jhi; j++) acc = fmaf(pp[j], KvT<T>::ld(vs + j * hd + d), acc);
+        part_o[((hbase + (size_t)hg * nchunk) + chunk) * hd + d] = acc;
     }
+    // the last page of this (session, kv head) to finish combines all pages
+    __threadfence();
+    __syncthreads();
+    int *cnt = counters + (size_t)b * sh.heads_kv + kvh;
+    if (threadIdx.x == 0) last = atomicAdd(cnt, 1) == (c1 - c0);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
+        const int hg = idx / hd, d = idx % hd;
+        const size_t hb = hbase + (size_t)hg * nchunk;
+        float sum = 0.0f, o = 0.0f;
+        for (int c = c0; c <= c1; c++) {
+            sum += __ldcg(part_s + hb + c);
+            o += __ldcg(part_o + (hb + c) * hd + d);
+        }
+        out[(size_t)b * ldo + (size_t)(kvh * G + hg) * hd + d] = __fmul_rn(o, __fdiv_rn(1.0f, sum));
+    }
+    if (threadIdx.x == 0) *cnt = 0;  // ready for the next layer / step
 }
 
-// ---------------------------------------------------------------- pass 3: combine
-__global__ void attn_combine_kernel(const int32_t *__restrict__ pos, AttnShape sh, const float *__restrict__ part_s,
-                                    const float *__restrict__ part_o, float *__restrict__ out, int ldo)
+static size_t scores_smem(const AttnShape &sh, size_t esz)
 {
-    const int h = blockIdx.x, b = blockIdx.y, hd = sh.head_dim, nchunk = sh.max_ctx / KV_PAGE;
-    int start, seq_len;
-    window(pos[b], sh.sliding_window, start, seq_len);
-    const int c0 = start / KV_PAGE, c1 = (seq_len - 1) / KV_PAGE;
-    const uint64_t base = ((uint64_t)b * sh.heads + h) * nchunk;
-    float sum = 0.0f;
-    for (int c = c0; c <= c1; c++) sum += part_s[base + c];
-    const float inv = __fdiv_rn(1.0f, sum);
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float o = 0.0f;
-        for (int c = c0; c <= c1; c++) o += part_o[(base + c) * hd + d];
-        out[(uint64_t)b * ldo + (uint64_t)h * hd + d] = __fmul_rn(o, inv);
-    }
+    const int G = sh.heads / sh.heads_kv;
+    return (size_t)KV_PAGE * (sh.head_dim + (esz == 2 ? 2 : 1)) * esz + 16 + sizeof(float) * (G * sh.head_dim + G) + 16;
+}
+static size_t pv_smem(const AttnShape &sh, size_t esz)
+{
+    const int G = sh.heads / sh.heads_kv;
+    return (size_t)KV_PAGE * sh.head_dim * esz + sizeof(float) * (G * KV_PAGE + G) + 16;
 }
 
-int launch_attention_decode(const float *q, int ldq, const int32_t *pos, const KvView *views, int layer, int kv_type,
-                            const AttnShape &sh, int batch, float *scores, float *part_m, float *part_s, float *part_o,
-                            float *out, int ldo, cudaStream_t st)
+template <typename T>
+static int launch_attn_t(const float *q, int ldq, const float *k, const float *v, int ldkv, const int32_t *pos,
+                         const float *cos_t, const float *sin_t, const KvView *views, int layer, const AttnShape &sh,
+                         int batch, float *scores, float *part_m, float *part_s, float *part_o, int *counters,
+                         float *out, int ldo, bool pdl, cudaStream_t st)
 {
-    const int G = sh.heads / sh.heads_kv, nchunk = sh.max_ctx / KV_PAGE;
+    const int nchunk = sh.max_ctx / KV_PAGE;
     dim3 grid(nchunk, sh.heads_kv, batch);
-    size_t sm1 = sizeof(float) * (G * sh.head_dim + G);
-    size_t sm2 = sizeof(float) * (G * KV_PAGE + 2 * G);
-    if (kv_type == LLMDOT_KV_F16) {
-        attn_scores_kernel<__half><<<grid, 256, sm1, st>>>(q, ldq, pos, views, layer, sh, scores, part_m);
-        attn_pv_kernel<__half><<<grid, 256, sm2, st>>>(pos, views, layer, sh, scores, part_m, part_s, part_o);
-    } else {
-        attn_scores_kernel<float><<<grid, 256, sm1, st>>>(q, ldq, pos, views, layer, sh, scores, part_m);
-        attn_pv_kernel<float><<<grid, 256, sm2, st>>>(pos, views, layer, sh, scores, part_m, part_s, part_o);
+    static bool attr_set = false;
+    if (!attr_set) {
+        LLMDOT_CUDA_TRY(cudaFuncSetAttribute(attn_scores_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        LLMDOT_CUDA_TRY(cudaFuncSetAttribute(attn_pv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr_set = true;
     }
-    LLMDOT_CUDA_TRY(cudaGetLastError());
-    attn_combine_kernel<<<dim3(sh.heads, batch), sh.head_dim < 256 ? sh.head_dim : 256, 0, st>>>(pos, sh, part_s, part_o,
-                                                                                              out, ldo);
-    LLMDOT_CUDA_TRY(cudaGetLastError());
+    LLMDOT_CUDA_TRY(launch_kernel(pdl, attn_scores_kernel<T>, grid, dim3(256), scores_smem(sh, sizeof(T)), st, q, ldq, k,
+                                  v, ldkv, pos, cos_t, sin_t, views, layer, sh, scores, part_m));
+    LLMDOT_CUDA_TRY(launch_kernel(pdl, attn_pv_kernel<T>, grid, dim3(256), pv_smem(sh, sizeof(T)), st, pos, views, layer,
+                                  sh, (const float *)scores, (const float *)part_m, part_s, part_o, counters, out, ldo));
     return LLMDOT_OK;
+}
+
+int launch_attention_step(const float *q, int ldq, const float *k, const float *v, int ldkv, const int32_t *pos,
+                          const float *cos_t, const float *sin_t, const KvView *views, int layer, int kv_type,
+                          const AttnShape &sh, int batch, float *scores, float *part_m, float *part_s, float *part_o,
+                          int *counters, float *out, int ldo, bool pdl, cudaStream_t st)
+{
+    if (scores_smem(sh, 4) > 200 * 1024 || pv_smem(sh, 4) > 200 * 1024)
+        return fail(LLMDOT_E_UNSUPPORTED, "attention: head too large for the page staging");
+    if (kv_type == LLMDOT_KV_F16)
+        return launch_attn_t<__half>(q, ldq, k, v, ldkv, pos, cos_t, sin_t, views, layer, sh, batch, scores, part_m,
+                                     part_s, part_o, counters, out, ldo, pdl, st);
+    return launch_attn_t<float>(q, ldq, k, v, ldkv, pos, cos_t, sin_t, views, layer, sh, batch, scores, part_m, part_s,
+                                part_o, counters, out, ldo, pdl, st);
 }
 
 }  // namespace llmdot

@@ -1,4 +1,4 @@
-// attention.cuh -- paged KV cache views and the decode-attention launchers.
+// attention.cuh -- paged KV cache views and the decode-attention launcher.
 #pragma once
 #include "common.cuh"
 
@@ -22,16 +22,14 @@ struct AttnShape {
     int rope_half;
 };
 
-// RoPE of q (in place) and k, then k and v appended to the cache at pos[b].
-int launch_rope_append(float *q, int ldq, const float *k, const float *v, int ldkv, const int32_t *pos,
-                       const float *cos_t, const float *sin_t, const KvView *views, int layer, int kv_type,
-                       const AttnShape &sh, int batch, cudaStream_t st);
-
-// softmax(q K^T * 1/sqrt(hd), softcap) V over the window of every session, written to
-// out[b][h*hd + d].  Scratch: scores [batch][heads][max_ctx], part_o
-// [batch][heads][max_ctx/KV_PAGE][head_dim], part_m/part_s [batch][heads][max_ctx/KV_PAGE].
-int launch_attention_decode(const float *q, int ldq, const int32_t *pos, const KvView *views, int layer, int kv_type,
-                            const AttnShape &sh, int batch, float *scores, float *part_m, float *part_s, float *part_o,
-                            float *out, int ldo, cudaStream_t st);
+// One layer of decode attention for `batch` sessions: RoPE of q and of the new k, append of
+// k and v at pos[b], softmax(q K^T / sqrt(hd), softcap) V over the window, written to
+// out[b][h*hd + d].  q/k/v are the raw projections.  Scratch: scores [batch][heads][max_ctx],
+// part_m/part_s [batch][heads][max_ctx/KV_PAGE], part_o [..][head_dim], counters
+// [batch][heads_kv] (zero on entry, left zero).
+int launch_attention_step(const float *q, int ldq, const float *k, const float *v, int ldkv, const int32_t *pos,
+                          const float *cos_t, const float *sin_t, const KvView *views, int layer, int kv_type,
+                          const AttnShape &sh, int batch, float *scores, float *part_m, float *part_s, float *part_o,
+                          int *counters, float *out, int ldo, bool pdl, cudaStream_t st);
 
 }  // namespace llmdot

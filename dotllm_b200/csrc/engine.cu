@@ -1,6 +1,7 @@
 // engine.cu -- model upload, sessions, and the decode step (the device-resident
 // counterpart of InferenceEngine.ProcessToken, src/Llmdot.Core/Inference/InferenceEngine.cs:134-602).
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 #include <strings.h>
 
@@ -108,6 +109,11 @@ int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc 
     llmdot_model *m = new llmdot_model();
     m->device = device;
     m->cfg = c;
+    // LLMDOT_REFERENCE_MATVEC=1 selects the generic (per-element) matvec everywhere; the tests
+    // use it to check the tensor-core path against the straightforward one.
+    m->use_fast_gemv = getenv("LLMDOT_REFERENCE_MATVEC") == nullptr;
+    // programmatic dependent launch between the step's kernels (LLMDOT_NO_PDL=1 turns it off)
+    m->use_pdl = getenv("LLMDOT_NO_PDL") == nullptr;
     int rc = LLMDOT_OK;
     auto bail = [&](int code) { model_destroy(m); return code; };
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -236,6 +242,8 @@ int ensure_workspace(llmdot_model *m, int batch)
     LLMDOT_TRY(dalloc(a, &w.err, 1));
     LLMDOT_TRY(dalloc(a, &w.hist, (size_t)HIST_STEPS * B));
     LLMDOT_TRY(dalloc(a, &w.hist_step, 1));
+    LLMDOT_TRY(dalloc(a, &w.counters, B * c.heads_kv));
+    LLMDOT_CUDA_TRY(cudaMemset(w.counters, 0, sizeof(int) * B * c.heads_kv));
     LLMDOT_CUDA_TRY(cudaMemset(w.err, 0, sizeof(int)));
     LLMDOT_CUDA_TRY(cudaMemset(w.hist_step, 0, sizeof(int32_t)));
     w.batch = batch;
@@ -257,6 +265,7 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
     const int H = c.hidden, qDim = c.heads * c.head_dim, kvDim = c.heads_kv * c.head_dim;
     const bool gemma = c.template_id == 2;
     const bool fast = m->use_fast_gemv;
+    const bool pdl = m->use_pdl;
     AttnShape sh;
     sh.heads = c.heads;
     sh.heads_kv = c.heads_kv;
@@ -268,53 +277,78 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
     sh.inv_sqrt_hd = 1.0f / sqrtf((float)c.head_dim);
     sh.rope_half = m->rope_half;
 
+    // y = epilogue(W . [rmsnorm](x)); the tensor-core kernel fuses the norm and the epilogue,
+    // the generic kernel runs them as separate launches.
+    auto mv = [&](const DevMat &W, const DevMat *W1, const float *x, int ldx, const float *norm_w, float *y, int ldy,
+                  int mode) -> int {
+        if (fast && gemv_fast_supported(W, batch) && (!W1 || gemv_fast_supported(*W1, batch)))
+            return launch_gemv_fast_ex(W, W1, norm_w, c.eps, x, ldx, batch, y, ldy, mode, st, pdl);
+        const float *xin = x;
+        int ld = ldx;
+        if (norm_w) {
+            LLMDOT_TRY(launch_rmsnorm(x, ldx, norm_w, w.xn, H, H, batch, c.eps, st));
+            xin = w.xn;
+            ld = H;
+        }
+        if (mode == GEMV_SILU_MUL || mode == GEMV_GELU_MUL) {
+            LLMDOT_TRY(launch_gemv_ref(W.raw, W.type, W.rows, W.cols, xin, ld, batch, w.gate, c.ffn, false, st));
+            LLMDOT_TRY(launch_gemv_ref(W1->raw, W1->type, W1->rows, W1->cols, xin, ld, batch, w.up, c.ffn, false, st));
+            return launch_act_mul(mode == GEMV_GELU_MUL, w.gate, w.up, y, c.ffn, batch, st);
+        }
+        return launch_gemv_ref(W.raw, W.type, W.rows, W.cols, xin, ld, batch, y, ldy, mode == GEMV_ADD, st);
+    };
+
     // GetEmbedding + EmbeddingScale
     LLMDOT_TRY(launch_embed(m->emb.raw, m->emb.type, H, c.vocab, tokens, batch, c.emb_scale, w.h, H, w.err, st));
     for (int l = 0; l < c.layers; l++) {
         const LayerW &L = m->layers[l];
-        // ApplyNorm(attn_norm) :544-562
-        LLMDOT_TRY(launch_rmsnorm(w.h, H, L.attn_norm, w.xn, H, H, batch, c.eps, st));
-        // Q/K/V projections :321-353
+        // ApplyNorm(attn_norm) :544-562 fused into the Q/K/V projections :321-353
         float *q, *k, *v;
         int ldq, ldkv;
         if (L.qkv.valid()) {
-            LLMDOT_TRY(gemv(L.qkv, w.xn, H, batch, w.qkv, qDim + 2 * kvDim, false, fast, st));
+            LLMDOT_TRY(mv(L.qkv, nullptr, w.h, H, L.attn_norm, w.qkv, qDim + 2 * kvDim, GEMV_STORE));
             q = w.qkv;
             k = w.qkv + qDim;
             v = w.qkv + qDim + kvDim;
             ldq = ldkv = qDim + 2 * kvDim;
         } else {
-            LLMDOT_TRY(gemv(L.q, w.xn, H, batch, w.q, qDim, false, fast, st));
-            LLMDOT_TRY(gemv(L.k, w.xn, H, batch, w.k, kvDim, false, fast, st));
-            LLMDOT_TRY(gemv(L.v, w.xn, H, batch, w.v, kvDim, false, fast, st));
+            int qkv_rc = LLMDOT_E_UNSUPPORTED;
+            if (fast && gemv_fast_supported(L.q, batch) && gemv_fast_supported(L.k, batch) &&
+                gemv_fast_supported(L.v, batch)) {
+                // Q, K and V share the normed input: one launch
+                const GemvTarget tg[3] = {{&L.q, nullptr, w.q, qDim}, {&L.k, nullptr, w.k, kvDim},
+                                          {&L.v, nullptr, w.v, kvDim}};
+                qkv_rc = launch_gemv_multi(tg, 3, L.attn_norm, c.eps, w.h, H, batch, GEMV_STORE, pdl, st);
+                if (qkv_rc != LLMDOT_OK && qkv_rc != LLMDOT_E_UNSUPPORTED) return qkv_rc;
+            }
+            if (qkv_rc != LLMDOT_OK) {
+                // mixed Q4_K/Q6_K segments whose shared-memory layout does not fit one launch
+                LLMDOT_TRY(mv(L.q, nullptr, w.h, H, L.attn_norm, w.q, qDim, GEMV_STORE));
+                LLMDOT_TRY(mv(L.k, nullptr, w.h, H, L.attn_norm, w.k, kvDim, GEMV_STORE));
+                LLMDOT_TRY(mv(L.v, nullptr, w.h, H, L.attn_norm, w.v, kvDim, GEMV_STORE));
+            }
             q = w.q;
             k = w.k;
             v = w.v;
             ldq = qDim;
             ldkv = kvDim;
         }
-        // RoPE of q and k, K/V cache append :362-382
-        LLMDOT_TRY(launch_rope_append(q, ldq, k, v, ldkv, pos, m->cos_t, m->sin_t, views, l, kv_type, sh,
-                                      batch, st));
-        // attention :384-442
-        LLMDOT_TRY(launch_attention_decode(q, ldq, pos, views, l, kv_type, sh, batch, w.scores, w.part_m,
-                                           w.part_s, w.part_o, w.attn, qDim, st));
+        // RoPE of q and k, K/V cache append :362-382, attention :384-442
+        LLMDOT_TRY(launch_attention_step(q, ldq, k, v, ldkv, pos, m->cos_t, m->sin_t, views, l, kv_type, sh, batch,
+                                         w.scores, w.part_m, w.part_s, w.part_o, w.counters, w.attn, qDim, pdl, st));
         // attn_output matvec + residual add :444-449, :189
-        LLMDOT_TRY(gemv(L.o, w.attn, qDim, batch, w.h, H, true, fast, st));
+        LLMDOT_TRY(mv(L.o, nullptr, w.attn, qDim, nullptr, w.h, H, GEMV_ADD));
         if (gemma && L.post_attn) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_attn, w.h, H, H, batch, c.eps, st));
-        // ApplyNorm(ffn_norm ?? attn_norm)
-        LLMDOT_TRY(launch_rmsnorm(w.h, H, L.ffn_norm ? L.ffn_norm : L.attn_norm, w.xn, H, H, batch, c.eps, st));
-        // FfnForward :452-487: gate, act, up, mul, down + residual add
-        LLMDOT_TRY(gemv(L.gate, w.xn, H, batch, w.gate, c.ffn, false, fast, st));
-        LLMDOT_TRY(gemv(L.up, w.xn, H, batch, w.up, c.ffn, false, fast, st));
-        LLMDOT_TRY(launch_act_mul(c.ffn_type == 2, w.gate, w.up, w.gate, c.ffn, batch, st));
-        LLMDOT_TRY(gemv(L.down, w.gate, c.ffn, batch, w.h, H, true, fast, st));
+        // FfnForward :452-487: ApplyNorm(ffn_norm ?? attn_norm), gate and up, act(gate)*up in one launch
+        LLMDOT_TRY(mv(L.gate, &L.up, w.h, H, L.ffn_norm ? L.ffn_norm : L.attn_norm, w.gate, c.ffn,
+                      c.ffn_type == 2 ? GEMV_GELU_MUL : GEMV_SILU_MUL));
+        // down projection + residual add
+        LLMDOT_TRY(mv(L.down, nullptr, w.gate, c.ffn, nullptr, w.h, H, GEMV_ADD));
         if (gemma && L.post_ffw) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_ffw, w.h, H, H, batch, c.eps, st));
     }
-    // ApplyFinalNorm :575-581, ComputeLogits :583-602
-    LLMDOT_TRY(launch_rmsnorm(w.h, H, m->out_norm, w.xn, H, H, batch, c.eps, st));
+    // ApplyFinalNorm :575-581 fused into ComputeLogits :583-602
     const DevMat &head = m->out.valid() ? m->out : m->emb;
-    LLMDOT_TRY(gemv(head, w.xn, H, batch, w.logits, c.vocab, false, fast, st));
+    LLMDOT_TRY(mv(head, nullptr, w.h, H, m->out_norm, w.logits, c.vocab, GEMV_STORE));
     // final softcap + greedy argmax (InferenceEngine.cs:105-108, Sampler.cs:26-27)
     LLMDOT_TRY(launch_argmax(w.logits, c.vocab, c.vocab, batch, w.keys, next, c.has_final_cap != 0, c.final_cap,
                              nullptr, st));

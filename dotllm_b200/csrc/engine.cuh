@@ -37,6 +37,7 @@ struct Workspace {
     int32_t *tokens = nullptr, *pos = nullptr, *next = nullptr;
     KvView *views = nullptr;
     int *err = nullptr;
+    int *counters = nullptr;   // [batch][heads_kv] attention page-combine arrival counters
     int32_t *hist = nullptr;   // [HIST_STEPS][batch] greedy ids recorded by captured steps
     int32_t *hist_step = nullptr;
     std::vector<void *> allocs;
@@ -60,6 +61,7 @@ struct llmdot_model {
     std::map<std::string, llmdot::DevMat *> by_name;
     llmdot::Workspace ws;
     bool use_fast_gemv = true;
+    bool use_pdl = true;
 };
 
 struct llmdot_session {

@@ -1,11 +1,737 @@
-// gemv.cu -- tensor-core quantised matvec (placeholder until the tiled kernel lands).
+// gemv.cu -- tensor-core quantised matvec for decode (1..4 input rows).
+//
+// Replaces TensorOps.MatMulFusedQ4_K / MatMulFusedQ6_K (src/Llmdot.Core/Tensors/TensorOps.cs:230-395)
+// on the device.  The matvec is HBM-bound, so the design goal is to stream every weight byte
+// exactly once with fully coalesced 128-bit loads and to spend as few issue slots per weight
+// as possible turning it into tensor-core operands:
+//
+// * Layout.  At model load every Q4_K / Q6_K matrix is re-laid out (same byte count) into
+//   tiles of 16 rows x one 256-weight super-block.  Inside a tile, the bytes lane L of a warp
+//   needs are one 16-byte slot of each 512-byte "plane", so each plane is one fully coalesced
+//   warp load; the per-row headers (d, dmin, scales) sit behind the planes.
+// * Math.  mma.sync m16n8k16 (fp16 in, fp32 accumulate).  The weights enter as exact small
+//   integers in fp16, built from nibbles with one LOP3 (magic 0x6400 = 1024.0) and one packed
+//   HFMA2/HSUB2.  The activation x is split into x_hi + x_lo (two fp16 columns of the MMA) after
+//   an exact power-of-two scaling, so each product is exact and the sum is fp32: the result
+//   agrees with the reference's fp32 dot to fp32 rounding, not to fp16 precision.
+//     Q4_K: A = q*sc (<= 945, exact), one MMA chain per super-block, then
+//           y += d*C - sum_j (8*d*sc_j + dmin*m_j) * S_j   with S_j the sub-block sums of x;
+//     Q6_K: A = q-32 (exact), one MMA per 16-weight sub-block, y += (d*sc_s) * C_s.
+// * One launch covers up to three matrices that read the same input (Q, K, V), each with its
+//   own type, and an optional RMSNorm of the input in the prologue (ApplyNorm,
+//   InferenceEngine.cs:544-562).  Epilogues: store, residual add (Add, :189/:195), or
+//   silu/gelu(gate)*up for the FFN (FfnForward :466-474, both matrices in one launch).
+// * Programmatic dependent launch: each warp fetches its first weight tile before waiting for
+//   the previous kernel, so weight streaming overlaps the predecessor's tail.
 #include "gemv.cuh"
+#include "ops.cuh"
 
 namespace llmdot {
-int prepare_tiled(llmdot_model *, DevMat &) { return LLMDOT_OK; }
-bool gemv_fast_supported(const DevMat &, int) { return false; }
-int launch_gemv_fast(const DevMat &, const float *, int, int, float *, int, bool, cudaStream_t)
-{
-    return fail(LLMDOT_E_UNSUPPORTED, "fast matvec not built");
+
+enum { QT_Q4K = 0, QT_Q6K = 1 };
+enum { GM_STORE = GEMV_STORE, GM_ADD = GEMV_ADD, GM_SILU_MUL = GEMV_SILU_MUL, GM_GELU_MUL = GEMV_GELU_MUL };
+
+constexpr int Q4K_TILE = 16 * 144;  // 2304
+constexpr int Q6K_TILE = 16 * 210;  // 3360
+
+// ------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c)
+{  // (a & b) | c
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
 }
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c)
+{
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ void mma_f16(float &d0, float &d1, float &d2, float &d3, uint32_t a0, uint32_t a1,
+                                        uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint4 ldg_stream(const void *p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
+{
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+__device__ __forceinline__ float half_bits(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)v)); }
+
+// ------------------------------------------------------------------ repack kernels
+// Q4_K tile (16 rows x 1 super-block), lane L = 4g + t owns rows g, g+8 and sub-blocks 2t, 2t+1:
+//   plane p (0..3) at p*512 + L*16: nibble bytes of sub-block 2t + (p&1) of row (p < 2 ? g : g+8)
+//   header at 2048 + g*32: bytes 0..15 of row g's block, then of row g+8's block
+__global__ void repack_q4k_kernel(const uint8_t *__restrict__ raw, uint8_t *__restrict__ tiled, int rows, int nsb,
+                                  uint64_t rbytes, int ntiles)
+{
+    int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= ntiles * 32) return;
+    int tile = idx >> 5, L = idx & 31, g = L >> 2, t = L & 3;
+    int rt = tile / nsb, sb = tile % nsb;
+    uint8_t *dst = tiled + (uint64_t)tile * Q4K_TILE;
+    for (int p = 0; p < 4; p++) {
+        int row = rt * 16 + (p < 2 ? g : g + 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (row < rows) v = *(const uint4 *)(raw + (uint64_t)row * rbytes + (uint64_t)sb * 144 + 16 + 16 * (2 * t + (p & 1)));
+        *(uint4 *)(dst + p * 512 + L * 16) = v;
+    }
+    if (t == 0)
+        for (int h = 0; h < 2; h++) {
+            int row = rt * 16 + g + 8 * h;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (row < rows) v = *(const uint4 *)(raw + (uint64_t)row * rbytes + (uint64_t)sb * 144);
+            *(uint4 *)(dst + 2048 + g * 32 + h * 16) = v;
+        }
+}
+
+// Q6_K element (sub-block s, lane t, i) = super-block element 16s + 4t + i.  Per lane and row:
+//   L_w (w = 0..7): nibbles of sub-blocks 2w (bits 0-3 i0, 16-19 i1, 4-7 i2, 20-23 i3) and
+//                   2w+1 (bits 8-11 i0, 24-27 i1, 12-15 i2, 28-31 i3);
+//   H_u (u = 0..3): 2-bit highs of L_{2u} pair k at bits 4+2k / 20+2k, of L_{2u+1} pair k at
+//                   {0,2,12,14}[k] / {16,18,28,30}[k]  (pair k = (s odd ? 2 : 0) + (i >= 2)).
+//   planes 0,1 = L_0..3, L_4..7 of row g; plane 2 = H_0..3 of row g; planes 3..5 the same for row g+8;
+//   sc at 3072 + g*32 (16 int8 of row g, then row g+8); d at 3328 + g*4 (row g, row g+8).
+__device__ __forceinline__ int q6_value(const uint8_t *blk, int e)
+{
+    int n = e >> 7, rr = e & 127, tt = rr >> 5, l = rr & 31;
+    int lo = (tt & 1) ? blk[n * 64 + l + 32] : blk[n * 64 + l];
+    lo = (tt & 2) ? (lo >> 4) : (lo & 0xF);
+    int hi = (blk[128 + n * 32 + l] >> (2 * tt)) & 3;
+    return lo | (hi << 4);
+}
+
+__global__ void repack_q6k_kernel(const uint8_t *__restrict__ raw, uint8_t *__restrict__ tiled, int rows, int nsb,
+                                  uint64_t rbytes, int ntiles)
+{
+    int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= ntiles * 32) return;
+    int tile = idx >> 5, L = idx & 31, g = L >> 2, t = L & 3;
+    int rt = tile / nsb, sb = tile % nsb;
+    uint8_t *dst = tiled + (uint64_t)tile * Q6K_TILE;
+    for (int h = 0; h < 2; h++) {
+        int row = rt * 16 + g + 8 * h;
+        uint32_t Lw[8] = {0, 0, 0, 0, 0, 0, 0, 0}, Hu[4] = {0, 0, 0, 0};
+        if (row < rows) {
+            const uint8_t *blk = raw + (uint64_t)row * rbytes + (uint64_t)sb * 210;
+            for (int s = 0; s < 16; s++)
+                for (int i = 0; i < 4; i++) {
+                    int q = q6_value(blk, 16 * s + 4 * t + i);
+                    int w = s >> 1, odd = s & 1, k = (odd ? 2 : 0) + (i >> 1), high = i & 1;
+                    int lobit = 4 * k + (high ? 16 : 0);
+                    Lw[w] |= (uint32_t)(q & 0xF) << lobit;
+                    int hb;
+                    if ((w & 1) == 0) hb = 4 + 2 * k + (high ? 16 : 0);
+                    else {
+                        const int pl[4] = {0, 2, 12, 14};
+                        hb = pl[k] + (high ? 16 : 0);
+                    }
+                    Hu[w >> 1] |= (uint32_t)((q >> 4) & 3) << hb;
+                }
+        }
+        *(uint4 *)(dst + (3 * h) * 512 + L * 16) = make_uint4(Lw[0], Lw[1], Lw[2], Lw[3]);
+        *(uint4 *)(dst + (3 * h + 1) * 512 + L * 16) = make_uint4(Lw[4], Lw[5], Lw[6], Lw[7]);
+        *(uint4 *)(dst + (3 * h + 2) * 512 + L * 16) = make_uint4(Hu[0], Hu[1], Hu[2], Hu[3]);
+        if (t == 0) {
+            uint8_t *scd = dst + 3072 + g * 32 + h * 16;
+            uint8_t *dd = dst + 3328 + g * 4 + h * 2;
+            if (row < rows) {
+                const uint8_t *blk = raw + (uint64_t)row * rbytes + (uint64_t)sb * 210;
+                for (int s = 0; s < 16; s++) scd[s] = blk[192 + s];
+                dd[0] = blk[208];
+                dd[1] = blk[209];
+            } else {
+                for (int s = 0; s < 16; s++) scd[s] = 0;
+                dd[0] = dd[1] = 0;
+            }
+        }
+    }
+}
+
+int prepare_tiled(llmdot_model *m, DevMat &W)
+{
+    if (W.type != T_Q4_K && W.type != T_Q6_K) return LLMDOT_OK;
+    if (W.cols % 256 != 0) return LLMDOT_OK;
+    const int nsb = W.cols / 256, nrt = (W.rows + 15) / 16, ntiles = nsb * nrt;
+    const size_t tb = W.type == T_Q4_K ? Q4K_TILE : Q6K_TILE;
+    cudaError_t e = cudaMalloc(&W.tiled, tb * (size_t)ntiles);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        W.tiled = nullptr;
+        return fail(LLMDOT_E_NOMEM, "tiled weight allocation failed");
+    }
+    m->allocs.push_back(W.tiled);
+    int threads = ntiles * 32;
+    if (W.type == T_Q4_K)
+        repack_q4k_kernel<<<(threads + 255) / 256, 256, 0, m->stream>>>(W.raw, W.tiled, W.rows, nsb, W.rbytes, ntiles);
+    else
+        repack_q6k_kernel<<<(threads + 255) / 256, 256, 0, m->stream>>>(W.raw, W.tiled, W.rows, nsb, W.rbytes, ntiles);
+    LLMDOT_CUDA_TRY(cudaGetLastError());
+    return LLMDOT_OK;
+}
+
+// ------------------------------------------------------------------ the matvec kernel
+struct GemvSeg {
+    const uint8_t *w;   // tiled weights
+    const uint8_t *w1;  // second ("up") matrix of the *_MUL epilogues (segment 0 only)
+    float *y;           // [nv][ldy]
+    int rows, nrt, qt, ldy;
+};
+
+struct GemvArgs {
+    GemvSeg seg[3];
+    int nseg, rt_total, nsb;
+    const float *x;  // [nv][ldx]
+    int ldx;
+    const float *norm_w;  // fused RMSNorm weight (nullable)
+    float eps;
+    int need_q4, need_q6;  // x layouts the segments use
+};
+
+// Tiles in flight per warp: each warp streams its tiles through a private ring of RING (2 or 3)
+// shared-memory slots filled with cp.async, so RING-1 tiles are always on their way while it
+// computes one.
+
+// x fragments in shared memory: 16-byte units u(sb, t, w, v, part) holding the B operands of
+// MMAs 2w and 2w+1 for lane-column (v, part); XOR-swizzled so a quarter-warp hits 8 distinct
+// bank groups.
+template <int NV> __device__ __forceinline__ int xunit(int sb, int t, int w, int v, int part)
+{
+    return (sb * 4 + t) * (16 * NV) + ((w * 2 * NV + v * 2 + part) ^ (2 * t));
+}
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc)
+{
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// The warp copies one tile (global, contiguous) into a ring slot: every lane moves its own
+// 16-byte plane slots (fully coalesced), the header bytes are split over the first lanes.
+__device__ __forceinline__ void issue_tile(uint8_t *slot, const uint8_t *tp, int qt, int lane)
+{
+    if (qt == QT_Q4K) {
+#pragma unroll
+        for (int p = 0; p < 4; p++) cp_async16(slot + p * 512 + lane * 16, tp + p * 512 + lane * 16);
+        if (lane < 16) cp_async16(slot + 2048 + lane * 16, tp + 2048 + lane * 16);
+    } else {
+#pragma unroll
+        for (int p = 0; p < 6; p++) cp_async16(slot + p * 512 + lane * 16, tp + p * 512 + lane * 16);
+        if (lane < 16) cp_async16(slot + 3072 + lane * 16, tp + 3072 + lane * 16);
+        else if (lane < 18) cp_async16(slot + 3328 + (lane - 16) * 16, tp + 3328 + (lane - 16) * 16);
+    }
+}
+
+// Per-lane view of one weight tile (Q4_K uses 6 of the registers, Q6_K 9), read from the slot.
+struct TileRegs {
+    uint4 r[9];
+};
+
+__device__ __forceinline__ void read_tile(TileRegs &T, const uint8_t *slot, int qt, int lane)
+{
+    const int g = lane >> 2;
+    if (qt == QT_Q4K) {
+#pragma unroll
+        for (int p = 0; p < 4; p++) T.r[p] = *(const uint4 *)(slot + p * 512 + lane * 16);
+        T.r[4] = *(const uint4 *)(slot + 2048 + g * 32);
+        T.r[5] = *(const uint4 *)(slot + 2048 + g * 32 + 16);
+    } else {
+#pragma unroll
+        for (int p = 0; p < 6; p++) T.r[p] = *(const uint4 *)(slot + p * 512 + lane * 16);
+        T.r[6] = *(const uint4 *)(slot + 3072 + g * 32);
+        T.r[7] = *(const uint4 *)(slot + 3072 + g * 32 + 16);
+        T.r[8].x = *(const uint32_t *)(slot + 3328 + g * 4);
+    }
+}
+
+template <int NV>
+__device__ __forceinline__ void q4k_tile(const TileRegs &T, const uint4 *__restrict__ xs, const float *__restrict__ S,
+                                         int nsb, int sb, int t, bool bact, int bv, int bpart, float &acc0, float &acc1,
+                                         float *corr0, float *corr1)
+{
+    float d_r[2], dm_r[2];
+    uint32_t sc2[2][2], nsc2[2][2];
+    float coef[2][2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const uint4 hd = T.r[4 + h];
+        d_r[h] = half_bits(hd.x & 0xFFFF);
+        dm_r[h] = half_bits(hd.x >> 16);
+        // the 24-bit (sc, m) pair of sub-blocks 2t, 2t+1 starts at byte 4 + 3t of the block
+        uint64_t yz = (uint64_t)hd.y | ((uint64_t)hd.z << 32);
+        uint64_t zw = (uint64_t)hd.z | ((uint64_t)hd.w << 32);
+        uint32_t pr = t == 0 ? (uint32_t)yz : t == 1 ? (uint32_t)(yz >> 24) : t == 2 ? (uint32_t)(zw >> 16)
+                                                                                      : (uint32_t)(hd.w >> 8);
+        int scA = pr & 63, mA = (pr >> 6) & 63, scB = (pr >> 12) & 63, mB = (pr >> 18) & 63;
+        uint32_t sA = hsub2(0x64006400u | (uint32_t)scA | ((uint32_t)scA << 16), 0x64006400u);
+        uint32_t sB = hsub2(0x64006400u | (uint32_t)scB | ((uint32_t)scB << 16), 0x64006400u);
+        sc2[h][0] = sA;
+        sc2[h][1] = sB;
+        nsc2[h][0] = hfma2(sA, 0xE400E400u, 0u);  // * -1024
+        nsc2[h][1] = hfma2(sB, 0xE400E400u, 0u);
+        coef[h][0] = fmaf(8.0f * d_r[h], (float)scA, dm_r[h] * (float)mA);
+        coef[h][1] = fmaf(8.0f * d_r[h], (float)scB, dm_r[h] * (float)mB);
+    }
+    float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        const int j = w >> 2;  // sub-block 2t + j
+        const uint32_t W0 = (&T.r[j].x)[w & 3], W1 = (&T.r[2 + j].x)[w & 3];
+        uint4 b = make_uint4(0, 0, 0, 0);
+        if (bact) b = xs[xunit<NV>(sb, t, w, bv, bpart)];
+        uint32_t a0 = hfma2(and_or(W0, 0x000F000Fu, 0x64006400u), sc2[0][j], nsc2[0][j]);
+        uint32_t a1 = hfma2(and_or(W1, 0x000F000Fu, 0x64006400u), sc2[1][j], nsc2[1][j]);
+        uint32_t a2 = hfma2(and_or(W0 >> 4, 0x000F000Fu, 0x64006400u), sc2[0][j], nsc2[0][j]);
+        uint32_t a3 = hfma2(and_or(W1 >> 4, 0x000F000Fu, 0x64006400u), sc2[1][j], nsc2[1][j]);
+        mma_f16(c0, c1, c2, c3, a0, a1, a2, a3, b.x, b.y);
+        a0 = hfma2(and_or(W0 >> 8, 0x000F000Fu, 0x64006400u), sc2[0][j], nsc2[0][j]);
+        a1 = hfma2(and_or(W1 >> 8, 0x000F000Fu, 0x64006400u), sc2[1][j], nsc2[1][j]);
+        a2 = hfma2(and_or(W0 >> 12, 0x000F000Fu, 0x64006400u), sc2[0][j], nsc2[0][j]);
+        a3 = hfma2(and_or(W1 >> 12, 0x000F000Fu, 0x64006400u), sc2[1][j], nsc2[1][j]);
+        mma_f16(c0, c1, c2, c3, a0, a1, a2, a3, b.z, b.w);
+    }
+    acc0 = fmaf(d_r[0], c0 + c1, acc0);
+    acc1 = fmaf(d_r[1], c2 + c3, acc1);
+#pragma unroll
+    for (int v = 0; v < NV; v++) {
+        const float *Sv = S + v * nsb * 8 + sb * 8 + 2 * t;
+        corr0[v] = fmaf(coef[0][0], Sv[0], fmaf(coef[0][1], Sv[1], corr0[v]));
+        corr1[v] = fmaf(coef[1][0], Sv[0], fmaf(coef[1][1], Sv[1], corr1[v]));
+    }
+}
+
+template <int NV>
+__device__ __forceinline__ void q6k_tile(const TileRegs &T, const uint4 *__restrict__ xs, int sb, int t, bool bact,
+                                         int bv, int bpart, float &acc0, float &acc1)
+{
+    const float d0 = half_bits(T.r[8].x & 0xFFFF);
+    const float d1 = half_bits(T.r[8].x >> 16);
+#pragma unroll
+    for (int s = 0; s < 16; s++) {
+        const int w = s >> 1, u = s >> 2, k0 = (s & 1) ? 2 : 0;
+        float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
+        uint32_t av[4];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t Lw = (&T.r[3 * h + (w >> 2)].x)[w & 3];
+            const uint32_t Hu = (&T.r[3 * h + 2].x)[u];
+#pragma unroll
+            for (int kk = 0; kk < 2; kk++) {
+                const int k = k0 + kk;
+                uint32_t hb;
+                if ((w & 1) == 0) hb = Hu >> (2 * k);
+                else hb = k == 0 ? (Hu << 4) : k == 1 ? (Hu << 2) : k == 2 ? (Hu >> 8) : (Hu >> 10);
+                uint32_t q = and_or(hb, 0x00300030u, and_or(Lw >> (4 * k), 0x000F000Fu, 0x64006400u));
+                av[kk * 2 + h] = hsub2(q, 0x64206420u);  // - (1024 + 32)
+            }
+        }
+        uint2 b = make_uint2(0, 0);
+        if (bact) {
+            const uint4 bb = xs[xunit<NV>(sb, t, w, bv, bpart)];
+            b = (s & 1) ? make_uint2(bb.z, bb.w) : make_uint2(bb.x, bb.y);
+        }
+        mma_f16(c0, c1, c2, c3, av[0], av[1], av[2], av[3], b.x, b.y);
+        const float s0 = d0 * (float)(int8_t)((&T.r[6].x)[s >> 2] >> (8 * (s & 3)));
+        const float s1 = d1 * (float)(int8_t)((&T.r[7].x)[s >> 2] >> (8 * (s & 3)));
+        acc0 = fmaf(s0, c0 + c1, acc0);
+        acc1 = fmaf(s1, c2 + c3, acc1);
+    }
+}
+
+__device__ __forceinline__ int find_seg(const GemvArgs &a, int gt, int &rt)
+{
+    int s = 0;
+    rt = gt;
+    while (s + 1 < a.nseg && rt >= a.seg[s].nrt) {
+        rt -= a.seg[s].nrt;
+        s++;
+    }
+    return s;
+}
+
+constexpr int GEMV_WARPS = 16;  // warps per CTA (one CTA per SM)
+
+// Shared memory of one CTA (byte offsets; all 16-byte aligned).
+struct GemvSmem {
+    int xs4, xs6, S, P, red, stat, wred, ring, total, slot;
+};
+__host__ __device__ inline GemvSmem gemv_layout(int nv, int nsb, int nmat, bool q4, bool q6, int max_rt_cta,
+                                                int ring)
+{
+    GemvSmem L;
+    const int xsz = nsb * 64 * nv * 16;
+    int o = 0;
+    L.xs4 = o;
+    o += q4 ? xsz : 0;
+    L.xs6 = o;
+    o += q6 ? xsz : 0;
+    L.S = o;
+    o += q4 ? nv * nsb * 8 * 4 : 0;
+    L.P = o;
+    o += q4 ? nv * nsb * 32 * 4 : 0;
+    L.red = o;  // [max_rt_cta][nmat][GEMV_WARPS][16][nv]
+    o += (max_rt_cta * nmat * GEMV_WARPS * 16 * nv * 4 + 15) / 16 * 16;
+    L.stat = o;
+    o += 16 * ((2 * nv * 4 + 15) / 16);
+    L.wred = o;
+    o += (GEMV_WARPS * 2 * nv * 4 + 15) / 16 * 16;
+    L.slot = q6 ? Q6K_TILE : Q4K_TILE;
+    L.ring = o;
+    o += GEMV_WARPS * ring * L.slot;
+    L.total = o;
+    return L;
+}
+
+template <int NV, int MODE, int RING>
+__global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, int max_rt_cta)
+{
+    constexpr int NMAT = (MODE >= GM_SILU_MUL) ? 2 : 1;
+    constexpr int NT = GEMV_WARPS * 32;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int nsb = a.nsb, cols = nsb * 256;
+    const GemvSmem L = gemv_layout(NV, nsb, NMAT, a.need_q4, a.need_q6, max_rt_cta, RING);
+    uint4 *xs4 = (uint4 *)(smem + L.xs4), *xs6 = (uint4 *)(smem + L.xs6);
+    float *S = (float *)(smem + L.S), *P = (float *)(smem + L.P), *red = (float *)(smem + L.red);
+    float *stat = (float *)(smem + L.stat), *wred = (float *)(smem + L.wred);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    uint8_t *ring = smem + L.ring + (size_t)warp * RING * L.slot;
+    // this CTA owns row tiles [rt_lo, rt_hi) of the concatenated segments; its flat tile list
+    // is (row tile, matrix, super-block), and warp w takes tiles w, w+16, ...
+    const int rt_lo = (int)((long long)blockIdx.x * a.rt_total / gridDim.x);
+    const int rt_hi = (int)((long long)(blockIdx.x + 1) * a.rt_total / gridDim.x);
+    const int nrt = rt_hi - rt_lo, per_rt = NMAT * nsb, ntile = nrt * per_rt;
+    const int F = ntile > warp ? (ntile - warp + GEMV_WARPS - 1) / GEMV_WARPS : 0;
+    auto issue = [&](int f) {
+        if (f < F) {
+            const int ti = warp + f * GEMV_WARPS, rtl = ti / per_rt, rem = ti % per_rt;
+            int rt;
+            const GemvSeg &sg = a.seg[find_seg(a, rt_lo + rtl, rt)];
+            const int tb = sg.qt == QT_Q4K ? Q4K_TILE : Q6K_TILE;
+            issue_tile(ring + (f % RING) * L.slot,
+                       (rem / nsb == 0 ? sg.w : sg.w1) + ((size_t)rt * nsb + rem % nsb) * tb, sg.qt, lane);
+        }
+        cp_async_commit();  // (possibly empty) group: keeps the wait count uniform
+    };
+    // weights are constant: start streaming before waiting for the previous kernel
+#pragma unroll
+    for (int f = 0; f < RING - 1; f++) issue(f);
+    pdl_launch();
+    pdl_wait();
+
+    // ---- prologue pass A: sum of squares (norm) and max |x| per vector, all threads
+    {
+        float ss[NV], mx[NV];
+#pragma unroll
+        for (int v = 0; v < NV; v++) ss[v] = mx[v] = 0.0f;
+        for (int i = tid; i < cols; i += NT) {
+            const float wn = a.norm_w ? a.norm_w[i] : 1.0f;
+#pragma unroll
+            for (int v = 0; v < NV; v++) {
+                const float h = a.x[(size_t)v * a.ldx + i];
+                ss[v] = fmaf(h, h, ss[v]);
+                mx[v] = fmaxf(mx[v], fabsf(a.norm_w ? __fmul_rn(wn, h) : h));
+            }
+        }
+#pragma unroll
+        for (int v = 0; v < NV; v++) {
+            ss[v] = warp_sum(ss[v]);
+            mx[v] = warp_max(mx[v]);
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int v = 0; v < NV; v++) {
+                wred[warp * 2 * NV + v] = ss[v];
+                wred[warp * 2 * NV + NV + v] = mx[v];
+            }
+        for (int i = tid; i < nrt * NMAT * GEMV_WARPS * 16 * NV; i += NT) red[i] = 0.0f;
+        __syncthreads();
+        if (tid < NV) {
+            float s = 0.0f, m = 0.0f;
+            for (int w = 0; w < GEMV_WARPS; w++) {
+                s += wred[w * 2 * NV + tid];
+                m = fmaxf(m, wred[w * 2 * NV + NV + tid]);
+            }
+            float inv = 1.0f;
+            if (a.norm_w) {  // VectorMath.RmsNorm: 1 / sqrt(ss/n + eps); x = (w*h)*inv
+                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)cols), a.eps)));
+                m = __fmul_rn(m, inv);  // rounding is monotone: max of the products
+            }
+            float sc = 1.0f;  // exact power of two putting max|x|*sc in [2^14, 2^15)
+            if (m > 0.0f && m < INFINITY) {
+                int e;
+                frexpf(m, &e);
+                sc = ldexpf(1.0f, 15 - e);
+            }
+            stat[tid] = inv;
+            stat[NV + tid] = sc;
+        }
+        __syncthreads();
+    }
+    // ---- pass B: fp16 hi/lo fragments of the scaled x for the layouts in use
+    for (int lay = 0; lay < 2; lay++) {
+        if ((lay == 0 && !a.need_q4) || (lay == 1 && !a.need_q6)) continue;
+        uint4 *xs = lay == 0 ? xs4 : xs6;
+        for (int it = tid; it < nsb * 32 * NV; it += NT) {
+            const int v = it % NV, r = it / NV, w = r & 7, tt = (r >> 3) & 3, sb = r >> 5;
+            // Q4_K: 8 consecutive weights 64t+8w.. in slot order {0,4,1,5,2,6,3,7};
+            // Q6_K: 4 at 32w+4t.. and 4 at 32w+16+4t.. in order
+            const int e0 = lay == 0 ? sb * 256 + 64 * tt + 8 * w : sb * 256 + 32 * w + 4 * tt;
+            const int e1 = lay == 0 ? e0 + 4 : e0 + 16;
+            const float *h = a.x + (size_t)v * a.ldx;
+            float4 p0 = *(const float4 *)(h + e0), p1 = *(const float4 *)(h + e1);
+            float c[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+            const float sc = stat[NV + v];
+            if (a.norm_w) {
+                // ((w*h)*inv)*sc == (w*h)*(inv*sc): sc is a power of two
+                const float f = stat[v] * sc;
+                const float4 n0 = *(const float4 *)(a.norm_w + e0), n1 = *(const float4 *)(a.norm_w + e1);
+                const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++) c[k] = __fmul_rn(__fmul_rn(nw[k], c[k]), f);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; k++) c[k] *= sc;
+            }
+            if (lay == 0) {
+                float psum = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 8; k++) psum += c[k];
+                P[((v * nsb + sb) * 4 + tt) * 8 + w] = psum;
+            }
+            float o[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) o[k] = lay == 0 ? c[(k >> 1) + 4 * (k & 1)] : c[k];
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                __half2 hh = __floats2half2_rn(o[2 * k], o[2 * k + 1]);
+                float2 hf = __half22float2(hh);
+                hi[k] = *reinterpret_cast<uint32_t *>(&hh);
+                lo[k] = pack_half2(o[2 * k] - hf.x, o[2 * k + 1] - hf.y);
+            }
+            xs[xunit<NV>(sb, tt, w, v, 0)] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            xs[xunit<NV>(sb, tt, w, v, 1)] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+    }
+    if (a.need_q4) {
+        __syncthreads();
+        // pass C: sub-block sums S_j = sum of its four 8-weight partials, fixed order
+        for (int it = tid; it < NV * nsb * 8; it += NT) {
+            const int v = it / (nsb * 8), jj = it % (nsb * 8), sb = jj >> 3, j = jj & 7;
+            const float *pp = P + ((v * nsb + sb) * 4 + (j >> 1)) * 8 + 4 * (j & 1);
+            S[it] = ((pp[0] + pp[1]) + pp[2]) + pp[3];
+        }
+    }
+    __syncthreads();
+
+    // ---- streaming loop: no CTA-wide barrier inside, warps run independently
+    const bool bact = g < 2 * NV;  // lanes whose B column is a real (vector, part)
+    const int bv = g >> 1, bpart = g & 1;
+    for (int f = 0; f < F; f++) {
+        issue(f + RING - 1);
+        cp_async_wait<RING - 1>();
+        __syncwarp();
+        const int ti = warp + f * GEMV_WARPS, rtl = ti / per_rt, rem = ti % per_rt, mat = rem / nsb, sb = rem % nsb;
+        int rt;
+        const int qt = a.seg[find_seg(a, rt_lo + rtl, rt)].qt;
+        float acc0 = 0.0f, acc1 = 0.0f;  // rows g, g+8 for vector t (MMA columns 2t, 2t+1)
+        float corr0[NV], corr1[NV];
+#pragma unroll
+        for (int v = 0; v < NV; v++) corr0[v] = corr1[v] = 0.0f;
+        TileRegs T;
+        read_tile(T, ring + (f % RING) * L.slot, qt, lane);
+        if (qt == QT_Q4K) q4k_tile<NV>(T, xs4, S, nsb, sb, t, bact, bv, bpart, acc0, acc1, corr0, corr1);
+        else q6k_tile<NV>(T, xs6, sb, t, bact, bv, bpart, acc0, acc1);
+        __syncwarp();  // the slot is refilled by a later issue
+        if (qt == QT_Q4K) {
+            // offset term: each lane of a row group covered 2 sub-blocks; sum over the group
+            float k0 = 0.0f, k1 = 0.0f;
+#pragma unroll
+            for (int v = 0; v < NV; v++) {
+                float c0v = corr0[v], c1v = corr1[v];
+                c0v += __shfl_xor_sync(0xffffffffu, c0v, 1);
+                c0v += __shfl_xor_sync(0xffffffffu, c0v, 2);
+                c1v += __shfl_xor_sync(0xffffffffu, c1v, 1);
+                c1v += __shfl_xor_sync(0xffffffffu, c1v, 2);
+                if (v == t) {
+                    k0 = c0v;
+                    k1 = c1v;
+                }
+            }
+            acc0 -= k0;
+            acc1 -= k1;
+        }
+        if (t < NV) {  // this warp's running partial for (row tile, matrix); only this warp writes it
+            float *rp = red + ((size_t)((rtl * NMAT + mat) * GEMV_WARPS + warp) * 16) * NV;
+            rp[g * NV + t] += acc0;
+            rp[(g + 8) * NV + t] += acc1;
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // ---- epilogue: every (row tile, row, vector) of the CTA, warps summed in a fixed order
+    for (int it = tid; it < nrt * 16 * NV; it += NT) {
+        const int rtl = it / (16 * NV), rr = (it / NV) % 16, v = it % NV;
+        int rt;
+        const GemvSeg &sg = a.seg[find_seg(a, rt_lo + rtl, rt)];
+        const int row = rt * 16 + rr;
+        if (row >= sg.rows) continue;
+        float o[NMAT];
+#pragma unroll
+        for (int mtx = 0; mtx < NMAT; mtx++) {
+            float s = 0.0f;
+            for (int w = 0; w < GEMV_WARPS; w++) s += red[(((rtl * NMAT + mtx) * GEMV_WARPS + w) * 16 + rr) * NV + v];
+            o[mtx] = s * (1.0f / stat[NV + v]);
+        }
+        float *yp = sg.y + (size_t)v * sg.ldy + row;
+        if (MODE == GM_STORE) *yp = o[0];
+        else if (MODE == GM_ADD) *yp = __fadd_rn(*yp, o[0]);
+        else {
+            const bool vl = row < sg.rows - sg.rows % 8;
+            const float act = MODE == GM_SILU_MUL ? silu_ref(o[0], vl) : gelu_ref(o[0], vl);
+            *yp = __fmul_rn(act, o[NMAT - 1]);
+        }
+    }
+}
+
+constexpr int GEMV_SMEM_MAX = 220 * 1024;
+
+// Shared memory needed for `nv` rows through matrices with nsb super-blocks (worst case over the
+// row-tile blocking); 0 when it does not fit even with a 2-deep ring.
+static size_t gemv_need(int nv, int nsb, int nmat, bool q4, bool q6, int max_rt, int *ring)
+{
+    for (int r = 3; r >= 2; r--) {
+        const GemvSmem L = gemv_layout(nv, nsb, nmat, q4, q6, max_rt, r);
+        if (L.total <= GEMV_SMEM_MAX) {
+            if (ring) *ring = r;
+            return (size_t)L.total;
+        }
+    }
+    return 0;
+}
+
+bool gemv_fast_supported(const DevMat &W, int nv)
+{
+    if (!W.tiled || nv < 1 || nv > 4) return false;
+    const bool q4 = W.type == T_Q4_K;
+    return gemv_need(nv, W.cols / 256, 2, q4, !q4, 4, nullptr) != 0;
+}
+
+template <int NV, int MODE, int RING> static int launch_r(const GemvArgs &a, int grid, int max_rt, size_t sm, bool pdl,
+                                                          cudaStream_t st)
+{
+    auto kern = gemv_mma_kernel<NV, MODE, RING>;
+    static bool attr_set = false;  // once per instantiation
+    if (!attr_set) {
+        LLMDOT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_MAX));
+        attr_set = true;
+    }
+    LLMDOT_CUDA_TRY(launch_kernel(pdl, kern, dim3(grid), dim3(GEMV_WARPS * 32), sm, st, a, max_rt));
+    return LLMDOT_OK;
+}
+
+template <int NV, int MODE> static int launch_t(const GemvArgs &a, bool pdl, cudaStream_t st)
+{
+    constexpr int NMAT = (MODE >= GM_SILU_MUL) ? 2 : 1;
+    // one CTA per SM (148 on B200), each with a contiguous block of row tiles; more CTAs only
+    // when the per-row-tile partial sums would not fit in shared memory
+    int grid = a.rt_total < 148 ? a.rt_total : 148;
+    int max_rt = (a.rt_total + grid - 1) / grid, ring = 0;
+    size_t sm = gemv_need(NV, a.nsb, NMAT, a.need_q4, a.need_q6, max_rt, &ring);
+    while (sm == 0 && grid < a.rt_total) {
+        grid += 148;
+        if (grid > a.rt_total) grid = a.rt_total;
+        max_rt = (a.rt_total + grid - 1) / grid;
+        sm = gemv_need(NV, a.nsb, NMAT, a.need_q4, a.need_q6, max_rt, &ring);
+    }
+    if (sm == 0) return fail(LLMDOT_E_UNSUPPORTED, "fast matvec: shared memory");
+    if (ring == 3) return launch_r<NV, MODE, 3>(a, grid, max_rt, sm, pdl, st);
+    return launch_r<NV, MODE, 2>(a, grid, max_rt, sm, pdl, st);
+}
+
+template <int MODE> static int launch_mode(const GemvArgs &a, int nv, bool pdl, cudaStream_t st)
+{
+    switch (nv) {
+    case 1: return launch_t<1, MODE>(a, pdl, st);
+    case 2: return launch_t<2, MODE>(a, pdl, st);
+    case 3: return launch_t<3, MODE>(a, pdl, st);
+    default: return launch_t<4, MODE>(a, pdl, st);
+    }
+}
+
+int launch_gemv_multi(const GemvTarget *tg, int ntarget, const float *norm_w, float eps, const float *x, int ldx,
+                      int nv, int mode, bool pdl, cudaStream_t st)
+{
+    if (ntarget < 1 || ntarget > 3 || (mode >= GEMV_SILU_MUL && ntarget != 1))
+        return fail(LLMDOT_E_INVALID, "fast matvec: bad target list");
+    GemvArgs a = {};
+    a.nseg = ntarget;
+    a.nsb = tg[0].W->cols / 256;
+    a.x = x;
+    a.ldx = ldx;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    for (int i = 0; i < ntarget; i++) {
+        const DevMat &W = *tg[i].W;
+        if (!gemv_fast_supported(W, nv) || W.cols != tg[0].W->cols)
+            return fail(LLMDOT_E_UNSUPPORTED, "fast matvec: unsupported matrix");
+        if (tg[i].W1 && (tg[i].W1->type != W.type || tg[i].W1->rows != W.rows || tg[i].W1->cols != W.cols ||
+                         !tg[i].W1->tiled))
+            return fail(LLMDOT_E_UNSUPPORTED, "fast matvec: gate/up matrices differ");
+        GemvSeg &s = a.seg[i];
+        s.w = W.tiled;
+        s.w1 = tg[i].W1 ? tg[i].W1->tiled : nullptr;
+        s.y = tg[i].y;
+        s.ldy = tg[i].ldy;
+        s.rows = W.rows;
+        s.nrt = (W.rows + 15) / 16;
+        s.qt = W.type == T_Q4_K ? QT_Q4K : QT_Q6K;
+        a.rt_total += s.nrt;
+        a.need_q4 |= s.qt == QT_Q4K;
+        a.need_q6 |= s.qt == QT_Q6K;
+    }
+    switch (mode) {
+    case GM_STORE: return launch_mode<GM_STORE>(a, nv, pdl, st);
+    case GM_ADD: return launch_mode<GM_ADD>(a, nv, pdl, st);
+    case GM_SILU_MUL: return launch_mode<GM_SILU_MUL>(a, nv, pdl, st);
+    default: return launch_mode<GM_GELU_MUL>(a, nv, pdl, st);
+    }
+}
+
+int launch_gemv_fast_ex(const DevMat &W0, const DevMat *W1, const float *norm_w, float eps, const float *x, int ldx,
+                        int nv, float *y, int ldy, int mode, cudaStream_t st, bool pdl)
+{
+    GemvTarget tg = {&W0, W1, y, ldy};
+    return launch_gemv_multi(&tg, 1, norm_w, eps, x, ldx, nv, mode, pdl, st);
+}
+
+int launch_gemv_fast(const DevMat &W, const float *x, int ldx, int nv, float *y, int ldy, bool accumulate,
+                     cudaStream_t st)
+{
+    return launch_gemv_fast_ex(W, nullptr, nullptr, 0.0f, x, ldx, nv, y, ldy, accumulate ? GM_ADD : GM_STORE, st,
+                               false);
+}
+
 }  // namespace llmdot

@@ -1,11 +1,29 @@
-// gemv.cuh -- tensor-core quantised matvec over 16-row tiled weights.
+// gemv.cuh -- tensor-core quantised matvec over 16-row tiled weights (see gemv.cu).
 #pragma once
 #include "engine.cuh"
 
 namespace llmdot {
-// Allocate and fill W.tiled (the tensor-core layout) when the type has a fast kernel.
+// Epilogues of the fast matvec
+enum { GEMV_STORE = 0, GEMV_ADD = 1, GEMV_SILU_MUL = 2, GEMV_GELU_MUL = 3 };
+
+// One output of a multi-matrix launch: y[v][row] (ldy) = epilogue(W . x[v]); W1 is the "up"
+// matrix of the GEMV_*_MUL epilogues.
+struct GemvTarget {
+    const DevMat *W;
+    const DevMat *W1;
+    float *y;
+    int ldy;
+};
+
+// Allocate and fill W.tiled (the tensor-core layout) for Q4_K / Q6_K matrices.
 int prepare_tiled(llmdot_model *m, DevMat &W);
 bool gemv_fast_supported(const DevMat &W, int nv);
 int launch_gemv_fast(const DevMat &W, const float *x, int ldx, int nv, float *y, int ldy, bool accumulate,
                      cudaStream_t st);
+// y = epilogue(W0 . rmsnorm(x)); norm_w == null means no fused norm.
+int launch_gemv_fast_ex(const DevMat &W0, const DevMat *W1, const float *norm_w, float eps, const float *x, int ldx,
+                        int nv, float *y, int ldy, int mode, cudaStream_t st, bool pdl = false);
+// Up to three matrices with the same input (e.g. Q, K, V) in one launch.
+int launch_gemv_multi(const GemvTarget *tg, int ntarget, const float *norm_w, float eps, const float *x, int ldx,
+                      int nv, int mode, bool pdl, cudaStream_t st);
 }  // namespace llmdot

@@ -59,6 +59,19 @@ class CudaModel:
         check(lib().llmdot_cuda_profile_matvec(self._h, tensor.encode(), batch, iters, C.byref(ms), C.byref(nb)))
         return ms.value, nb.value
 
+    def matvec(self, tensor: str, x, rows: int, mode: int = 0, norm_w=None) -> np.ndarray:
+        """y [batch, rows] = W.x for one uploaded weight (mode 0: the decode step's kernel,
+        1: the generic kernel, 2: the step's kernel with the fused RMSNorm of x by norm_w)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim == 1:
+            x = x[None, :]
+        nw = np.ascontiguousarray(norm_w, dtype=np.float32) if norm_w is not None else None
+        y = np.empty((x.shape[0], rows), dtype=np.float32)
+        check(lib().llmdot_cuda_model_matvec(self._h, tensor.encode(), x.ctypes.data_as(F32P), x.shape[0], mode,
+                                             nw.ctypes.data_as(F32P) if nw is not None else None,
+                                             y.ctypes.data_as(F32P)))
+        return y
+
     def weight_bytes(self) -> Tuple[int, int]:
         a, b = C.c_uint64(), C.c_uint64()
         check(lib().llmdot_cuda_model_weight_bytes(self._h, C.byref(a), C.byref(b)))

@@ -226,12 +226,25 @@ def _tensor_job(args):
 def build_model(cfg: SynthConfig, path: Optional[str] = None, workers: Optional[int] = None) -> str:
     """Write (or reuse) the synthetic GGUF for ``cfg`` and return its path.
 
-    Large models are generated by a pool of *spawned* worker processes (safe to
-    use in a process that already initialised CUDA); the file is identical to a
+    Large models are generated by a pool of worker processes.  The pool runs inside a
+    fresh interpreter (``python -m dotllm_b200.synth``), so callers may be scripts without
+    a ``__main__`` guard and may already have initialised CUDA; the file is identical to a
     single-process build because every tensor has its own seed."""
     path = path or model_path(cfg)
     if os.path.exists(path):
         return path
+    total = sum(t.n_bytes for t, _ in tensor_plan(cfg))
+    if workers is None and total > (64 << 20) and cfg.name in ALL_CONFIGS and ALL_CONFIGS[cfg.name] == cfg:
+        import subprocess
+        import sys
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        subprocess.run([sys.executable, "-m", "dotllm_b200.synth", cfg.name, path], check=True, cwd=root,
+                       timeout=1800)
+        return path
+    return _build_local(cfg, path, workers)
+
+
+def _build_local(cfg: SynthConfig, path: str, workers: Optional[int]) -> str:
     plan = tensor_plan(cfg)
     infos = [t for t, _ in plan]
     roles = {t.name: (r, i) for i, (t, r) in enumerate(plan)}
@@ -285,3 +298,14 @@ def get(name: str) -> SynthConfig:
 
 def with_overrides(cfg: SynthConfig, **kw) -> SynthConfig:
     return replace(cfg, **kw)
+
+
+if __name__ == "__main__":
+    import sys
+
+    # python -m dotllm_b200.synth NAME [PATH]: generate one synthetic model (worker pool)
+    _cfg = get(sys.argv[1])
+    _path = sys.argv[2] if len(sys.argv) > 2 else model_path(_cfg)
+    if not os.path.exists(_path):
+        _build_local(_cfg, _path, min(os.cpu_count() or 1, 24))
+    print(_path)

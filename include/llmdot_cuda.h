@@ -245,9 +245,18 @@ LLMDOT_API int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
                                         int n_steps, int32_t *out_tokens, float *elapsed_ms,
                                         int *kernels_per_step);
 
-/* Profiling hook (no counterpart in the reference): average device time of `iters` matvec
- * launches over the named weight tensor for `batch` input rows, timed with CUDA events on the
- * model's stream; bytes receives the quantised bytes one launch streams. */
+/* Diagnostic (no counterpart in the reference): y = W . x for one uploaded weight tensor and
+ * `batch` host input rows x [batch][cols] -> y [batch][rows] (host), through the same device
+ * matvec the decode step uses for that tensor (mode 0), the generic per-element kernel (mode 1),
+ * or with the step's fused RMSNorm of x by norm_w (mode 2, norm_w host [cols]). */
+LLMDOT_API int llmdot_cuda_model_matvec(llmdot_model *m, const char *tensor, const float *x, int batch,
+                                        int mode, const float *norm_w, float *y);
+
+/* Profiling hook (no counterpart in the reference): average device time of one matvec launch
+ * over the named weight tensor for `batch` input rows; `iters` launches are captured into a CUDA
+ * graph and one replay is timed with CUDA events on the model's stream.  A name of the form
+ * "blk.*.<suffix>" walks that matrix of every layer in turn (weights stream from HBM as in a
+ * decode step).  bytes receives the quantised bytes one launch streams (layer average). */
 LLMDOT_API int llmdot_cuda_profile_matvec(llmdot_model *m, const char *tensor, int batch, int iters,
                                           float *avg_ms, uint64_t *bytes);
 
