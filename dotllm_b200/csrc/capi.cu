@@ -434,7 +434,7 @@ namespace llmdot {
 // views from the workspace, so replays only need those arrays refreshed.
 struct StepGraph {
     cudaGraphExec_t exec = nullptr;
-    int batch = 0, kv_type = 0, kernels = 0;
+    int batch = 0, kv_type = 0, kernels = 0, gen = 0;
 };
 
 struct ModelExtra {
@@ -488,6 +488,13 @@ __global__ void advance_record_kernel(int32_t *pos, const int32_t *next, int32_t
 static int step_graph(llmdot_model *m, int batch, int kv_type, cudaGraphExec_t *out, int *kernels = nullptr)
 {
     ModelExtra &x = extra(m);
+    for (size_t i = 0; i < x.graphs.size();)  // graphs captured before the workspace was reallocated
+        if (x.graphs[i].gen != m->ws.gen) {
+            cudaGraphExecDestroy(x.graphs[i].exec);
+            x.graphs.erase(x.graphs.begin() + i);
+        } else {
+            i++;
+        }
     for (auto &g : x.graphs)
         if (g.batch == batch && g.kv_type == kv_type) {
             *out = g.exec;
@@ -521,7 +528,7 @@ static int step_graph(llmdot_model *m, int batch, int kv_type, cudaGraphExec_t *
     e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
-    x.graphs.push_back({exec, batch, kv_type, kn});
+    x.graphs.push_back({exec, batch, kv_type, kn, m->ws.gen});
     *out = exec;
     if (kernels) *kernels = kn;
     return LLMDOT_OK;
@@ -651,7 +658,11 @@ static int check_err_flag(llmdot_model *m)
     LLMDOT_CUDA_TRY(cudaMemcpy(&e, m->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {
         cudaMemset(m->ws.err, 0, sizeof(int));
-        return fail(LLMDOT_E_INVALID, "token id outside the vocabulary");
+        if (e == 1) return fail(LLMDOT_E_INVALID, "token id outside the vocabulary");
+        // a bounded wait of the persistent step kernel gave up: re-arm its state
+        step_kernel_reset(m, m->stream);
+        cudaStreamSynchronize(m->stream);
+        return fail(LLMDOT_E_TIMEOUT, e == 2 ? "step kernel: grid barrier timed out" : "step kernel: weight tile wait timed out");
     }
     return LLMDOT_OK;
 }
@@ -681,8 +692,14 @@ extern "C" int llmdot_cuda_prefill(llmdot_session *s, const int32_t *tokens, int
     cudaMemcpyAsync(dtok, hp.data(), sizeof(int32_t) * 2 * n, cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(w.views, &s->view, sizeof(KvView), cudaMemcpyHostToDevice, st);
     int rc = LLMDOT_OK;
-    for (int i = 0; i < n && rc == LLMDOT_OK; i++)
-        rc = forward_step(m, 1, s->kv_type, dtok + i, dpos + i, w.views, w.next, st);
+    if (step_kernel_supported(m, 1)) {
+        // all prompt tokens in one persistent launch; logits of the last one only
+        cudaMemcpyAsync(w.pos, dpos, sizeof(int32_t), cudaMemcpyDeviceToDevice, st);
+        rc = launch_step_kernel(m, 1, s->kv_type, n, dtok, st);
+    } else {
+        for (int i = 0; i < n && rc == LLMDOT_OK; i++)
+            rc = forward_step(m, 1, s->kv_type, dtok + i, dpos + i, w.views, w.next, st);
+    }
     cudaFreeAsync(dtok, st);
     if (rc != LLMDOT_OK) return rc;
     if (logits) LLMDOT_CUDA_TRY(cudaMemcpyAsync(logits, w.logits, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, st));
@@ -722,12 +739,14 @@ extern "C" int llmdot_cuda_decode(llmdot_session **sessions, int batch, const in
         x.h_pinned[x.cap + i] = sessions[i]->pos;
         x.h_views[i] = sessions[i]->view;
     }
-    cudaGraphExec_t g;
-    LLMDOT_TRY(step_graph(m, batch, kv_type, &g));
+    const bool persistent = m->step_decode && step_kernel_supported(m, batch);
+    cudaGraphExec_t g = nullptr;
+    if (!persistent) LLMDOT_TRY(step_graph(m, batch, kv_type, &g));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.next, x.h_pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.views, x.h_views, sizeof(KvView) * batch, cudaMemcpyHostToDevice, st));
-    LLMDOT_CUDA_TRY(cudaGraphLaunch(g, st));
+    if (persistent) LLMDOT_TRY(launch_step_kernel(m, batch, kv_type, 1, nullptr, st));
+    else LLMDOT_CUDA_TRY(cudaGraphLaunch(g, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(x.h_pinned + 2 * x.cap, w.next, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost, st));
     if (logits)
         LLMDOT_CUDA_TRY(cudaMemcpyAsync(logits, w.logits, sizeof(float) * (size_t)batch * m->cfg.vocab,
@@ -762,8 +781,9 @@ extern "C" int llmdot_cuda_generate(llmdot_session *s, const int32_t *prompt, in
     ModelExtra &x = extra(m);
     Workspace &w = m->ws;
     cudaStream_t st = m->stream;
-    cudaGraphExec_t g;
-    LLMDOT_TRY(step_graph(m, 1, s->kv_type, &g));
+    const bool persistent = m->step_decode && step_kernel_supported(m, 1);
+    cudaGraphExec_t g = nullptr;
+    if (!persistent) LLMDOT_TRY(step_graph(m, 1, s->kv_type, &g));
     // device state: w.next holds the token to feed, w.pos its position
     x.h_pinned[x.cap] = s->pos;
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t), cudaMemcpyHostToDevice, st));
@@ -773,7 +793,8 @@ extern "C" int llmdot_cuda_generate(llmdot_session *s, const int32_t *prompt, in
         out_tokens[produced++] = next;
         if (next == m->cfg.eos || produced == max_tokens) break;
         if (s->pos >= s->max_ctx) return fail(LLMDOT_E_INVALID, "generate: context length exceeded");
-        LLMDOT_CUDA_TRY(cudaGraphLaunch(g, st));
+        if (persistent) LLMDOT_TRY(launch_step_kernel(m, 1, s->kv_type, 1, nullptr, st));
+        else LLMDOT_CUDA_TRY(cudaGraphLaunch(g, st));
         LLMDOT_CUDA_TRY(cudaMemcpyAsync(x.h_pinned + 2 * x.cap, w.next, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
         LLMDOT_CUDA_TRY(cudaStreamSynchronize(st));
         next = x.h_pinned[2 * x.cap];
@@ -811,8 +832,13 @@ extern "C" int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
         x.h_pinned[x.cap + i] = sessions[i]->pos;
         x.h_views[i] = sessions[i]->view;
     }
-    cudaGraphExec_t g;
-    LLMDOT_TRY(step_graph(m, batch, kv_type, &g, kernels_per_step));
+    const bool persistent = m->step_decode && step_kernel_supported(m, batch);
+    cudaGraphExec_t g = nullptr;
+    if (persistent) {
+        if (kernels_per_step) *kernels_per_step = 1;  // at most: one launch runs a whole chunk of steps
+    } else {
+        LLMDOT_TRY(step_graph(m, batch, kv_type, &g, kernels_per_step));
+    }
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.next, x.h_pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.views, x.h_views, sizeof(KvView) * batch, cudaMemcpyHostToDevice, st));
@@ -825,11 +851,15 @@ extern "C" int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
         int chunk = n_steps - done < HIST_STEPS ? n_steps - done : HIST_STEPS;
         cudaMemsetAsync(w.hist_step, 0, sizeof(int32_t), st);
         cudaEventRecord(e0, st);
-        for (int i = 0; i < chunk; i++)
-            if (cudaGraphLaunch(g, st) != cudaSuccess) {
-                rc = cuda_fail(cudaGetLastError(), "cudaGraphLaunch");
-                break;
-            }
+        if (persistent) {
+            rc = launch_step_kernel(m, batch, kv_type, chunk, nullptr, st);
+        } else {
+            for (int i = 0; i < chunk; i++)
+                if (cudaGraphLaunch(g, st) != cudaSuccess) {
+                    rc = cuda_fail(cudaGetLastError(), "cudaGraphLaunch");
+                    break;
+                }
+        }
         cudaEventRecord(e1, st);
         if (rc == LLMDOT_OK &&
             cudaMemcpyAsync(out_tokens + (size_t)done * batch, w.hist, sizeof(int32_t) * (size_t)chunk * batch,
@@ -847,6 +877,56 @@ extern "C" int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
     LLMDOT_TRY(check_err_flag(m));
     for (int i = 0; i < batch; i++) sessions[i]->pos += n_steps;
     if (elapsed_ms) *elapsed_ms = total_ms;
+    return LLMDOT_OK;
+}
+
+extern "C" int llmdot_cuda_trace_step(llmdot_session **sessions, int batch, const int32_t *tokens, uint64_t *events,
+                                      int *kinds, int *n_phases, int *n_cta)
+{
+    if (!sessions || batch <= 0 || !tokens || !n_phases || !n_cta) return fail(LLMDOT_E_INVALID, "trace_step: bad arguments");
+    llmdot_model *m = sessions[0] ? sessions[0]->m : nullptr;
+    if (!m) return fail(LLMDOT_E_INVALID, "trace_step: null session");
+    const int kv_type = sessions[0]->kv_type;
+    for (int i = 0; i < batch; i++) {
+        llmdot_session *s = sessions[i];
+        if (!s || s->m != m || s->kv_type != kv_type)
+            return fail(LLMDOT_E_INVALID, "trace_step: sessions must share one model and KV type");
+        if (s->pos >= s->max_ctx) return fail(LLMDOT_E_INVALID, "trace_step: context length exceeded");
+        if (tokens[i] < 0 || tokens[i] >= m->cfg.vocab) return fail(LLMDOT_E_INVALID, "trace_step: token id outside the vocabulary");
+    }
+    LLMDOT_CUDA_TRY(cudaSetDevice(m->device));
+    LLMDOT_TRY(ensure_workspace(m, batch));
+    if (!step_kernel_supported(m, batch)) return fail(LLMDOT_E_UNSUPPORTED, "trace_step: no persistent step kernel");
+    std::vector<int> kind_buf(4096);
+    LLMDOT_TRY(step_kernel_shape(m, batch, n_phases, n_cta, kind_buf.data(), (int)kind_buf.size()));
+    if (!events) return LLMDOT_OK;
+    if (kinds)
+        for (int i = 0; i < *n_phases && i < (int)kind_buf.size(); i++) kinds[i] = kind_buf[i];
+    LLMDOT_TRY(ensure_pinned(m, batch));
+    ModelExtra &x = extra(m);
+    Workspace &w = m->ws;
+    cudaStream_t st = m->stream;
+    for (int i = 0; i < batch; i++) {
+        x.h_pinned[i] = tokens[i];
+        x.h_pinned[x.cap + i] = sessions[i]->pos;
+        x.h_views[i] = sessions[i]->view;
+    }
+    const size_t n_ev = (size_t)*n_phases * *n_cta * 16;
+    unsigned long long *d_ev = nullptr;
+    LLMDOT_CUDA_TRY(cudaMalloc(&d_ev, sizeof(unsigned long long) * n_ev));
+    cudaMemsetAsync(d_ev, 0, sizeof(unsigned long long) * n_ev, st);
+    cudaMemcpyAsync(w.next, x.h_pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(w.views, x.h_views, sizeof(KvView) * batch, cudaMemcpyHostToDevice, st);
+    int rc = launch_step_kernel(m, batch, kv_type, 1, nullptr, st, d_ev);
+    if (rc == LLMDOT_OK &&
+        cudaMemcpyAsync(events, d_ev, sizeof(unsigned long long) * n_ev, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        rc = cuda_fail(cudaGetLastError(), "trace copy");
+    if (cudaStreamSynchronize(st) != cudaSuccess && rc == LLMDOT_OK) rc = cuda_fail(cudaGetLastError(), "trace_step");
+    cudaFree(d_ev);
+    LLMDOT_TRY(rc);
+    LLMDOT_TRY(check_err_flag(m));
+    for (int i = 0; i < batch; i++) sessions[i]->pos += 1;
     return LLMDOT_OK;
 }
 

@@ -114,6 +114,11 @@ int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc 
     m->use_fast_gemv = getenv("LLMDOT_REFERENCE_MATVEC") == nullptr;
     // programmatic dependent launch between the step's kernels (LLMDOT_NO_PDL=1 turns it off)
     m->use_pdl = getenv("LLMDOT_NO_PDL") == nullptr;
+    // persistent whole-step kernel: prompt prefill by default (LLMDOT_NO_STEP_KERNEL=1 turns it
+    // off), greedy decode steps only with LLMDOT_STEP_DECODE=1 (the per-operation graph is faster
+    // there today)
+    m->use_step_kernel = getenv("LLMDOT_NO_STEP_KERNEL") == nullptr;
+    m->step_decode = m->use_step_kernel && getenv("LLMDOT_STEP_DECODE") != nullptr;
     int rc = LLMDOT_OK;
     auto bail = [&](int code) { model_destroy(m); return code; };
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -203,6 +208,7 @@ void model_destroy(llmdot_model *m)
     if (!m) return;
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    step_cache_free(m);
     for (void *p : m->ws.allocs) cudaFree(p);
     for (void *p : m->allocs) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -215,7 +221,9 @@ int ensure_workspace(llmdot_model *m, int batch)
     if (w.batch >= batch) return LLMDOT_OK;
     cudaStreamSynchronize(m->stream);
     for (void *p : w.allocs) cudaFree(p);
+    const int gen = w.gen + 1;
     w = Workspace();
+    w.gen = gen;
     const llmdot_config &c = m->cfg;
     const size_t B = (size_t)batch, qDim = (size_t)c.heads * c.head_dim, kvDim = (size_t)c.heads_kv * c.head_dim;
     const size_t nchunk = (size_t)m->max_ctx / KV_PAGE;

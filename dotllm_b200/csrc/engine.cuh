@@ -6,6 +6,7 @@
 
 #include "attention.cuh"
 #include "common.cuh"
+#include "step.cuh"
 
 namespace llmdot {
 
@@ -30,6 +31,7 @@ struct LayerW {
 // Step scratch, sized for `batch` rows.
 struct Workspace {
     int batch = 0;
+    int gen = 0;  // bumped whenever the buffers are reallocated (captured graphs and plans go stale)
     float *h = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *qkv = nullptr, *attn = nullptr;
     float *gate = nullptr, *up = nullptr, *logits = nullptr;
     float *scores = nullptr, *part_m = nullptr, *part_s = nullptr, *part_o = nullptr;
@@ -62,6 +64,9 @@ struct llmdot_model {
     llmdot::Workspace ws;
     bool use_fast_gemv = true;
     bool use_pdl = true;
+    bool use_step_kernel = true;            // persistent whole-step kernel for prefill
+    bool step_decode = false;               // ... and for decode steps
+    llmdot::StepCache *step_cache = nullptr;  // per-batch launch plans of that kernel
 };
 
 struct llmdot_session {

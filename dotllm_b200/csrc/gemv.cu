@@ -24,57 +24,12 @@
 // * Programmatic dependent launch: each warp fetches its first weight tile before waiting for
 //   the previous kernel, so weight streaming overlaps the predecessor's tail.
 #include "gemv.cuh"
+#include "gemv_tile.cuh"
 #include "ops.cuh"
 
 namespace llmdot {
 
-enum { QT_Q4K = 0, QT_Q6K = 1 };
 enum { GM_STORE = GEMV_STORE, GM_ADD = GEMV_ADD, GM_SILU_MUL = GEMV_SILU_MUL, GM_GELU_MUL = GEMV_GELU_MUL };
-
-constexpr int Q4K_TILE = 16 * 144;  // 2304
-constexpr int Q6K_TILE = 16 * 210;  // 3360
-
-// ------------------------------------------------------------------ PTX helpers
-__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c)
-{  // (a & b) | c
-    uint32_t r;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
-    return r;
-}
-__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c)
-{
-    uint32_t r;
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
-    return r;
-}
-__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b)
-{
-    uint32_t r;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-    return r;
-}
-__device__ __forceinline__ void mma_f16(float &d0, float &d1, float &d2, float &d3, uint32_t a0, uint32_t a1,
-                                        uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1)
-{
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint4 ldg_stream(const void *p)
-{
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
-{
-    __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t *>(&h);
-}
-__device__ __forceinline__ float half_bits(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)v)); }
 
 // ------------------------------------------------------------------ repack kernels
 // Q4_K tile (16 rows x 1 super-block), lane L = 4g + t owns rows g, g+8 and sub-blocks 2t, 2t+1:
@@ -210,14 +165,6 @@ struct GemvArgs {
 // shared-memory slots filled with cp.async, so RING-1 tiles are always on their way while it
 // computes one.
 
-// x fragments in shared memory: 16-byte units u(sb, t, w, v, part) holding the B operands of
-// MMAs 2w and 2w+1 for lane-column (v, part); XOR-swizzled so a quarter-warp hits 8 distinct
-// bank groups.
-template <int NV> __device__ __forceinline__ int xunit(int sb, int t, int w, int v, int part)
-{
-    return (sb * 4 + t) * (16 * NV) + ((w * 2 * NV + v * 2 + part) ^ (2 * t));
-}
-
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc)
 {
     const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
@@ -239,122 +186,6 @@ __device__ __forceinline__ void issue_tile(uint8_t *slot, const uint8_t *tp, int
         for (int p = 0; p < 6; p++) cp_async16(slot + p * 512 + lane * 16, tp + p * 512 + lane * 16);
         if (lane < 16) cp_async16(slot + 3072 + lane * 16, tp + 3072 + lane * 16);
         else if (lane < 18) cp_async16(slot + 3328 + (lane - 16) * 16, tp + 3328 + (lane - 16) * 16);
-    }
-}
-
-// Per-lane view of one weight tile (Q4_K uses 6 of the registers, Q6_K 9), read from the slot.
-struct TileRegs {
-    uint4 r[9];
-};
-
-__device__ __forceinline__ void read_tile(TileRegs &T, const uint8_t *slot, int qt, int lane)
-{
-    const int g = lane >> 2;
-    if (qt == QT_Q4K) {
-#pragma unroll
-        for (int p = 0; p < 4; p++) T.r[p] = *(const uint4 *)(slot + p * 512 + lane * 16);
-        T.r[4] = *(const uint4 *)(slot + 2048 + g * 32);
-        T.r[5] = *(const uint4 *)(slot + 2048 + g * 32 + 16);
-    } else {
-#pragma unroll
-        for (int p = 0; p < 6; p++) T.r[p] = *(const uint4 *)(slot + p * 512 + lane * 16);
-        T.r[6] = *(const uint4 *)(slot + 3072 + g * 32);
-        T.r[7] = *(const uint4 *)(slot + 3072 + g * 32 + 16);
-        T.r[8].x = *(const uint32_t *)(slot + 3328 + g * 4);
-    }
-}
-
-template <int NV>
-__device__ __forceinline__ void q4k_tile(const TileRegs &T, const uint4 *__restrict__ xs, const float *__restrict__ S,
-                                         int nsb, int sb, int t, bool bact, int bv, int bpart, float &acc0, float &acc1,
-                                         float *corr0, float *corr1)
-{
-    float d_r[2], dm_r[2];
-    uint32_t sc2[2][2], nsc2[2][2];
-    float coef[2][2];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const uint4 hd = T.r[4 + h];
-        d_r[h] = half_bits(hd.x & 0xFFFF);
-        dm_r[h] = half_bits(hd.x >> 16);
-        // the 24-bit (sc, m) pair of sub-blocks 2t, 2t+1 starts at byte 4 + 3t of the block
-        uint64_t yz = (uint64_t)hd.y | ((uint64_t)hd.z << 32);
-        uint64_t zw = (uint64_t)hd.z | ((uint64_t)hd.w << 32);
-        uint32_t pr = t == 0 ? (uint32_t)yz : t == 1 ? (uint32_t)(yz >> 24) : t == 2 ? (uint32_t)(zw >> 16)
-                                                                                      : (uint32_t)(hd.w >> 8);
-        int scA = pr & 63, mA = (pr >> 6) & 63, scB = (pr >> 12) & 63, mB = (pr >> 18) & 63;
-        uint32_t sA = hsub2(0x64006400u | (uint32_t)scA | ((uint32_t)scA << 16), 0x64006400u);
-        uint32_t sB = hsub2(0x64006400u | (uint32_t)scB | ((uint32_t)scB << 16), 0x64006400u);
-        sc2[h][0] = sA;
-        sc2[h][1] = sB;
-        nsc2[h][0] = hfma2(sA, 0xE400E400u, 0u);  // * -1024
-        nsc2[h][1] = hfma2(sB, 0xE400E400u, 0u);
-        coef[h][0] = fmaf(8.0f * d_r[h], (float)scA, dm_r[h] * (float)mA);
-        coef[h][1] = fmaf(8.0f * d_r[h], (float)scB, dm_r[h] * (float)mB);
-    }
-    float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 8; w++) {
-        const int j = w >> 2;  // sub-block 2t + j
-        const uint32_t W0 = (&T.r[j].x)[w & 3], W1 = (&T.r[2 + j].x)[w & 3];
-        uint4 b = make_uint4(0, 0, 0, 0);
-        if (bact) b = xs[xunit<NV>(sb, t, w, bv, bpart)];
-        uint32_t a0 = hfma2(and_or(W0, 0x000F000Fu, 0x64006400u), sc2[0][j], nsc2[0][j]);
-        uint32_t a1 = hfma2(and_or(W1, 0x000F000Fu, 0x64006400u), sc2[1][j], nsc2[1][j]);
-        uint32_t a2 = hfma2(and_or(W0 >> 4, 0x000F000Fu, 0x64006400u), sc2[0][j], nsc2[0][j]);
-        uint32_t a3 = hfma2(and_or(W1 >> 4, 0x000F000Fu, 0x64006400u), sc2[1][j], nsc2[1][j]);
-        mma_f16(c0, c1, c2, c3, a0, a1, a2, a3, b.x, b.y);
-        a0 = hfma2(and_or(W0 >> 8, 0x000F000Fu, 0x64006400u), sc2[0][j], nsc2[0][j]);
-        a1 = hfma2(and_or(W1 >> 8, 0x000F000Fu, 0x64006400u), sc2[1][j], nsc2[1][j]);
-        a2 = hfma2(and_or(W0 >> 12, 0x000F000Fu, 0x64006400u), sc2[0][j], nsc2[0][j]);
-        a3 = hfma2(and_or(W1 >> 12, 0x000F000Fu, 0x64006400u), sc2[1][j], nsc2[1][j]);
-        mma_f16(c0, c1, c2, c3, a0, a1, a2, a3, b.z, b.w);
-    }
-    acc0 = fmaf(d_r[0], c0 + c1, acc0);
-    acc1 = fmaf(d_r[1], c2 + c3, acc1);
-#pragma unroll
-    for (int v = 0; v < NV; v++) {
-        const float *Sv = S + v * nsb * 8 + sb * 8 + 2 * t;
-        corr0[v] = fmaf(coef[0][0], Sv[0], fmaf(coef[0][1], Sv[1], corr0[v]));
-        corr1[v] = fmaf(coef[1][0], Sv[0], fmaf(coef[1][1], Sv[1], corr1[v]));
-    }
-}
-
-template <int NV>
-__device__ __forceinline__ void q6k_tile(const TileRegs &T, const uint4 *__restrict__ xs, int sb, int t, bool bact,
-                                         int bv, int bpart, float &acc0, float &acc1)
-{
-    const float d0 = half_bits(T.r[8].x & 0xFFFF);
-    const float d1 = half_bits(T.r[8].x >> 16);
-#pragma unroll
-    for (int s = 0; s < 16; s++) {
-        const int w = s >> 1, u = s >> 2, k0 = (s & 1) ? 2 : 0;
-        float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
-        uint32_t av[4];
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const uint32_t Lw = (&T.r[3 * h + (w >> 2)].x)[w & 3];
-            const uint32_t Hu = (&T.r[3 * h + 2].x)[u];
-#pragma unroll
-            for (int kk = 0; kk < 2; kk++) {
-                const int k = k0 + kk;
-                uint32_t hb;
-                if ((w & 1) == 0) hb = Hu >> (2 * k);
-                else hb = k == 0 ? (Hu << 4) : k == 1 ? (Hu << 2) : k == 2 ? (Hu >> 8) : (Hu >> 10);
-                uint32_t q = and_or(hb, 0x00300030u, and_or(Lw >> (4 * k), 0x000F000Fu, 0x64006400u));
-                av[kk * 2 + h] = hsub2(q, 0x64206420u);  // - (1024 + 32)
-            }
-        }
-        uint2 b = make_uint2(0, 0);
-        if (bact) {
-            const uint4 bb = xs[xunit<NV>(sb, t, w, bv, bpart)];
-            b = (s & 1) ? make_uint2(bb.z, bb.w) : make_uint2(bb.x, bb.y);
-        }
-        mma_f16(c0, c1, c2, c3, av[0], av[1], av[2], av[3], b.x, b.y);
-        const float s0 = d0 * (float)(int8_t)((&T.r[6].x)[s >> 2] >> (8 * (s & 3)));
-        const float s1 = d1 * (float)(int8_t)((&T.r[7].x)[s >> 2] >> (8 * (s & 3)));
-        acc0 = fmaf(s0, c0 + c1, acc0);
-        acc1 = fmaf(s1, c2 + c3, acc1);
     }
 }
 

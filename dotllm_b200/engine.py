@@ -154,6 +154,21 @@ def decode_steps(sessions: List[CudaSession], tokens, n_steps: int):
     return out[:n_steps], ms.value, kps.value
 
 
+def trace_step(sessions: List[CudaSession], tokens):
+    """One greedy step of the persistent step kernel with per-phase timestamps.
+    Returns (events [phases, ctas, 16], kinds [phases]); see llmdot_cuda_trace_step."""
+    B = len(sessions)
+    arr = (VP * B)(*[s._h for s in sessions])
+    toks = np.ascontiguousarray(tokens, dtype=np.int32)
+    nph, ncta = C.c_int(), C.c_int()
+    check(lib().llmdot_cuda_trace_step(arr, B, toks.ctypes.data_as(I32P), None, None, C.byref(nph), C.byref(ncta)))
+    ev = np.zeros((nph.value, ncta.value, 16), dtype=np.uint64)
+    kinds = np.zeros(nph.value, dtype=np.int32)
+    check(lib().llmdot_cuda_trace_step(arr, B, toks.ctypes.data_as(I32P), ev.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                       kinds.ctypes.data_as(C.POINTER(C.c_int)), C.byref(nph), C.byref(ncta)))
+    return ev, kinds
+
+
 def decode_batch(sessions: List[CudaSession], tokens, want_logits: bool = False):
     """One greedy step for several sessions of one model (batched decode)."""
     B = len(sessions)

@@ -94,6 +94,8 @@ _SIGS = {
     "llmdot_cuda_generate": (C.c_int, [VP, I32P, C.c_int, C.c_int, I32P, C.POINTER(C.c_int)]),
     "llmdot_cuda_decode_steps": (C.c_int, [C.POINTER(VP), C.c_int, I32P, C.c_int, I32P, F32P, C.POINTER(C.c_int)]),
     "llmdot_cuda_profile_matvec": (C.c_int, [VP, C.c_char_p, C.c_int, C.c_int, F32P, C.POINTER(C.c_uint64)]),
+    "llmdot_cuda_trace_step": (C.c_int, [C.POINTER(VP), C.c_int, I32P, C.POINTER(C.c_uint64), C.POINTER(C.c_int),
+                                         C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "llmdot_cuda_argmax_noalloc": (C.c_int, [VP, C.c_int, C.c_int, C.c_int, VP, VP]),
     "llmdot_cuda_model_matvec": (C.c_int, [VP, C.c_char_p, F32P, C.c_int, C.c_int, F32P, F32P]),
 }

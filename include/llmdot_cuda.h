@@ -260,6 +260,18 @@ LLMDOT_API int llmdot_cuda_model_matvec(llmdot_model *m, const char *tensor, con
 LLMDOT_API int llmdot_cuda_profile_matvec(llmdot_model *m, const char *tensor, int batch, int iters,
                                           float *avg_ms, uint64_t *bytes);
 
+/* Profiling hook (no counterpart in the reference): runs ONE greedy decode step of the
+ * persistent step kernel for `batch` sessions fed `tokens` and records %globaltimer stamps (ns)
+ * events[(phase * n_cta + cta) * 16 + k], k = 0 phase start, 1 input built, 2 weight tiles done,
+ * 3 phase end; for warp 0 of the CTA 4 ns waiting for weight tiles, 5 ns computing them, 6 tile
+ * count; inside the input build 8 first thread's loads done, 9 statistics reduced, 10 first
+ * thread's fragments written (other k unused, 0); kinds[phase] = 1 attention scores, 2 attention P.V, 10 + epilogue (0 store, 1 residual
+ * add, 2 silu*up, 3 gelu*up, 4 logits + argmax) for matvec phases.  With events == NULL only
+ * *n_phases and *n_cta are filled in (size the arrays from them).  The sessions advance by one
+ * token otherwise.  LLMDOT_E_UNSUPPORTED when the model / batch runs without that kernel. */
+LLMDOT_API int llmdot_cuda_trace_step(llmdot_session **sessions, int batch, const int32_t *tokens,
+                                      uint64_t *events, int *kinds, int *n_phases, int *n_cta);
+
 /* Greedy argmax over logits that are already in device memory, without allocating any device
  * memory.  No counterpart in the reference: it exists for hosts that own all device memory
  * themselves (e.g. pools reserved at start-up for weights, KV pages and logits) and cannot let
