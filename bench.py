@@ -142,6 +142,11 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum over the four matvec launches of one decode layer
+# (profiles/gemv_mma_kernel_llama1b_b1.md) divided by their quantised weight bytes
+DRAM_PER_ALGORITHMIC_BYTE = (2.431232 + 18.949632 + 13.859072 + 3.880960) / (2.359296 + 18.874368 + 13.762560 + 3.813376)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -274,7 +279,10 @@ def main():
                    "parallelism": f"dp{world} (independent sessions per GPU)",
                    "l2": f"weights ({(layer_b + head_b) / 1e6:.0f} MB) exceed L2 (126 MB): inputs larger than L2, no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "kernel": "quantised matvec (all launches of one step)",
+                     "traffic": tot_bytes * DRAM_PER_ALGORITHMIC_BYTE,
+                     "traffic_note": "DRAM bytes per step scaled from the ncu capture in "
+                                     "profiles/gemv_mma_kernel_llama1b_b1.md (read+write / algorithmic = 1.008)",
+                     "kernel": "quantised matvec (all launches of one step)",
                      "launches_per_step": launches, "bytes_per_step": tot_bytes,
                      "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind},
         "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (step_ms * 1e-3) / 1e9,

@@ -1028,12 +1028,21 @@ extern "C" int llmdot_cuda_model_matvec(llmdot_model *m, const char *tensor, con
     if (cudaMemcpyAsync(dx, x, sizeof(float) * nx, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         (norm_w && cudaMemcpyAsync(dn, norm_w, sizeof(float) * W.cols, cudaMemcpyHostToDevice, st) != cudaSuccess))
         rc = cuda_fail(cudaGetLastError(), "model_matvec upload");
+    const bool batched = mode != 1 && m->use_fast_gemv && batch >= GEMM_MIN_ROWS && gemm_supported(W, batch);
+    if (rc == LLMDOT_OK && batched) rc = ensure_workspace(m, batch);
     if (rc == LLMDOT_OK) {
-        if (mode == 1 || !m->use_fast_gemv || !gemv_fast_supported(W, batch))
-            rc = launch_gemv_ref(W.raw, W.type, W.rows, W.cols, dx, W.cols, batch, dy, W.rows, false, st);
-        else
+        if (batched) {
+            GemmInput in;
+            rc = gemm_prepare(dx, W.cols, batch, W.cols, mode == 2 ? dn : nullptr, m->cfg.eps, W.type, 0, m->ws.gemm,
+                              &in, st);
+            if (rc == LLMDOT_OK) rc = launch_gemm(W, in, dy, W.rows, GEMV_STORE, m->ws.gemm, m->ws.err, st);
+        } else if (mode == 1 || !m->use_fast_gemv || !gemv_fast_supported(W, batch)) {
+            if (mode == 2) rc = fail(LLMDOT_E_UNSUPPORTED, "model_matvec: fused norm needs the tensor-core path");
+            else rc = launch_gemv_ref(W.raw, W.type, W.rows, W.cols, dx, W.cols, batch, dy, W.rows, false, st);
+        } else {
             rc = launch_gemv_fast_ex(W, nullptr, mode == 2 ? dn : nullptr, m->cfg.eps, dx, W.cols, batch, dy, W.rows,
                                      GEMV_STORE, st);
+        }
     }
     if (rc == LLMDOT_OK && cudaMemcpyAsync(y, dy, sizeof(float) * ny, cudaMemcpyDeviceToHost, st) != cudaSuccess)
         rc = cuda_fail(cudaGetLastError(), "model_matvec download");

@@ -254,6 +254,11 @@ int ensure_workspace(llmdot_model *m, int batch)
     LLMDOT_CUDA_TRY(cudaMemset(w.counters, 0, sizeof(int) * B * c.heads_kv));
     LLMDOT_CUDA_TRY(cudaMemset(w.err, 0, sizeof(int)));
     LLMDOT_CUDA_TRY(cudaMemset(w.hist_step, 0, sizeof(int32_t)));
+    if (batch >= GEMM_MIN_ROWS) {
+        const int cols_max = std::max(std::max(c.hidden, (int)qDim), c.ffn);
+        const int rows_max = std::max(std::max(c.hidden, (int)(qDim + 2 * kvDim)), c.ffn);
+        LLMDOT_TRY(gemm_scratch_alloc(w.gemm, cols_max, rows_max, a));
+    }
     w.batch = batch;
     return LLMDOT_OK;
 }
@@ -287,10 +292,23 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
 
     // y = epilogue(W . [rmsnorm](x)); the tensor-core kernel fuses the norm and the epilogue,
     // the generic kernel runs them as separate launches.
+    const bool batched = fast && batch >= GEMM_MIN_ROWS && batch <= GEMM_MAX_ROWS && w.gemm.xf[0] != nullptr;
     auto mv = [&](const DevMat &W, const DevMat *W1, const float *x, int ldx, const float *norm_w, float *y, int ldy,
                   int mode) -> int {
         if (fast && gemv_fast_supported(W, batch) && (!W1 || gemv_fast_supported(*W1, batch)))
             return launch_gemv_fast_ex(W, W1, norm_w, c.eps, x, ldx, batch, y, ldy, mode, st, pdl);
+        if (batched && gemm_supported(W, batch) && (!W1 || gemm_supported(*W1, batch))) {
+            GemmInput in, in1;
+            LLMDOT_TRY(gemm_prepare(x, ldx, batch, W.cols, norm_w, c.eps, W.type, 0, w.gemm, &in, st));
+            if (mode == GEMV_SILU_MUL || mode == GEMV_GELU_MUL) {
+                LLMDOT_TRY(launch_gemm(W, in, w.gate, c.ffn, GEMV_STORE, w.gemm, w.err, st));
+                if (W1->type != W.type)
+                    LLMDOT_TRY(gemm_prepare(x, ldx, batch, W1->cols, norm_w, c.eps, W1->type, 1, w.gemm, &in1, st));
+                LLMDOT_TRY(launch_gemm(*W1, W1->type != W.type ? in1 : in, w.up, c.ffn, GEMV_STORE, w.gemm, w.err, st));
+                return launch_act_mul(mode == GEMV_GELU_MUL, w.gate, w.up, y, c.ffn, batch, st);
+            }
+            return launch_gemm(W, in, y, ldy, mode == GEMV_ADD ? GEMV_ADD : GEMV_STORE, w.gemm, w.err, st);
+        }
         const float *xin = x;
         int ld = ldx;
         if (norm_w) {
@@ -328,6 +346,25 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
                                           {&L.v, nullptr, w.v, kvDim}};
                 qkv_rc = launch_gemv_multi(tg, 3, L.attn_norm, c.eps, w.h, H, batch, GEMV_STORE, pdl, st);
                 if (qkv_rc != LLMDOT_OK && qkv_rc != LLMDOT_E_UNSUPPORTED) return qkv_rc;
+            }
+            if (qkv_rc != LLMDOT_OK && batched && gemm_supported(L.q, batch) && gemm_supported(L.k, batch) &&
+                gemm_supported(L.v, batch)) {
+                // batched: the fragments of the normed input are built once per tile layout
+                GemmInput in[2];
+                bool have[2] = {false, false};
+                const DevMat *mats[3] = {&L.q, &L.k, &L.v};
+                float *ys[3] = {w.q, w.k, w.v};
+                const int lds[3] = {qDim, kvDim, kvDim};
+                for (int i = 0; i < 3; i++) {
+                    const int lay = mats[i]->type == T_Q4_K ? 0 : 1;
+                    if (!have[lay]) {
+                        LLMDOT_TRY(gemm_prepare(w.h, H, batch, H, L.attn_norm, c.eps, mats[i]->type, lay, w.gemm,
+                                                &in[lay], st));
+                        have[lay] = true;
+                    }
+                    LLMDOT_TRY(launch_gemm(*mats[i], in[lay], ys[i], lds[i], GEMV_STORE, w.gemm, w.err, st));
+                }
+                qkv_rc = LLMDOT_OK;
             }
             if (qkv_rc != LLMDOT_OK) {
                 // mixed Q4_K/Q6_K segments whose shared-memory layout does not fit one launch

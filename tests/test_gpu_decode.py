@@ -146,3 +146,26 @@ def test_model_load_rejects_garbage(gpu, tmp_path):
     p.write_bytes(b"GGUF" + b"\xff" * 100)
     with pytest.raises(CudaBackendError):
         CudaModel.load(str(p))
+
+
+@pytest.mark.parametrize("B", [6, 20])
+def test_large_batch_decode_matches_single(gpu, B):
+    """5..32 sessions per step run the batched matmul; logits agree with one-session steps."""
+    name = "tiny"
+    cfg = synth.get(name)
+    m = model(name)
+    prompts = [synth.prompt_tokens(cfg, 4 + 3 * i, session=i) for i in range(B)]
+    sessions = [m.session(kv="f32") for _ in prompts]
+    cur = [s.prefill(p)[0] for s, p in zip(sessions, prompts)]
+    singles = [m.session(kv="f32") for _ in prompts]
+    for s, p in zip(singles, prompts):
+        s.prefill(p)
+    for _ in range(3):
+        nxt, lg = decode_batch(sessions, cur, want_logits=True)
+        for i, s in enumerate(singles):
+            n1, l1 = s.decode(int(cur[i]), want_logits=True)
+            assert np.abs(lg[i] - l1).max() < 1e-3
+            top2 = np.sort(l1)[-2:]
+            if top2[1] - top2[0] > 1e-3:
+                assert int(nxt[i]) == int(n1)
+        cur = [int(t) for t in nxt]

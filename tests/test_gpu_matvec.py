@@ -50,6 +50,46 @@ def test_matvec_every_weight(oracle, name, nv):
             assert np.all(err <= bound(x[v:v + 1], deq)[0]), f"{tname} v={v}: max err {err.max()}"
 
 
+@pytest.mark.parametrize("name", ["micro", "micro-phi3", "tiny"])
+@pytest.mark.parametrize("nv", [5, 8, 13, 32])
+def test_matmul_batched_every_weight(oracle, name, nv):
+    """5..32 input rows: the batched tensor-core kernel (gemm.cu) on every Q4_K / Q6_K matrix."""
+    m, f = loaded(name)
+    rng = np.random.default_rng(100 + nv)
+    for tname, info in f.tensors.items():
+        if len(info.dims) != 2 or info.ggml_type not in (gguf.GGML_Q4_K, gguf.GGML_Q6_K):
+            continue
+        cols, rows = info.dims
+        raw = np.array(f.tensor_bytes(tname))
+        x = rng.standard_normal((nv, cols)).astype(np.float32)
+        x[nv - 1] *= 1e-3  # rows of very different scale in one batch
+        y = m.matvec(tname, x, rows, mode=0)
+        deq = oracle.dequantize(raw, info.ggml_type, rows, cols).reshape(rows, cols)
+        for v in range(nv):
+            ref = oracle.matmul(x[v], raw, info.ggml_type, cols, rows)
+            err = np.abs(y[v] - ref)
+            assert np.all(err <= bound(x[v:v + 1], deq)[0]), f"{tname} v={v}: max err {err.max()}"
+
+
+def test_matmul_batched_fused_rmsnorm(oracle):
+    name = "tiny"
+    m, f = loaded(name)
+    cfg = synth.get(name)
+    rng = np.random.default_rng(6)
+    wn = (1 + 0.01 * rng.standard_normal(cfg.hidden)).astype(np.float32)
+    for tname in ("blk.0.attn_v.weight", "blk.1.ffn_up.weight", "output.weight"):
+        info = f.tensors[tname]
+        cols, rows = info.dims
+        raw = np.array(f.tensor_bytes(tname))
+        h = (rng.standard_normal((7, cols)) * 3).astype(np.float32)
+        y = m.matvec(tname, h, rows, mode=2, norm_w=wn)
+        deq = oracle.dequantize(raw, info.ggml_type, rows, cols).reshape(rows, cols)
+        for v in range(7):
+            xn = oracle.rmsnorm(h[v], wn, cfg.eps)
+            ref = oracle.matmul(xn, raw, info.ggml_type, cols, rows)
+            assert np.all(np.abs(y[v] - ref) <= bound(xn[None], deq)[0] + 1e-6)
+
+
 @pytest.mark.parametrize("name", ["micro", "tiny"])
 def test_matvec_fused_rmsnorm(oracle, name):
     m, f = loaded(name)
