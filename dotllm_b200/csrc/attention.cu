@@ -57,7 +57,8 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const float *__restric
                                                           const int32_t *__restrict__ pos,
                                                           const float *__restrict__ cos_t, const float *__restrict__ sin_t,
                                                           const KvView *__restrict__ views, int layer, AttnShape sh,
-                                                          float *__restrict__ scores, float *__restrict__ part_m)
+                                                          float *__restrict__ scores, float *__restrict__ part_m,
+                                                          int appended)
 {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -80,11 +81,13 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const float *__restric
     T *kg = (T *)vw.k + (size_t)layer * vw.layer_stride + head_off;
     T *vg = (T *)vw.v + (size_t)layer * vw.layer_stride + head_off;
     const int jlo = max(start - s0, 0), jhi = min(seq_len - s0, KV_PAGE);
-    const bool has_new = p >= s0 && p < s0 + KV_PAGE;
-    // earlier positions of the page are constant: stage them before the dependency wait
-    stage_page<T>(ks, kg, hd, stride, jlo, has_new ? p - s0 : jhi);
+    const bool has_new = !appended && p >= s0 && p < s0 + KV_PAGE;
+    // earlier positions of the page are constant: stage them before the dependency wait (with
+    // `appended`, the previous kernel wrote positions of this step: stage after the wait)
+    if (!appended) stage_page<T>(ks, kg, hd, stride, jlo, has_new ? p - s0 : jhi);
     pdl_launch();
     pdl_wait();
+    if (appended) stage_page<T>(ks, kg, hd, stride, jlo, jhi);
     const float *cs = cos_t + (size_t)p * half, *sn = sin_t + (size_t)p * half;
     // RoPE of the G query heads (TensorOps.ApplyRoPE, half-split pairs)
     for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
@@ -139,7 +142,7 @@ __global__ void __launch_bounds__(256) attn_pv_kernel(const int32_t *__restrict_
                                                       int layer, AttnShape sh, const float *__restrict__ scores,
                                                       const float *__restrict__ part_m, float *__restrict__ part_s,
                                                       float *__restrict__ part_o, int *__restrict__ counters,
-                                                      float *__restrict__ out, int ldo)
+                                                      float *__restrict__ out, int ldo, int appended)
 {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     __shared__ int last;
@@ -161,10 +164,11 @@ __global__ void __launch_bounds__(256) attn_pv_kernel(const int32_t *__restrict_
     const T *vg = (const T *)vw.v + (size_t)layer * vw.layer_stride + ((size_t)page * sh.heads_kv + kvh) * KV_PAGE * hd;
     const int jlo = max(start - s0, 0), jhi = min(seq_len - s0, KV_PAGE);
     const bool has_new = p >= s0 && p < s0 + KV_PAGE;
-    stage_page<T>(vs, vg, hd, hd, jlo, has_new ? p - s0 : jhi);
+    if (!appended) stage_page<T>(vs, vg, hd, hd, jlo, has_new ? p - s0 : jhi);
     pdl_launch();
     pdl_wait();
-    if (has_new) stage_page<T>(vs, vg, hd, hd, p - s0, p - s0 + 1);  // appended by kernel 1
+    if (appended) stage_page<T>(vs, vg, hd, hd, jlo, jhi);
+    else if (has_new) stage_page<T>(vs, vg, hd, hd, p - s0, p - s0 + 1);  // appended by kernel 1
     const int len = seq_len - start, nvec = len - len % 8;
     const int c0 = start / KV_PAGE, c1 = (seq_len - 1) / KV_PAGE;
     for (int hg = threadIdx.x; hg < G; hg += blockDim.x) {
@@ -219,6 +223,34 @@ __global__ void __launch_bounds__(256) attn_pv_kernel(const int32_t *__restrict_
     if (threadIdx.x == 0) *cnt = 0;  // ready for the next layer / step
 }
 
+// RoPE of the new keys and the K/V append of every row, ahead of the attention kernels: used
+// when several rows of one step belong to the same session (a prompt chunk), so that row i
+// sees the keys of rows < i (InferenceEngine.cs:375-382).
+template <typename T>
+__global__ void append_kv_kernel(const float *__restrict__ k, const float *__restrict__ v, int ldkv,
+                                 const int32_t *__restrict__ pos, const float *__restrict__ cos_t,
+                                 const float *__restrict__ sin_t, const KvView *__restrict__ views, int layer,
+                                 AttnShape sh)
+{
+    pdl_launch();
+    pdl_wait();
+    const int kvh = blockIdx.x, b = blockIdx.y, hd = sh.head_dim, half = sh.rope_half;
+    const int p = pos[b];
+    const KvView vw = views[b];
+    const int page = vw.pages[p / KV_PAGE], slot = p % KV_PAGE;
+    const size_t off = (size_t)layer * vw.layer_stride + (((size_t)page * sh.heads_kv + kvh) * KV_PAGE + slot) * hd;
+    const float *kx = k + (size_t)b * ldkv + (size_t)kvh * hd, *vx = v + (size_t)b * ldkv + (size_t)kvh * hd;
+    const float *cs = cos_t + (size_t)p * half, *sn = sin_t + (size_t)p * half;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float r;
+        if (d < half) r = __fsub_rn(__fmul_rn(kx[d], cs[d]), __fmul_rn(kx[d + half], sn[d]));
+        else if (d < 2 * half) r = __fadd_rn(__fmul_rn(kx[d - half], sn[d - half]), __fmul_rn(kx[d], cs[d - half]));
+        else r = kx[d];
+        ((T *)vw.k)[off + d] = KvT<T>::st(r);
+        ((T *)vw.v)[off + d] = KvT<T>::st(vx[d]);
+    }
+}
+
 static size_t scores_smem(const AttnShape &sh, size_t esz)
 {
     const int G = sh.heads / sh.heads_kv;
@@ -234,10 +266,14 @@ template <typename T>
 static int launch_attn_t(const float *q, int ldq, const float *k, const float *v, int ldkv, const int32_t *pos,
                          const float *cos_t, const float *sin_t, const KvView *views, int layer, const AttnShape &sh,
                          int batch, float *scores, float *part_m, float *part_s, float *part_o, int *counters,
-                         float *out, int ldo, bool pdl, cudaStream_t st)
+                         float *out, int ldo, bool append_first, bool pdl, cudaStream_t st)
 {
     const int nchunk = sh.max_ctx / KV_PAGE;
     dim3 grid(nchunk, sh.heads_kv, batch);
+    if (append_first)
+        LLMDOT_CUDA_TRY(launch_kernel(pdl, append_kv_kernel<T>, dim3(sh.heads_kv, batch), dim3(128), 0, st, k, v, ldkv,
+                                      pos, cos_t, sin_t, views, layer, sh));
+    const int appended = append_first ? 1 : 0;
     static bool attr_set = false;
     if (!attr_set) {
         LLMDOT_CUDA_TRY(cudaFuncSetAttribute(attn_scores_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
@@ -245,24 +281,25 @@ static int launch_attn_t(const float *q, int ldq, const float *k, const float *v
         attr_set = true;
     }
     LLMDOT_CUDA_TRY(launch_kernel(pdl, attn_scores_kernel<T>, grid, dim3(256), scores_smem(sh, sizeof(T)), st, q, ldq, k,
-                                  v, ldkv, pos, cos_t, sin_t, views, layer, sh, scores, part_m));
+                                  v, ldkv, pos, cos_t, sin_t, views, layer, sh, scores, part_m, appended));
     LLMDOT_CUDA_TRY(launch_kernel(pdl, attn_pv_kernel<T>, grid, dim3(256), pv_smem(sh, sizeof(T)), st, pos, views, layer,
-                                  sh, (const float *)scores, (const float *)part_m, part_s, part_o, counters, out, ldo));
+                                  sh, (const float *)scores, (const float *)part_m, part_s, part_o, counters, out, ldo,
+                                  appended));
     return LLMDOT_OK;
 }
 
 int launch_attention_step(const float *q, int ldq, const float *k, const float *v, int ldkv, const int32_t *pos,
                           const float *cos_t, const float *sin_t, const KvView *views, int layer, int kv_type,
                           const AttnShape &sh, int batch, float *scores, float *part_m, float *part_s, float *part_o,
-                          int *counters, float *out, int ldo, bool pdl, cudaStream_t st)
+                          int *counters, float *out, int ldo, bool append_first, bool pdl, cudaStream_t st)
 {
     if (scores_smem(sh, 4) > 200 * 1024 || pv_smem(sh, 4) > 200 * 1024)
         return fail(LLMDOT_E_UNSUPPORTED, "attention: head too large for the page staging");
     if (kv_type == LLMDOT_KV_F16)
         return launch_attn_t<__half>(q, ldq, k, v, ldkv, pos, cos_t, sin_t, views, layer, sh, batch, scores, part_m,
-                                     part_s, part_o, counters, out, ldo, pdl, st);
+                                     part_s, part_o, counters, out, ldo, append_first, pdl, st);
     return launch_attn_t<float>(q, ldq, k, v, ldkv, pos, cos_t, sin_t, views, layer, sh, batch, scores, part_m, part_s,
-                                part_o, counters, out, ldo, pdl, st);
+                                part_o, counters, out, ldo, append_first, pdl, st);
 }
 
 }  // namespace llmdot

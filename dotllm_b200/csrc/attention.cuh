@@ -26,10 +26,11 @@ struct AttnShape {
 // k and v at pos[b], softmax(q K^T / sqrt(hd), softcap) V over the window, written to
 // out[b][h*hd + d].  q/k/v are the raw projections.  Scratch: scores [batch][heads][max_ctx],
 // part_m/part_s [batch][heads][max_ctx/KV_PAGE], part_o [..][head_dim], counters
-// [batch][heads_kv] (zero on entry, left zero).
+// [batch][heads_kv] (zero on entry, left zero).  append_first: append every row's k/v in a
+// separate kernel before the attention, for rows of one session in one step (prompt chunks).
 int launch_attention_step(const float *q, int ldq, const float *k, const float *v, int ldkv, const int32_t *pos,
                           const float *cos_t, const float *sin_t, const KvView *views, int layer, int kv_type,
                           const AttnShape &sh, int batch, float *scores, float *part_m, float *part_s, float *part_o,
-                          int *counters, float *out, int ldo, bool pdl, cudaStream_t st);
+                          int *counters, float *out, int ldo, bool append_first, bool pdl, cudaStream_t st);
 
 }  // namespace llmdot

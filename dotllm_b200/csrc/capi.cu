@@ -11,6 +11,7 @@
 #include "engine.cuh"
 #include "gemv.cuh"
 #include "gguf_loader.h"
+#include "tp.cuh"
 #include "ops.cuh"
 
 namespace llmdot {
@@ -572,10 +573,52 @@ extern "C" int llmdot_cuda_model_load_gguf(int device, const char *path, llmdot_
     return rc;
 }
 
+extern "C" int llmdot_cuda_model_load_gguf_tp(int device, const char *path, int tp_size, int tp_rank,
+                                              llmdot_model **out)
+{
+    if (!out || !path) return fail(LLMDOT_E_INVALID, "null argument");
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(LLMDOT_E_CUDA, "no CUDA device available");
+    }
+    if (device < 0 || device >= n) return fail(LLMDOT_E_INVALID, "device index out of range");
+    GgufModelFile f;
+    LLMDOT_TRY(gguf_open(path, &f));
+    std::vector<llmdot_tensor_desc> descs;
+    gguf_descs(f, &descs);
+    int rc = model_upload(device, &f.cfg, descs.data(), (int)descs.size(), out, tp_size, tp_rank);
+    gguf_close(&f);
+    return rc;
+}
+
+extern "C" int llmdot_cuda_tp_shard(const llmdot_config *cfg, int tp_size, int tp_rank, int32_t *out8)
+{
+    if (!cfg || !out8) return fail(LLMDOT_E_INVALID, "null argument");
+    TpShard sh{};
+    LLMDOT_TRY(tp_shard(*cfg, tp_size, tp_rank, &sh));
+    const int32_t v[8] = {sh.q_lo, sh.q_n, sh.kv_lo, sh.kv_n, sh.f_lo, sh.f_n, sh.v_lo, sh.v_n};
+    memcpy(out8, v, sizeof(v));
+    return LLMDOT_OK;
+}
+
+extern "C" int llmdot_cuda_tp_unique_id(uint8_t *out128)
+{
+    if (!out128) return fail(LLMDOT_E_INVALID, "null argument");
+    return tp_unique_id(out128);
+}
+
+extern "C" int llmdot_cuda_tp_init(llmdot_model *m, const uint8_t *id128)
+{
+    if (!m || !id128) return fail(LLMDOT_E_INVALID, "null argument");
+    if (m->tp < 2) return fail(LLMDOT_E_INVALID, "tp_init: the model was loaded without tensor parallelism");
+    return tp_comm_init(m, id128);
+}
+
 extern "C" int llmdot_cuda_model_config(const llmdot_model *m, llmdot_config *out)
 {
     if (!m || !out) return fail(LLMDOT_E_INVALID, "null argument");
-    *out = m->cfg;
+    *out = m->full_cfg;
     return LLMDOT_OK;
 }
 
@@ -652,6 +695,46 @@ extern "C" int llmdot_cuda_session_free(llmdot_session *s)
     return LLMDOT_OK;
 }
 
+// logits[v][r * rows + j] = gathered[r][v][j]
+__global__ void logits_unshard_kernel(const float *__restrict__ g, float *__restrict__ full, int tp, int batch, int rows,
+                                      int vocab)
+{
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)tp * batch * rows) return;
+    const int j = (int)(i % rows), v = (int)((i / rows) % batch), r = (int)(i / ((size_t)rows * batch));
+    full[(size_t)v * vocab + (size_t)r * rows + j] = g[i];
+}
+
+// Copies row `row` (or all `batch` rows when row < 0) of the step's logits to host memory; under
+// tensor parallelism the vocabulary shards are gathered from every rank first (even split only).
+static int read_logits(llmdot_model *m, int batch, int row, float *host, cudaStream_t st)
+{
+    const int V = m->cfg.vocab;
+    const size_t count = (size_t)V * (row < 0 ? batch : 1);
+    if (m->tp > 1) {
+        if (V % m->tp) return fail(LLMDOT_E_UNSUPPORTED, "logits read-back under TP needs vocab % tp == 0");
+        const size_t per = (size_t)batch * m->head_rows;
+        float *g = nullptr;
+        LLMDOT_CUDA_TRY(cudaMallocAsync(&g, sizeof(float) * (per * m->tp + (size_t)batch * V), st));
+        float *full = g + per * m->tp;
+        int rc = tp_allgather(m, m->ws.logits, g, per, st);
+        if (rc == LLMDOT_OK) {
+            const size_t n = per * m->tp;
+            logits_unshard_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, full, m->tp, batch, m->head_rows, V);
+            if (cudaGetLastError() != cudaSuccess) rc = fail(LLMDOT_E_CUDA, "logits unshard launch");
+        }
+        if (rc == LLMDOT_OK && cudaMemcpyAsync(host, full + (row < 0 ? 0 : (size_t)row * V), sizeof(float) * count,
+                                               cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            rc = cuda_fail(cudaGetLastError(), "logits copy");
+        cudaStreamSynchronize(st);
+        cudaFreeAsync(g, st);
+        return rc;
+    }
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(host, m->ws.logits + (row < 0 ? 0 : (size_t)row * V), sizeof(float) * count,
+                                    cudaMemcpyDeviceToHost, st));
+    return LLMDOT_OK;
+}
+
 static int check_err_flag(llmdot_model *m)
 {
     int e = 0;
@@ -680,7 +763,9 @@ extern "C" int llmdot_cuda_prefill(llmdot_session *s, const int32_t *tokens, int
     LLMDOT_TRY(ensure_workspace(m, 1));
     Workspace &w = m->ws;
     cudaStream_t st = m->stream;
-    // token-by-token, like the reference's prefill loop (InferenceEngine.cs:84-88)
+    // The reference feeds the prompt token by token (InferenceEngine.cs:84-88); here runs of up
+    // to 32 consecutive tokens go through each layer together (same arithmetic per token, the
+    // K/V of a chunk appended before its attention so every token still sees only its prefix)
     int32_t *dtok = nullptr, *dpos = nullptr;
     LLMDOT_CUDA_TRY(cudaMallocAsync(&dtok, sizeof(int32_t) * 2 * n, st));
     dpos = dtok + n;
@@ -690,21 +775,39 @@ extern "C" int llmdot_cuda_prefill(llmdot_session *s, const int32_t *tokens, int
         hp[n + i] = s->pos + i;
     }
     cudaMemcpyAsync(dtok, hp.data(), sizeof(int32_t) * 2 * n, cudaMemcpyHostToDevice, st);
-    cudaMemcpyAsync(w.views, &s->view, sizeof(KvView), cudaMemcpyHostToDevice, st);
     int rc = LLMDOT_OK;
-    if (step_kernel_supported(m, 1)) {
+    int last_row = 0;  // row of the workspace that holds the last prompt token's logits
+    if (m->use_fast_gemv && !m->step_decode) {
+        // prompt chunks of up to GEMM_MAX_ROWS consecutive positions, one batched step each
+        const int CH = n < GEMM_MAX_ROWS ? n : GEMM_MAX_ROWS;
+        rc = ensure_workspace(m, CH);
+        if (rc == LLMDOT_OK) {
+            std::vector<KvView> vs(CH, s->view);
+            if (cudaMemcpyAsync(w.views, vs.data(), sizeof(KvView) * CH, cudaMemcpyHostToDevice, st) != cudaSuccess)
+                rc = cuda_fail(cudaGetLastError(), "prefill views");
+            for (int c0 = 0; c0 < n && rc == LLMDOT_OK; c0 += CH) {
+                const int T = n - c0 < CH ? n - c0 : CH;
+                const bool last = c0 + T == n;
+                rc = forward_step(m, T, s->kv_type, dtok + c0, dpos + c0, w.views, w.next, st,
+                                  STEP_CHUNK | (last ? 0 : STEP_NO_HEAD));
+                last_row = T - 1;
+            }
+        }
+    } else if (step_kernel_supported(m, 1)) {
         // all prompt tokens in one persistent launch; logits of the last one only
+        cudaMemcpyAsync(w.views, &s->view, sizeof(KvView), cudaMemcpyHostToDevice, st);
         cudaMemcpyAsync(w.pos, dpos, sizeof(int32_t), cudaMemcpyDeviceToDevice, st);
         rc = launch_step_kernel(m, 1, s->kv_type, n, dtok, st);
     } else {
+        cudaMemcpyAsync(w.views, &s->view, sizeof(KvView), cudaMemcpyHostToDevice, st);
         for (int i = 0; i < n && rc == LLMDOT_OK; i++)
             rc = forward_step(m, 1, s->kv_type, dtok + i, dpos + i, w.views, w.next, st);
     }
     cudaFreeAsync(dtok, st);
     if (rc != LLMDOT_OK) return rc;
-    if (logits) LLMDOT_CUDA_TRY(cudaMemcpyAsync(logits, w.logits, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, st));
+    if (logits) LLMDOT_TRY(read_logits(m, last_row + 1, last_row, logits, st));
     int32_t nt = 0;
-    LLMDOT_CUDA_TRY(cudaMemcpyAsync(&nt, w.next, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(&nt, w.next + last_row, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
     LLMDOT_CUDA_TRY(cudaStreamSynchronize(st));
     LLMDOT_TRY(check_err_flag(m));
     s->pos += n;
@@ -748,9 +851,7 @@ extern "C" int llmdot_cuda_decode(llmdot_session **sessions, int batch, const in
     if (persistent) LLMDOT_TRY(launch_step_kernel(m, batch, kv_type, 1, nullptr, st));
     else LLMDOT_CUDA_TRY(cudaGraphLaunch(g, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(x.h_pinned + 2 * x.cap, w.next, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost, st));
-    if (logits)
-        LLMDOT_CUDA_TRY(cudaMemcpyAsync(logits, w.logits, sizeof(float) * (size_t)batch * m->cfg.vocab,
-                                        cudaMemcpyDeviceToHost, st));
+    if (logits) LLMDOT_TRY(read_logits(m, batch, -1, logits, st));
     LLMDOT_CUDA_TRY(cudaStreamSynchronize(st));
     LLMDOT_TRY(check_err_flag(m));
     for (int i = 0; i < batch; i++) {

@@ -10,6 +10,7 @@
 #include "engine.cuh"
 #include "gemv.cuh"
 #include "ops.cuh"
+#include "tp.cuh"
 
 namespace llmdot {
 
@@ -37,29 +38,62 @@ static const llmdot_tensor_desc *find_desc(const llmdot_tensor_desc *t, int n, c
     return nullptr;
 }
 
-static int upload_mat(llmdot_model *m, const llmdot_tensor_desc *d, DevMat &out, int expect_cols, int expect_rows)
+// A run of `n` consecutive rows of a weight starting at row `lo`.
+struct RowRange {
+    int lo, n;
+};
+
+// Uploads the rows `ranges` (concatenated, in order) and the columns [col_lo, col_lo + col_n) of a
+// weight (col_n <= 0: all columns).  Without tensor parallelism that is the whole matrix.
+static int upload_mat(llmdot_model *m, const llmdot_tensor_desc *d, DevMat &out, int expect_cols, int expect_rows,
+                      std::vector<RowRange> ranges = {}, int col_lo = 0, int col_n = 0)
 {
     if (!d) return LLMDOT_OK;
     m->by_name[d->name] = &out;
     if (d->n_dims < 2) return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": expected a 2-D weight");
     out.type = d->type;
-    out.cols = (int)d->dims[0];
-    out.rows = (int)d->dims[1];
+    const int full_cols = (int)d->dims[0], full_rows = (int)d->dims[1];
     if (block_elems(out.type) == 0 || out.type == T_F16 || out.type == T_BF16)
         return fail(LLMDOT_E_UNSUPPORTED, std::string(d->name) + ": weight type " + std::to_string(out.type) +
                                               " is not supported by the device matvec");
-    if ((expect_cols > 0 && out.cols != expect_cols) || (expect_rows > 0 && out.rows != expect_rows))
-        return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": unexpected shape " + std::to_string(out.cols) + "x" +
-                                         std::to_string(out.rows));
-    if (out.cols % (int)block_elems(out.type) != 0)
-        return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": columns not a multiple of the block size");
+    if ((expect_cols > 0 && full_cols != expect_cols) || (expect_rows > 0 && full_rows != expect_rows))
+        return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": unexpected shape " + std::to_string(full_cols) + "x" +
+                                         std::to_string(full_rows));
+    const int be = (int)block_elems(out.type);
+    if (full_cols % be != 0) return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": columns not a multiple of the block size");
+    if (ranges.empty()) ranges.push_back({0, full_rows});
+    if (col_n <= 0) {
+        col_lo = 0;
+        col_n = full_cols;
+    }
+    if (col_lo % be || col_n % be || col_lo + col_n > full_cols)
+        return fail(LLMDOT_E_UNSUPPORTED, std::string(d->name) + ": column shard not on block boundaries");
+    out.cols = col_n;
+    out.rows = 0;
+    for (const RowRange &r : ranges) {
+        if (r.lo < 0 || r.n < 0 || r.lo + r.n > full_rows) return fail(LLMDOT_E_INVALID, "row shard out of range");
+        out.rows += r.n;
+    }
+    const uint64_t full_rb = row_bytes(out.type, (uint64_t)full_cols), col_off = row_bytes(out.type, (uint64_t)col_lo);
     out.rbytes = row_bytes(out.type, (uint64_t)out.cols);
-    uint64_t nb = out.rbytes * (uint64_t)out.rows;
-    if (!d->data || d->n_bytes < nb) return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": data too short");
+    const uint64_t nb = out.rbytes * (uint64_t)out.rows;
+    if (!d->data || d->n_bytes < full_rb * (uint64_t)full_rows)
+        return fail(LLMDOT_E_FORMAT, std::string(d->name) + ": data too short");
     // 256 zeroed bytes of slack: the Q3_K decoder reads one byte past each block
     LLMDOT_TRY(dmalloc(m->allocs, (void **)&out.raw, nb + 256));
     LLMDOT_CUDA_TRY(cudaMemsetAsync(out.raw + nb, 0, 256, m->stream));
-    LLMDOT_CUDA_TRY(cudaMemcpyAsync(out.raw, d->data, nb, cudaMemcpyHostToDevice, m->stream));
+    uint64_t dst_row = 0;
+    for (const RowRange &r : ranges) {
+        if (r.n == 0) continue;
+        const uint8_t *src = (const uint8_t *)d->data + (uint64_t)r.lo * full_rb + col_off;
+        if (out.rbytes == full_rb)
+            LLMDOT_CUDA_TRY(cudaMemcpyAsync(out.raw + dst_row * out.rbytes, src, out.rbytes * r.n,
+                                            cudaMemcpyHostToDevice, m->stream));
+        else
+            LLMDOT_CUDA_TRY(cudaMemcpy2DAsync(out.raw + dst_row * out.rbytes, out.rbytes, src, full_rb, out.rbytes, r.n,
+                                              cudaMemcpyHostToDevice, m->stream));
+        dst_row += r.n;
+    }
     LLMDOT_TRY(prepare_tiled(m, out));
     return LLMDOT_OK;
 }
@@ -88,7 +122,8 @@ static int upload_vec(llmdot_model *m, const llmdot_tensor_desc *d, float **out,
     return rc;
 }
 
-int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc *t, int n, llmdot_model **out)
+int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc *t, int n, llmdot_model **out, int tp,
+                 int tp_rank)
 {
     *out = nullptr;
     if (!cfg || !t || n <= 0) return fail(LLMDOT_E_INVALID, "model_load: null config or tensors");
@@ -105,10 +140,22 @@ int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc 
     if (rd > c.head_dim || rd % 2) return fail(LLMDOT_E_FORMAT, "model_load: bad rope dimension");
     if (c.head_dim % 8 != 0) return fail(LLMDOT_E_UNSUPPORTED, "model_load: head_dim must be a multiple of 8");
 
+    TpShard sh{};
+    LLMDOT_TRY(tp_shard(c, tp, tp_rank, &sh));
     LLMDOT_CUDA_TRY(cudaSetDevice(device));
     llmdot_model *m = new llmdot_model();
     m->device = device;
+    m->full_cfg = c;
     m->cfg = c;
+    m->tp = tp;
+    m->tp_rank = tp_rank;
+    m->head_lo = sh.v_lo;
+    m->head_rows = sh.v_n;
+    if (tp > 1) {  // this rank's local shapes drive every kernel; the vocabulary stays global
+        m->cfg.heads /= tp;
+        m->cfg.heads_kv /= tp;
+        m->cfg.ffn /= tp;
+    }
     // LLMDOT_REFERENCE_MATVEC=1 selects the generic (per-element) matvec everywhere; the tests
     // use it to check the tensor-core path against the straightforward one.
     m->use_fast_gemv = getenv("LLMDOT_REFERENCE_MATVEC") == nullptr;
@@ -125,6 +172,7 @@ int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc 
         return bail(fail(LLMDOT_E_CUDA, "stream create failed"));
 
     const int qDim = c.heads * c.head_dim, kvDim = c.heads_kv * c.head_dim, H = c.hidden;
+    const bool tps = tp > 1;
     auto D = [&](const std::string &s) { return find_desc(t, n, s); };
     const llmdot_tensor_desc *emb = D("token_embd.weight");
     if (!emb) return bail(fail(LLMDOT_E_FORMAT, "token_embd.weight missing"));
@@ -132,7 +180,15 @@ int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc 
     const llmdot_tensor_desc *outw = nullptr;
     for (int i = 0; i < n; i++)
         if (t[i].name && strcmp(t[i].name, "output.weight") == 0) outw = &t[i];
-    if (outw && (rc = upload_mat(m, outw, m->out, H, c.vocab))) return bail(rc);
+    if (tps) {
+        // the logits head holds this rank's vocabulary rows (tied models: a shard of the embedding,
+        // which itself stays whole for the lookup)
+        if ((rc = upload_mat(m, outw ? outw : emb, m->out, H, c.vocab, {{sh.v_lo, sh.v_n}}))) return bail(rc);
+        m->by_name["output.weight"] = &m->out;
+        m->by_name[emb->name] = &m->emb;
+    } else if (outw && (rc = upload_mat(m, outw, m->out, H, c.vocab))) {
+        return bail(rc);
+    }
     const llmdot_tensor_desc *on = D("output_norm.weight");
     if (!on) on = D("token_embd_norm.weight");
     if (!on) return bail(fail(LLMDOT_E_FORMAT, "output_norm.weight missing"));
@@ -151,23 +207,33 @@ int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc 
             if ((rc = upload_vec(m, D(p + "post_attention_norm.weight"), &L.post_attn, H))) return bail(rc);
             if ((rc = upload_vec(m, D(p + "post_ffw_norm.weight"), &L.post_ffw, H))) return bail(rc);
         }
+        // shards (tp > 1): q/k/v and gate/up by output rows, attn_output and ffn_down by input columns
+        const std::vector<RowRange> all;
+        const std::vector<RowRange> qr = tps ? std::vector<RowRange>{{sh.q_lo, sh.q_n}} : all;
+        const std::vector<RowRange> kvr = tps ? std::vector<RowRange>{{sh.kv_lo, sh.kv_n}} : all;
+        const std::vector<RowRange> fr = tps ? std::vector<RowRange>{{sh.f_lo, sh.f_n}} : all;
         if (c.qkv_fused) {
             if (!D(p + "attn_qkv.weight")) return bail(fail(LLMDOT_E_FORMAT, p + "attn_qkv.weight missing"));
-            if ((rc = upload_mat(m, D(p + "attn_qkv.weight"), L.qkv, H, qDim + 2 * kvDim))) return bail(rc);
+            const std::vector<RowRange> qkvr =
+                tps ? std::vector<RowRange>{{sh.q_lo, sh.q_n}, {qDim + sh.kv_lo, sh.kv_n}, {qDim + kvDim + sh.kv_lo, sh.kv_n}}
+                    : all;
+            if ((rc = upload_mat(m, D(p + "attn_qkv.weight"), L.qkv, H, qDim + 2 * kvDim, qkvr))) return bail(rc);
         } else {
             if (!D(p + "attn_q.weight") || !D(p + "attn_k.weight") || !D(p + "attn_v.weight"))
                 return bail(fail(LLMDOT_E_FORMAT, p + "attn_q/k/v missing"));
-            if ((rc = upload_mat(m, D(p + "attn_q.weight"), L.q, H, qDim))) return bail(rc);
-            if ((rc = upload_mat(m, D(p + "attn_k.weight"), L.k, H, kvDim))) return bail(rc);
-            if ((rc = upload_mat(m, D(p + "attn_v.weight"), L.v, H, kvDim))) return bail(rc);
+            if ((rc = upload_mat(m, D(p + "attn_q.weight"), L.q, H, qDim, qr))) return bail(rc);
+            if ((rc = upload_mat(m, D(p + "attn_k.weight"), L.k, H, kvDim, kvr))) return bail(rc);
+            if ((rc = upload_mat(m, D(p + "attn_v.weight"), L.v, H, kvDim, kvr))) return bail(rc);
         }
         if (!D(p + "attn_output.weight") || !D(p + "ffn_gate.weight") || !D(p + "ffn_up.weight") ||
             !D(p + "ffn_down.weight"))
             return bail(fail(LLMDOT_E_FORMAT, p + "attention output / FFN tensors missing"));
-        if ((rc = upload_mat(m, D(p + "attn_output.weight"), L.o, qDim, H))) return bail(rc);
-        if ((rc = upload_mat(m, D(p + "ffn_gate.weight"), L.gate, H, c.ffn))) return bail(rc);
-        if ((rc = upload_mat(m, D(p + "ffn_up.weight"), L.up, H, c.ffn))) return bail(rc);
-        if ((rc = upload_mat(m, D(p + "ffn_down.weight"), L.down, c.ffn, H))) return bail(rc);
+        if ((rc = upload_mat(m, D(p + "attn_output.weight"), L.o, qDim, H, all, tps ? sh.q_lo : 0, tps ? sh.q_n : 0)))
+            return bail(rc);
+        if ((rc = upload_mat(m, D(p + "ffn_gate.weight"), L.gate, H, c.ffn, fr))) return bail(rc);
+        if ((rc = upload_mat(m, D(p + "ffn_up.weight"), L.up, H, c.ffn, fr))) return bail(rc);
+        if ((rc = upload_mat(m, D(p + "ffn_down.weight"), L.down, c.ffn, H, all, tps ? sh.f_lo : 0, tps ? sh.f_n : 0)))
+            return bail(rc);
         for (const DevMat *w : {&L.q, &L.k, &L.v, &L.qkv, &L.o, &L.gate, &L.up, &L.down})
             if (w->valid()) m->layer_bytes += w->bytes();
         m->layer_bytes += (uint64_t)H * 4 * (L.post_attn ? 4 : 2);
@@ -208,6 +274,7 @@ void model_destroy(llmdot_model *m)
     if (!m) return;
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    tp_comm_destroy(m);
     step_cache_free(m);
     for (void *p : m->ws.allocs) cudaFree(p);
     for (void *p : m->allocs) cudaFree(p);
@@ -271,7 +338,7 @@ int gemv(const DevMat &W, const float *x, int ldx, int nv, float *y, int ldy, bo
 
 // ProcessToken (InferenceEngine.cs:134-146) for `batch` independent sessions at once.
 int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens, const int32_t *pos,
-                 const KvView *views, int32_t *next, cudaStream_t st)
+                 const KvView *views, int32_t *next, cudaStream_t st, int flags)
 {
     const llmdot_config &c = m->cfg;
     Workspace &w = m->ws;
@@ -380,24 +447,34 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
         }
         // RoPE of q and k, K/V cache append :362-382, attention :384-442
         LLMDOT_TRY(launch_attention_step(q, ldq, k, v, ldkv, pos, m->cos_t, m->sin_t, views, l, kv_type, sh, batch,
-                                         w.scores, w.part_m, w.part_s, w.part_o, w.counters, w.attn, qDim, pdl, st));
+                                         w.scores, w.part_m, w.part_s, w.part_o, w.counters, w.attn, qDim,
+                                         (flags & STEP_CHUNK) != 0, pdl, st));
         // attn_output matvec + residual add :444-449, :189
-        LLMDOT_TRY(mv(L.o, nullptr, w.attn, qDim, nullptr, w.h, H, GEMV_ADD));
+        // tensor parallel: rank 0 adds its partial onto the residual, the others store theirs, and
+        // the all-reduce leaves h + the sum of the partials on every rank
+        const int res_mode = (m->tp > 1 && m->tp_rank != 0) ? GEMV_STORE : GEMV_ADD;
+        LLMDOT_TRY(mv(L.o, nullptr, w.attn, qDim, nullptr, w.h, H, res_mode));
+        if (m->tp > 1) LLMDOT_TRY(tp_allreduce_sum(m, w.h, (size_t)batch * H, st));
         if (gemma && L.post_attn) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_attn, w.h, H, H, batch, c.eps, st));
         // FfnForward :452-487: ApplyNorm(ffn_norm ?? attn_norm), gate and up, act(gate)*up in one launch
         LLMDOT_TRY(mv(L.gate, &L.up, w.h, H, L.ffn_norm ? L.ffn_norm : L.attn_norm, w.gate, c.ffn,
                       c.ffn_type == 2 ? GEMV_GELU_MUL : GEMV_SILU_MUL));
         // down projection + residual add
-        LLMDOT_TRY(mv(L.down, nullptr, w.gate, c.ffn, nullptr, w.h, H, GEMV_ADD));
+        LLMDOT_TRY(mv(L.down, nullptr, w.gate, c.ffn, nullptr, w.h, H, res_mode));
+        if (m->tp > 1) LLMDOT_TRY(tp_allreduce_sum(m, w.h, (size_t)batch * H, st));
         if (gemma && L.post_ffw) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_ffw, w.h, H, H, batch, c.eps, st));
     }
+    if (flags & STEP_NO_HEAD) return LLMDOT_OK;  // prompt chunk before the last: no logits needed
     // ApplyFinalNorm :575-581 fused into ComputeLogits :583-602
     const DevMat &head = m->out.valid() ? m->out : m->emb;
-    LLMDOT_TRY(mv(head, nullptr, w.h, H, m->out_norm, w.logits, c.vocab, GEMV_STORE));
-    // final softcap + greedy argmax (InferenceEngine.cs:105-108, Sampler.cs:26-27)
-    LLMDOT_TRY(launch_argmax(w.logits, c.vocab, c.vocab, batch, w.keys, next, c.has_final_cap != 0, c.final_cap,
-                             nullptr, st));
-    return LLMDOT_OK;
+    // logits rows [head_lo, head_lo + head_rows): the whole vocabulary without tensor parallelism
+    LLMDOT_TRY(mv(head, nullptr, w.h, H, m->out_norm, w.logits, m->head_rows, GEMV_STORE));
+    // final softcap + greedy argmax (InferenceEngine.cs:105-108, Sampler.cs:26-27); across ranks the
+    // packed (value, index) keys reduce with max
+    LLMDOT_TRY(launch_argmax_keys(w.logits, m->head_rows, m->head_rows, batch, w.keys, c.has_final_cap != 0,
+                                  c.final_cap, nullptr, m->head_lo, c.vocab, st));
+    if (m->tp > 1) LLMDOT_TRY(tp_allreduce_max_u64(m, w.keys, batch, st));
+    return launch_argmax_finish(w.keys, batch, next, st);
 }
 
 }  // namespace llmdot

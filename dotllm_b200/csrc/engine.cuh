@@ -68,6 +68,11 @@ struct llmdot_model {
     bool use_pdl = true;
     bool use_step_kernel = true;            // persistent whole-step kernel for prefill
     bool step_decode = false;               // ... and for decode steps
+    // tensor parallelism: cfg above holds THIS rank's local heads / kv heads / FFN rows; full_cfg
+    // the model's; the logits head (m->out) holds vocabulary rows [head_lo, head_lo + head_rows)
+    int tp = 1, tp_rank = 0, head_lo = 0, head_rows = 0;
+    llmdot_config full_cfg{};
+    void *nccl = nullptr;  // ncclComm_t once llmdot_cuda_tp_init ran
     llmdot::StepCache *step_cache = nullptr;  // per-batch launch plans of that kernel
 };
 
@@ -80,14 +85,18 @@ struct llmdot_session {
 };
 
 namespace llmdot {
-int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc *t, int n, llmdot_model **out);
+int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc *t, int n, llmdot_model **out,
+                 int tp = 1, int tp_rank = 0);
 void model_destroy(llmdot_model *m);
 int ensure_workspace(llmdot_model *m, int batch);
 // One forward step (ProcessToken) for `batch` rows: token ids, positions and KV views are
 // device arrays of `batch` entries.  Raw logits land in ws.logits, greedy ids in next.
 // tokens may alias next (the step reads its tokens before it writes the argmax).
+// flags: STEP_CHUNK = the rows are consecutive positions of one session (a prompt chunk): K/V
+// of every row are appended before attention; STEP_NO_HEAD = skip final norm, logits, argmax.
+enum { STEP_CHUNK = 1, STEP_NO_HEAD = 2 };
 int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens, const int32_t *pos,
-                 const KvView *views, int32_t *next, cudaStream_t st);
+                 const KvView *views, int32_t *next, cudaStream_t st, int flags = 0);
 int gemv(const DevMat &W, const float *x, int ldx, int nv, float *y, int ldy, bool accumulate, bool fast,
          cudaStream_t st);
 }  // namespace llmdot

@@ -323,12 +323,14 @@ int launch_softmax(float *x, int n, bool has_cap, float cap, cudaStream_t st)
 // value wins and, among equal values, the lowest index.  Optional in-kernel final
 // softcap of the logits first (Generate applies it before sampling,
 // InferenceEngine.cs:105-106); the capped logits are written back to `capped` if given.
+// Under tensor parallelism x holds vocabulary entries [off, off + n) of `ntot`: keys carry the
+// global index, and the vector-lane / tail choice of the softcap uses the global position.
 __global__ void argmax_kernel(const float *__restrict__ x, int ldx, int n, unsigned long long *__restrict__ keys,
-                              int has_cap, float cap, float *__restrict__ capped)
+                              int has_cap, float cap, float *__restrict__ capped, int off, int ntot)
 {
     const int v = blockIdx.y;
     const float *xv = x + (uint64_t)v * ldx;
-    const int nvec = n - n % 8;
+    const int nvec = ntot - ntot % 8 - off;
     float inv_cap = has_cap ? __fdiv_rn(1.0f, cap) : 0.0f;
     unsigned long long best = 0ull;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -337,7 +339,7 @@ __global__ void argmax_kernel(const float *__restrict__ x, int ldx, int n, unsig
             f = softcap_ref(f, cap, inv_cap, i < nvec);
             if (capped) capped[(uint64_t)v * ldx + i] = f;
         }
-        unsigned long long k = ((unsigned long long)float_key(f) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+        unsigned long long k = ((unsigned long long)float_key(f) << 32) | (0xFFFFFFFFu - (uint32_t)(i + off));
         best = k > best ? k : best;
     }
 #pragma unroll
@@ -354,17 +356,29 @@ __global__ void argmax_finish_kernel(const unsigned long long *__restrict__ keys
     if (v < nv) out[v] = (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[v] & 0xFFFFFFFFull));
 }
 
-int launch_argmax(const float *x, int ldx, int n, int nv, unsigned long long *keys, int32_t *out, bool has_cap,
-                  float cap, float *capped, cudaStream_t st)
+int launch_argmax_keys(const float *x, int ldx, int n, int nv, unsigned long long *keys, bool has_cap, float cap,
+                       float *capped, int off, int ntot, cudaStream_t st)
 {
     LLMDOT_CUDA_TRY(cudaMemsetAsync(keys, 0, sizeof(unsigned long long) * nv, st));
     int blocks = (n + 1023) / 1024;
     if (blocks > 148) blocks = 148;
-    argmax_kernel<<<dim3(blocks, nv), 256, 0, st>>>(x, ldx, n, keys, has_cap ? 1 : 0, cap, capped);
+    argmax_kernel<<<dim3(blocks, nv), 256, 0, st>>>(x, ldx, n, keys, has_cap ? 1 : 0, cap, capped, off, ntot);
     LLMDOT_CUDA_TRY(cudaGetLastError());
+    return LLMDOT_OK;
+}
+
+int launch_argmax_finish(const unsigned long long *keys, int nv, int32_t *out, cudaStream_t st)
+{
     argmax_finish_kernel<<<(nv + 63) / 64, 64, 0, st>>>(keys, nv, out);
     LLMDOT_CUDA_TRY(cudaGetLastError());
     return LLMDOT_OK;
+}
+
+int launch_argmax(const float *x, int ldx, int n, int nv, unsigned long long *keys, int32_t *out, bool has_cap,
+                  float cap, float *capped, cudaStream_t st)
+{
+    LLMDOT_TRY(launch_argmax_keys(x, ldx, n, nv, keys, has_cap, cap, capped, 0, n, st));
+    return launch_argmax_finish(keys, nv, out, st);
 }
 
 // ------------------------------------------------------------------ conv1d

@@ -19,6 +19,11 @@ int launch_rope(float *x, int nheads, int head_dim, const float *cs, const float
 int launch_softmax(float *x, int n, bool has_cap, float cap, cudaStream_t st);
 int launch_argmax(const float *x, int ldx, int n, int nv, unsigned long long *keys, int32_t *out, bool has_cap,
                   float cap, float *capped, cudaStream_t st);
+// The two halves of launch_argmax, for a vocabulary shard [off, off + n) of ntot entries (keys
+// reduced across ranks in between).
+int launch_argmax_keys(const float *x, int ldx, int n, int nv, unsigned long long *keys, bool has_cap, float cap,
+                       float *capped, int off, int ntot, cudaStream_t st);
+int launch_argmax_finish(const unsigned long long *keys, int nv, int32_t *out, cudaStream_t st);
 int launch_conv1d(const float *in, const float *w, float *o, int ks, int dim, cudaStream_t st);
 int launch_embed(const uint8_t *emb, uint32_t type, int hidden, int vocab, const int32_t *tokens, int nv, float scale,
                  float *h, int ldh, int *err, cudaStream_t st);

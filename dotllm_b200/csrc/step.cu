@@ -1254,7 +1254,7 @@ static StepPlan *get_plan(llmdot_model *m, int batch)
 
 bool step_kernel_supported(llmdot_model *m, int batch)
 {
-    if (!m->use_step_kernel || !m->use_fast_gemv || batch < 1 || batch > NV_MAX) return false;
+    if (!m->use_step_kernel || !m->use_fast_gemv || m->tp > 1 || batch < 1 || batch > NV_MAX) return false;
     if (ensure_workspace(m, batch) != LLMDOT_OK) return false;
     return get_plan(m, batch)->status == LLMDOT_OK;
 }

@@ -1,0 +1,36 @@
+// tp.cuh -- tensor parallelism: shard geometry and the NCCL collectives of the decode step.
+#pragma once
+#include "common.cuh"
+
+struct llmdot_model;
+struct llmdot_config;
+
+namespace llmdot {
+
+// What rank `rank` of `tp` holds (Megatron-style split):
+//   q rows [q_lo, q_lo+q_n)            (its heads / tp query heads)
+//   k, v rows [kv_lo, kv_lo+kv_n)      (its heads_kv / tp kv heads)
+//   attn_output columns [q_lo, q_lo+q_n)
+//   gate, up rows / down columns [f_lo, f_lo+f_n)
+//   logits rows [v_lo, v_lo+v_n)       (vocabulary shard; the embedding stays whole)
+struct TpShard {
+    int q_lo, q_n, kv_lo, kv_n, f_lo, f_n, v_lo, v_n;
+};
+
+// Fills `s`; fails when the model does not split evenly into `tp` ranks (heads, kv heads and FFN
+// rows divisible by tp, and the column splits on whole 256-weight super-blocks).
+int tp_shard(const llmdot_config &c, int tp, int rank, TpShard *s);
+
+// NCCL is loaded at run time (libnccl.so.2) the first time tensor parallelism is used, so the
+// library has no link-time NCCL dependency and shares the process's NCCL when torch loaded one.
+int tp_unique_id(void *out128);
+int tp_comm_init(llmdot_model *m, const void *id128);
+void tp_comm_destroy(llmdot_model *m);
+// In-place sum of `n` floats across the ranks, on stream st.
+int tp_allreduce_sum(llmdot_model *m, float *buf, size_t n, cudaStream_t st);
+// In-place max of `n` packed (value key, index) argmax keys across the ranks.
+int tp_allreduce_max_u64(llmdot_model *m, unsigned long long *buf, size_t n, cudaStream_t st);
+// All-gather of `n` floats per rank: recv holds rank r's block at r*n.
+int tp_allgather(llmdot_model *m, const float *send, float *recv, size_t n, cudaStream_t st);
+
+}  // namespace llmdot

@@ -32,6 +32,18 @@ class CudaModel:
         return cls(h.value, device)
 
     @classmethod
+    def load_tp(cls, path: str, tp_size: int, tp_rank: int, device: int = 0) -> "CudaModel":
+        """This rank's tensor-parallel shard of the model (attach the group with tp_init)."""
+        h = VP()
+        check(lib().llmdot_cuda_model_load_gguf_tp(device, path.encode(), tp_size, tp_rank, C.byref(h)))
+        return cls(h.value, device)
+
+    def tp_init(self, unique_id: bytes) -> None:
+        """Join the NCCL group whose id rank 0 obtained from tp_unique_id()."""
+        buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
+        check(lib().llmdot_cuda_tp_init(self._h, buf))
+
+    @classmethod
     def from_tensors(cls, cfg: dict, tensors: Sequence[Tuple[str, int, Sequence[int], np.ndarray]],
                      device: int = 0) -> "CudaModel":
         """Upload tensors the host already holds (the .NET LoadedModel path)."""
@@ -180,3 +192,19 @@ def decode_batch(sessions: List[CudaSession], tokens, want_logits: bool = False)
     check(lib().llmdot_cuda_decode(arr, B, toks.ctypes.data_as(I32P), nxt.ctypes.data_as(I32P),
                                    logits.ctypes.data_as(F32P) if logits is not None else None))
     return nxt, logits
+
+
+def tp_unique_id() -> bytes:
+    """An NCCL unique id (128 bytes) for llmdot_cuda_tp_init."""
+    buf = (C.c_uint8 * 128)()
+    check(lib().llmdot_cuda_tp_unique_id(buf))
+    return bytes(buf)
+
+
+def tp_shard(config: dict, tp_size: int, tp_rank: int) -> dict:
+    """Rows / columns of the full matrices that rank tp_rank holds (host only)."""
+    c = LlmdotConfig(**{k: v for k, v in config.items() if k in dict(LlmdotConfig._fields_)})
+    out = (C.c_int32 * 8)()
+    check(lib().llmdot_cuda_tp_shard(C.byref(c), tp_size, tp_rank, out))
+    keys = ["q_lo", "q_n", "kv_lo", "kv_n", "ffn_lo", "ffn_n", "vocab_lo", "vocab_n"]
+    return dict(zip(keys, list(out)))

@@ -252,6 +252,27 @@ LLMDOT_API int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
 LLMDOT_API int llmdot_cuda_model_matvec(llmdot_model *m, const char *tensor, const float *x, int batch,
                                         int mode, const float *norm_w, float *y);
 
+/* ---- tensor parallelism (Megatron-style, one process per GPU) ---------------------------
+ * The one-process-per-GPU form of the survey's `_tp_init(model, tpSize, devices)`: every rank
+ * loads ITS shard of the model, rank 0 creates an NCCL unique id that the host distributes
+ * (e.g. with torch.distributed), and every rank attaches it.  Shards: attn_q/k/v and
+ * ffn_gate/up by output rows (whole heads), attn_output and ffn_down by input columns, the
+ * logits head by vocabulary rows; the embedding and norms stay whole.  Each decode step then
+ * does one in-place NCCL all-reduce of the residual after attn_output and one after ffn_down,
+ * and a max all-reduce of the packed argmax keys.  All ranks must make the same prefill /
+ * decode / generate calls in the same order (they contain collectives); logits read back under
+ * TP are gathered from every rank (needs vocab % tp_size == 0).  llmdot_cuda_model_config
+ * returns the full model's configuration. */
+LLMDOT_API int llmdot_cuda_model_load_gguf_tp(int device, const char *path, int tp_size, int tp_rank,
+                                              llmdot_model **out);
+/* 128 bytes of ncclUniqueId (NCCL is loaded at run time from libnccl.so.2). */
+LLMDOT_API int llmdot_cuda_tp_unique_id(uint8_t *out128);
+/* Attaches the NCCL communicator (ncclCommInitRank on the model's device). */
+LLMDOT_API int llmdot_cuda_tp_init(llmdot_model *m, const uint8_t *id128);
+/* Shard geometry of rank tp_rank (host only, no device needed): out8 = {q_lo, q_n, kv_lo, kv_n,
+ * ffn_lo, ffn_n, vocab_lo, vocab_n} in rows / columns of the full matrices. */
+LLMDOT_API int llmdot_cuda_tp_shard(const llmdot_config *cfg, int tp_size, int tp_rank, int32_t *out8);
+
 /* Profiling hook (no counterpart in the reference): average device time of one matvec launch
  * over the named weight tensor for `batch` input rows; `iters` launches are captured into a CUDA
  * graph and one replay is timed with CUDA events on the model's stream.  A name of the form

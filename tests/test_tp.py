@@ -1,0 +1,153 @@
+"""Tensor parallelism: shard geometry on CPU ranks, and TP=2 decode on two GPUs.
+
+CPU part: two `gloo` ranks each ask the library (host-only entry point, no device) for their
+shard of several BASELINE shapes and all-gather them; the shards must tile every split
+dimension exactly once.  GPU part (skipped with fewer than two GPUs): two spawned processes
+load their shards of the tiny config, join one NCCL group and must reproduce the single-GPU
+greedy tokens and logits.
+"""
+import json
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from dotllm_b200 import synth
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _shard_rank(rank, world, port, configs, q):
+    import torch.distributed as dist
+
+    from dotllm_b200.engine import tp_shard
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        mine = {name: tp_shard(cfg, world, rank) for name, cfg in configs.items()}
+        everyone = [None] * world
+        dist.all_gather_object(everyone, mine)
+        if rank == 0:
+            q.put(everyone)
+    finally:
+        dist.destroy_process_group()
+
+
+def _config_dict(cfg):
+    return {"template_id": 0, "hidden": cfg.hidden, "layers": cfg.layers, "context": cfg.context,
+            "vocab": cfg.vocab, "ffn": cfg.ffn, "heads": cfg.heads, "heads_kv": cfg.heads_kv,
+            "head_dim": cfg.head_dim}
+
+
+def test_tp_shards_tile_gloo():
+    configs = {n: _config_dict(synth.get(n)) for n in ("tiny", "llama1b", "llama8b")}
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shard_rank, args=(r, world, port, configs, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    everyone = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for name, cfg in configs.items():
+        hd = cfg["head_dim"]
+        for lo, n, total in (("q_lo", "q_n", cfg["heads"] * hd), ("kv_lo", "kv_n", cfg["heads_kv"] * hd),
+                             ("ffn_lo", "ffn_n", cfg["ffn"]), ("vocab_lo", "vocab_n", cfg["vocab"])):
+            spans = sorted((r[name][lo], r[name][n]) for r in everyone)
+            pos = 0
+            for a, b in spans:
+                assert a == pos and b > 0, (name, lo, spans)
+                pos = a + b
+            assert pos == total, (name, lo, spans, total)
+        # column shards of attn_output / ffn_down fall on whole 256-weight super-blocks
+        for r in everyone:
+            assert r[name]["q_n"] % 256 == 0 and r[name]["ffn_n"] % 256 == 0
+
+
+def test_tp_shard_rejects_uneven():
+    from dotllm_b200.engine import tp_shard
+    from dotllm_b200.native import CudaBackendError
+
+    cfg = _config_dict(synth.get("tiny"))
+    with pytest.raises(CudaBackendError):
+        tp_shard(cfg, 3, 0)  # 8 heads / 4 kv heads do not split in 3
+    with pytest.raises(CudaBackendError):
+        tp_shard(cfg, 4, 0)  # 128-column attn_output shards are not whole super-blocks
+
+
+def _tp_rank(rank, world, path, prompt, steps, q_in, q_out):
+    from dotllm_b200.engine import CudaModel, tp_unique_id
+
+    m = CudaModel.load_tp(path, world, rank, device=rank)
+    if rank == 0:
+        uid = tp_unique_id()
+        for _ in range(world - 1):
+            q_in.put(uid)
+    else:
+        uid = q_in.get(timeout=120)
+    m.tp_init(uid)
+    s = m.session(kv="f32")
+    _, lg = s.prefill(prompt, want_logits=True)
+    toks = s.generate(prompt, steps)
+    # five sessions decoded together take the batched matmul path
+    ss = [m.session(kv="f32") for _ in range(5)]
+    firsts = [x.prefill(prompt)[0] for x in ss]
+    from dotllm_b200.engine import decode_batch
+    nxt, blg = decode_batch(ss, firsts, want_logits=True)
+    if rank == 0:
+        q_out.put((list(map(int, toks)), lg, firsts, list(map(int, nxt)), blg))
+    s.close()
+    for x in ss:
+        x.close()
+    m.close()
+
+
+@pytest.mark.gpu
+def test_tp2_matches_single_gpu(gpu):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from dotllm_b200.engine import CudaModel, decode_batch
+
+    name = "tiny"
+    cfg = synth.get(name)
+    path = synth.build_model(cfg)
+    prompt = synth.prompt_tokens(cfg)
+    steps = 24
+    ref = CudaModel.load(path)
+    rs = ref.session(kv="f32")
+    _, ref_lg = rs.prefill(prompt, want_logits=True)
+    ref_toks = list(map(int, rs.generate(prompt, steps)))
+    rss = [ref.session(kv="f32") for _ in range(5)]
+    rf = [x.prefill(prompt)[0] for x in rss]
+    ref_nxt, ref_blg = decode_batch(rss, rf, want_logits=True)
+    ctx = mp.get_context("spawn")
+    q_in, q_out = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_tp_rank, args=(r, 2, path, prompt, steps, q_in, q_out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    toks, lg, firsts, nxt, blg = q_out.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert np.abs(lg - ref_lg).max() < 1e-3
+    assert toks == ref_toks
+    assert firsts == [ref_toks[0]] * 5
+    assert np.abs(blg - ref_blg).max() < 1e-3
+    assert nxt == list(map(int, ref_nxt))
+    golden = json.load(open(os.path.join(HERE, "golden", "greedy_tokens.json")))["tiny"]["tokens"]
+    assert toks == golden[:steps]
