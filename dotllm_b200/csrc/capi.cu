@@ -807,7 +807,10 @@ extern "C" int llmdot_cuda_prefill(llmdot_session *s, const int32_t *tokens, int
     if (rc != LLMDOT_OK) return rc;
     if (logits) LLMDOT_TRY(read_logits(m, last_row + 1, last_row, logits, st));
     int32_t nt = 0;
-    LLMDOT_CUDA_TRY(cudaMemcpyAsync(&nt, w.next + last_row, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    // the device loop of generate feeds next[0]: the last prompt token's argmax goes there
+    if (last_row > 0)
+        LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.next, w.next + last_row, sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(&nt, w.next, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
     LLMDOT_CUDA_TRY(cudaStreamSynchronize(st));
     LLMDOT_TRY(check_err_flag(m));
     s->pos += n;
