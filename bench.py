@@ -129,10 +129,13 @@ def run_reference(args, rank):
     res = cpu_baseline_sample(path, cfg, threads, n_prompt, k)
     v = res["decode_tok_s"]
     line = {
-        "impl": "reference", "metric": "decode tok/s", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": f"decode tok/s (batch {args.batch})", "value": v, "unit": "tok/s",
+        "n_gpus": args.gpus,
         "steps": k, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.config, "batch": 1, "kv": "f32 (reference KvCache)"},
+        "config": {"workload": WORKLOADS.get(args.config, args.config).format(prompt=n_prompt, kv="f32", ctx="its",
+                                                                              batch=1),
+                   "model": args.config, "note": "the reference decodes one session at a time on the host cores"},
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": f"{n_prompt}-token prompt then {k} greedy decode steps of the {args.config} model "
                                    f"(C restatement of llmdot's managed CPU path, row-parallel OpenMP, {threads} threads)"},
@@ -147,6 +150,44 @@ def run_reference(args, rank):
 DRAM_PER_ALGORITHMIC_BYTE = (2.431232 + 18.949632 + 13.859072 + 3.880960) / (2.359296 + 18.874368 + 13.762560 + 3.813376)
 
 
+def measure(m, cfg, args, B, n_prompt, ctx, rank, steps, dist, local, clocks=False):
+    """Prefill B sessions, warm up, then time `steps` device-resident greedy steps of all of them
+    (max over ranks).  Returns the sessions, the device ms, kernels per step, prefill seconds and
+    the clock record."""
+    import torch
+    from dotllm_b200.engine import decode_steps
+    sessions = [m.session(max_ctx=ctx, kv=args.kv) for _ in range(B)]
+    # under tensor parallelism every rank decodes the same sessions; under DP, distinct ones
+    sid = 0 if args.tp else rank * B
+    prompts = [synth.prompt_tokens(cfg, n_prompt, session=sid + i) for i in range(B)]
+    t0 = time.perf_counter()
+    first = [s.prefill(p)[0] for s, p in zip(sessions, prompts)]
+    prefill_s = time.perf_counter() - t0
+    toks, _, _ = decode_steps(sessions, first, args.warmup)
+    cur = toks[-1]
+    if dist:
+        dist.barrier()
+        torch.cuda.synchronize()
+    gpu_index = local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            gpu_index = int(vis.split(",")[local])
+        except ValueError:
+            pass
+    clk = ClockSampler(gpu_index if clocks else -1)
+    if clocks:
+        with clk:
+            out, dev_ms, kps = decode_steps(sessions, cur, steps)
+    else:
+        out, dev_ms, kps = decode_steps(sessions, cur, steps)
+    if dist:
+        t = torch.tensor([dev_ms, prefill_s], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, prefill_s = float(t[0].item()), float(t[1].item())
+    return sessions, out[-1], dev_ms, kps, prefill_s, clk
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -154,16 +195,20 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="llama1b")
-    ap.add_argument("--batch", type=int, default=1, help="sessions per GPU")
+    ap.add_argument("--batch", type=int, default=1, help="sessions per GPU (per TP group with --tp)")
     ap.add_argument("--prompt", type=int, default=None)
     ap.add_argument("--kv", choices=["f16", "f32"], default="f16")
+    ap.add_argument("--tp", action="store_true", help="the torchrun ranks form ONE tensor-parallel group")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch32", action="store_true", help="skip the sharded batch-32 measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
+    if world == 1:
+        args.tp = False
 
     if args.impl == "reference":
         run_reference(args, rank)
@@ -194,37 +239,18 @@ def main():
                "sample": f"{n_pre}-token prompt then {n_dec} greedy decode steps of the same model, C restatement of "
                          f"llmdot's managed CPU path (oracle/), 1 thread"}
 
-    from dotllm_b200.engine import CudaModel, decode_batch, decode_steps
-    m = CudaModel.load(path, device=local)
+    from dotllm_b200.engine import CudaModel, decode_batch, tp_unique_id
+    if args.tp:
+        m = CudaModel.load_tp(path, world, rank, device=local)
+        uid = [tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        m.tp_init(uid[0])
+    else:
+        m = CudaModel.load(path, device=local)
     ctx = min(cfg.context, 4096) if args.config == "llama1b" else cfg.context
     B = args.batch
-    sessions = [m.session(max_ctx=ctx, kv=args.kv) for _ in range(B)]
-    prompts = [synth.prompt_tokens(cfg, n_prompt, session=rank * B + i) for i in range(B)]
-    t0 = time.perf_counter()
-    first = [s.prefill(p)[0] for s, p in zip(sessions, prompts)]
-    prefill_s = time.perf_counter() - t0
-    toks, _, _ = decode_steps(sessions, first, args.warmup)
-    cur = toks[-1]
-
-    if dist:
-        import torch
-        dist.barrier()
-        torch.cuda.synchronize()
-    gpu_index = local
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    if vis:
-        try:
-            gpu_index = int(vis.split(",")[local])
-        except ValueError:
-            pass
-    with ClockSampler(gpu_index) as clk:
-        out, dev_ms, kps = decode_steps(sessions, cur, args.steps)
-    if dist:
-        import torch
-        t = torch.tensor([dev_ms], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dev_ms = float(t.item())
-    cur = out[-1]
+    sessions, cur, dev_ms, kps, prefill_s, clk = measure(m, cfg, args, B, n_prompt, ctx, rank, args.steps, dist,
+                                                         local, clocks=True)
 
     # end to end through the public per-step API: host tokens in, host ids out, every step
     if dist:
@@ -239,6 +265,8 @@ def main():
         t = torch.tensor([e2e_s], device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
+    for s in sessions:
+        s.close()
 
     # roofline of the dominant kernel family: the quantised matvec launches of one step,
     # each timed live with CUDA events (profile_matvec), aggregated over the step's launches
@@ -251,7 +279,7 @@ def main():
         tot_ms += ms * c["layers"]
         tot_bytes += nb * c["layers"]
         launches += c["layers"]
-    head = "token_embd.weight" if c["tied"] else "output.weight"
+    head = "output.weight" if (args.tp or not c["tied"]) else "token_embd.weight"
     ms, nb = m.profile_matvec(head, B, 10)
     tot_ms += ms
     tot_bytes += nb
@@ -259,25 +287,40 @@ def main():
     peak, peak_kind = peaks()
     achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
 
+    # sessions sharded over the GPUs: 32 in total (the north star's scaling workload)
+    b32 = None
+    if not args.tp and not args.no_batch32 and 32 % world == 0 and 32 // world != B:
+        per = 32 // world
+        k32 = min(args.steps, 64)
+        ss, _, ms32, _, pre32, _ = measure(m, cfg, args, per, n_prompt, ctx, rank, k32, dist, local)
+        for s in ss:
+            s.close()
+        b32 = {"global_batch": 32, "sessions_per_gpu": per, "steps": k32, "value": per * world * k32 / (ms32 * 1e-3),
+               "unit": "tok/s", "ms_per_step": ms32 / k32, "prefill_tok_s": per * world * n_prompt / pre32}
+
     K = args.steps
     step_ms = dev_ms / K
     layer_b, head_b = m.weight_bytes()
     kv_bytes_per_elem = 2 if args.kv == "f16" else 4
-    kv_dim = c["heads_kv"] * c["head_dim"]
+    kv_dim = c["heads_kv"] * c["head_dim"] // (world if args.tp else 1)
     mean_pos = n_prompt + args.warmup + K / 2.0
     kv_read = B * c["layers"] * 2 * kv_dim * kv_bytes_per_elem * mean_pos
     step_bytes = layer_b + head_b + kv_read
-    value = B * K * world / (dev_ms * 1e-3)
+    ranks_tokens = 1 if args.tp else world  # a TP group decodes one set of sessions
+    value = B * K * ranks_tokens / (dev_ms * 1e-3)
+    par = f"tp{world} (one tensor-parallel group, NCCL all-reduce after attn-out and ffn-down)" if args.tp else \
+        f"dp{world} (independent sessions per GPU)"
     line = {
         "metric": f"decode tok/s (batch {B})", "value": value, "unit": "tok/s", "n_gpus": world, "steps": K,
-        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32",
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+        "scaling": "strong" if args.tp else "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded N(0,0.02) weights quantised to Q4_K/Q6_K, uniform random prompt ids",
         "config": {"workload": WORKLOADS.get(args.config, args.config).format(prompt=n_prompt, kv=args.kv, ctx=ctx,
                                                                               batch=B),
-                   "model": args.config, "global_batch": B * world, "seq_len": n_prompt, "kv": args.kv,
-                   "parallelism": f"dp{world} (independent sessions per GPU)",
-                   "l2": f"weights ({(layer_b + head_b) / 1e6:.0f} MB) exceed L2 (126 MB): inputs larger than L2, no flush"},
+                   "model": args.config, "global_batch": B * ranks_tokens, "seq_len": n_prompt, "kv": args.kv,
+                   "parallelism": par,
+                   "l2": f"weights ({(layer_b + head_b) / 1e6:.0f} MB per GPU) exceed L2 (126 MB): inputs larger "
+                         f"than L2, no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": tot_bytes * DRAM_PER_ALGORITHMIC_BYTE,
                      "traffic_note": "DRAM bytes per step scaled from the ncu capture in "
@@ -287,17 +330,16 @@ def main():
                      "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind},
         "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (step_ms * 1e-3) / 1e9,
                           "frac": step_bytes / (step_ms * 1e-3) / 1e9 / peak,
-                          "note": "quantised weights + KV reads at the mean position / device step time"},
+                          "note": "per GPU: quantised weights + KV reads at the mean position / device step time"},
         "cpu_baseline": cpu,
-        "e2e": {"value": B * e2e_steps * world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": B * (4 + 4 + 32),
+        "e2e": {"value": B * e2e_steps * ranks_tokens / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": B * (4 + 4 + 32),
                 "d2h_bytes_per_step": B * 4},
         "gpu_launches": kps * K,
         "kernels_per_step": kps,
         "clocks": clk.summary(),
-        "prefill_tok_s": B * n_prompt / prefill_s,
+        "prefill_tok_s": B * ranks_tokens * n_prompt / prefill_s,
+        "sharded_batch32": b32,
     }
-    for s in sessions:
-        s.close()
     m.close()
     if dist:
         dist.barrier()
