@@ -1062,6 +1062,10 @@ extern "C" int llmdot_cuda_profile_matvec(llmdot_model *m, const char *tensor, i
         total += W->bytes();
     }
     LLMDOT_CUDA_TRY(cudaSetDevice(m->device));
+    // 5..32 rows run the batched kernel, as in the decode step (input fragments + matmul per launch)
+    bool batched = m->use_fast_gemv && batch >= GEMM_MIN_ROWS && batch <= GEMM_MAX_ROWS;
+    for (const DevMat *W : mats) batched = batched && gemm_supported(*W, batch);
+    if (batched) LLMDOT_TRY(ensure_workspace(m, batch));
     float *x = nullptr, *y = nullptr;
     LLMDOT_CUDA_TRY(cudaMalloc(&x, sizeof(float) * (size_t)batch * max_cols));
     LLMDOT_CUDA_TRY(cudaMalloc(&y, sizeof(float) * (size_t)batch * max_rows));
@@ -1069,7 +1073,14 @@ extern "C" int llmdot_cuda_profile_matvec(llmdot_model *m, const char *tensor, i
     cudaMemsetAsync(x, 0, sizeof(float) * (size_t)batch * max_cols, st);
     auto pass = [&]() {
         for (const DevMat *W : mats) {
-            const int rc = gemv(*W, x, W->cols, batch, y, W->rows, false, m->use_fast_gemv, st);
+            int rc;
+            if (batched) {
+                GemmInput in;
+                rc = gemm_prepare(x, W->cols, batch, W->cols, nullptr, m->cfg.eps, W->type, 0, m->ws.gemm, &in, st);
+                if (rc == LLMDOT_OK) rc = launch_gemm(*W, in, y, W->rows, GEMV_STORE, m->ws.gemm, m->ws.err, st);
+            } else {
+                rc = gemv(*W, x, W->cols, batch, y, W->rows, false, m->use_fast_gemv, st);
+            }
             if (rc != LLMDOT_OK) return rc;
         }
         return (int)LLMDOT_OK;
