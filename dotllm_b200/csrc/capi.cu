@@ -737,6 +737,7 @@ static int read_logits(llmdot_model *m, int batch, int row, float *host, cudaStr
 
 static int check_err_flag(llmdot_model *m)
 {
+    LLMDOT_TRY(gemv_timeout_check());
     int e = 0;
     LLMDOT_CUDA_TRY(cudaMemcpy(&e, m->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {

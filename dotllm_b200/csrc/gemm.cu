@@ -387,10 +387,7 @@ __global__ void __launch_bounds__(GW * 32, 1) gemm_q_kernel(const __grid_constan
                 w_done = i + 1;
                 TileRegs T;
                 read_tile(T, ring + (size_t)slot * GSLOT, a.qt, lane);
-                const uint4 *xs = (const uint4 *)(xb + buf * XB);
-                if (q4) q4k_tile_nb<NB>(T, xs, (const uint32_t *)(xb + buf * XB + xsb_bytes(NB)), t, g, acc, cc);
-                else q6k_tile_nb<NB>(T, xs, t, g, acc);
-                __syncwarp();  // every lane has consumed the slot before it is refilled
+                __syncwarp();  // the tile is in registers: refill its slot before the math
                 if (i + GRING < n) {
                     if (lane == 0) {
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -399,6 +396,9 @@ __global__ void __launch_bounds__(GW * 32, 1) gemm_q_kernel(const __grid_constan
                     }
                     w_issued = i + 1 + GRING;
                 }
+                const uint4 *xs = (const uint4 *)(xb + buf * XB);
+                if (q4) q4k_tile_nb<NB>(T, xs, (const uint32_t *)(xb + buf * XB + xsb_bytes(NB)), t, g, acc, cc);
+                else q6k_tile_nb<NB>(T, xs, t, g, acc);
             }
         }
         if (!__syncthreads_and(ok)) {  // every warp is done with fragment buffer `buf`, or one gave up

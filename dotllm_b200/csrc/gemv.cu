@@ -162,31 +162,53 @@ struct GemvArgs {
 };
 
 // Tiles in flight per warp: each warp streams its tiles through a private ring of RING (2 or 3)
-// shared-memory slots filled with cp.async, so RING-1 tiles are always on their way while it
-// computes one.
+// shared-memory slots.  Lane 0 fetches a whole tile with one TMA bulk copy (cp.async.bulk, tiles
+// are contiguous) completing on the slot's mbarrier; the refill of a slot is issued as soon as
+// the warp has consumed it, so RING tiles are always on their way.  Every wait is bounded.
+constexpr unsigned long long GEMV_WAIT_NS = 2000000000ull;
+__device__ int g_gemv_timeout;  // set when a bounded wait gave up (read by gemv_timeout_check)
 
-__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc)
+__device__ __forceinline__ uint32_t gsm_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ uint64_t g_timer()
 {
-    const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
-    asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// The warp copies one tile (global, contiguous) into a ring slot: every lane moves its own
-// 16-byte plane slots (fully coalesced), the header bytes are split over the first lanes.
-__device__ __forceinline__ void issue_tile(uint8_t *slot, const uint8_t *tp, int qt, int lane)
+__device__ __forceinline__ void gmbar_init(uint64_t *b)
 {
-    if (qt == QT_Q4K) {
-#pragma unroll
-        for (int p = 0; p < 4; p++) cp_async16(slot + p * 512 + lane * 16, tp + p * 512 + lane * 16);
-        if (lane < 16) cp_async16(slot + 2048 + lane * 16, tp + 2048 + lane * 16);
-    } else {
-#pragma unroll
-        for (int p = 0; p < 6; p++) cp_async16(slot + p * 512 + lane * 16, tp + p * 512 + lane * 16);
-        if (lane < 16) cp_async16(slot + 3072 + lane * 16, tp + 3072 + lane * 16);
-        else if (lane < 18) cp_async16(slot + 3328 + (lane - 16) * 16, tp + 3328 + (lane - 16) * 16);
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(gsm_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool gmbar_test(uint64_t *b, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(gsm_u32(b)), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait for the fill with the given parity; the answer is uniform across the warp
+__device__ __forceinline__ bool gmbar_wait(uint64_t *b, uint32_t parity)
+{
+    bool ok = gmbar_test(b, parity);
+    if (!ok) {
+        const uint64_t t0 = g_timer();
+        while (!(ok = gmbar_test(b, parity)))
+            if (g_timer() - t0 > GEMV_WAIT_NS) break;
     }
+    return __all_sync(0xffffffffu, ok);
+}
+// lane 0: one bulk copy of a tile into a ring slot
+__device__ __forceinline__ void issue_bulk(uint8_t *slot, const uint8_t *src, uint32_t bytes, uint64_t *b)
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(gsm_u32(b)), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     gsm_u32(slot)),
+                 "l"(src), "r"(bytes), "r"(gsm_u32(b))
+                 : "memory");
 }
 
 __device__ __forceinline__ int find_seg(const GemvArgs &a, int gt, int &rt)
@@ -204,14 +226,14 @@ constexpr int GEMV_WARPS = 16;  // warps per CTA (one CTA per SM)
 
 // Shared memory of one CTA (byte offsets; all 16-byte aligned).
 struct GemvSmem {
-    int xs4, xs6, S, P, red, stat, wred, ring, total, slot;
+    int xs4, xs6, S, P, red, stat, wred, ring, total, slot;  // byte offsets (slot: bytes per ring slot)
 };
 __host__ __device__ inline GemvSmem gemv_layout(int nv, int nsb, int nmat, bool q4, bool q6, int max_rt_cta,
                                                 int ring)
 {
     GemvSmem L;
     const int xsz = nsb * 64 * nv * 16;
-    int o = 0;
+    int o = GEMV_WARPS * 3 * 8;  // slot mbarriers [GEMV_WARPS][3]
     L.xs4 = o;
     o += q4 ? xsz : 0;
     L.xs6 = o;
@@ -247,26 +269,38 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     uint8_t *ring = smem + L.ring + (size_t)warp * RING * L.slot;
+    uint64_t *mb = (uint64_t *)smem + warp * 3;  // this warp's slot mbarriers
     // this CTA owns row tiles [rt_lo, rt_hi) of the concatenated segments; its flat tile list
     // is (row tile, matrix, super-block), and warp w takes tiles w, w+16, ...
     const int rt_lo = (int)((long long)blockIdx.x * a.rt_total / gridDim.x);
     const int rt_hi = (int)((long long)(blockIdx.x + 1) * a.rt_total / gridDim.x);
     const int nrt = rt_hi - rt_lo, per_rt = NMAT * nsb, ntile = nrt * per_rt;
     const int F = ntile > warp ? (ntile - warp + GEMV_WARPS - 1) / GEMV_WARPS : 0;
-    auto issue = [&](int f) {
-        if (f < F) {
-            const int ti = warp + f * GEMV_WARPS, rtl = ti / per_rt, rem = ti % per_rt;
+    // issue cursor: tile f = row tile rtl, position rem (matrix rem / nsb, super-block rem % nsb)
+    int i_f = 0, i_rtl = warp / per_rt, i_rem = warp % per_rt;
+    auto issue = [&]() {  // next tile of the warp into slot i_f % RING
+        if (i_f >= F) return;
+        if (lane == 0) {
             int rt;
-            const GemvSeg &sg = a.seg[find_seg(a, rt_lo + rtl, rt)];
-            const int tb = sg.qt == QT_Q4K ? Q4K_TILE : Q6K_TILE;
-            issue_tile(ring + (f % RING) * L.slot,
-                       (rem / nsb == 0 ? sg.w : sg.w1) + ((size_t)rt * nsb + rem % nsb) * tb, sg.qt, lane);
+            const GemvSeg &sg = a.seg[find_seg(a, rt_lo + i_rtl, rt)];
+            const uint32_t tb = sg.qt == QT_Q4K ? Q4K_TILE : Q6K_TILE;
+            const int mat = i_rem >= nsb ? 1 : 0, sb = i_rem - mat * nsb;
+            issue_bulk(ring + (i_f % RING) * L.slot, (mat ? sg.w1 : sg.w) + ((size_t)rt * nsb + sb) * tb, tb,
+                       mb + i_f % RING);
         }
-        cp_async_commit();  // (possibly empty) group: keeps the wait count uniform
+        i_f++;
+        i_rem += GEMV_WARPS;
+        while (i_rem >= per_rt) {
+            i_rem -= per_rt;
+            i_rtl++;
+        }
     };
+    if (tid < GEMV_WARPS * 3) gmbar_init((uint64_t *)smem + tid);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
     // weights are constant: start streaming before waiting for the previous kernel
 #pragma unroll
-    for (int f = 0; f < RING - 1; f++) issue(f);
+    for (int f = 0; f < RING; f++) issue();
     pdl_launch();
     pdl_wait();
 
@@ -379,11 +413,22 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
     // ---- streaming loop: no CTA-wide barrier inside, warps run independently
     const bool bact = g < 2 * NV;  // lanes whose B column is a real (vector, part)
     const int bv = g >> 1, bpart = g & 1;
+    int c_rtl = warp / per_rt, c_rem = warp % per_rt;  // consume cursor
+    bool ok = true;
+    int f_fail = F;
     for (int f = 0; f < F; f++) {
-        issue(f + RING - 1);
-        cp_async_wait<RING - 1>();
-        __syncwarp();
-        const int ti = warp + f * GEMV_WARPS, rtl = ti / per_rt, rem = ti % per_rt, mat = rem / nsb, sb = rem % nsb;
+        const int rtl = c_rtl, mat = c_rem >= nsb ? 1 : 0, sb = c_rem - mat * nsb;
+        c_rem += GEMV_WARPS;
+        while (c_rem >= per_rt) {
+            c_rem -= per_rt;
+            c_rtl++;
+        }
+        if (!gmbar_wait(mb + f % RING, (uint32_t)(f / RING) & 1u)) {
+            ok = false;
+            f_fail = f;
+            if (lane == 0) atomicExch(&g_gemv_timeout, 1);
+            break;
+        }
         int rt;
         const int qt = a.seg[find_seg(a, rt_lo + rtl, rt)].qt;
         float acc0 = 0.0f, acc1 = 0.0f;  // rows g, g+8 for vector t (MMA columns 2t, 2t+1)
@@ -392,9 +437,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
         for (int v = 0; v < NV; v++) corr0[v] = corr1[v] = 0.0f;
         TileRegs T;
         read_tile(T, ring + (f % RING) * L.slot, qt, lane);
+        __syncwarp();  // the tile is in registers: refill its slot with tile f + RING before the math
+        issue();
         if (qt == QT_Q4K) q4k_tile<NV>(T, xs4, S, nsb, sb, t, bact, bv, bpart, acc0, acc1, corr0, corr1);
         else q6k_tile<NV>(T, xs6, sb, t, bact, bv, bpart, acc0, acc1);
-        __syncwarp();  // the slot is refilled by a later issue
         if (qt == QT_Q4K) {
             // offset term: each lane of a row group covered 2 sub-blocks; sum over the group
             float k0 = 0.0f, k1 = 0.0f;
@@ -419,8 +465,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
             rp[(g + 8) * NV + t] += acc1;
         }
     }
-    cp_async_wait<0>();
-    __syncthreads();
+    if (!ok)  // bounded drain of this warp's copies still in flight, then leave the output untouched
+        for (int k = f_fail; k < i_f; k++) gmbar_wait(mb + k % RING, (uint32_t)(k / RING) & 1u);
+    if (!__syncthreads_and(ok)) return;
 
     // ---- epilogue: every (row tile, row, vector) of the CTA, warps summed in a fixed order
     for (int it = tid; it < nrt * 16 * NV; it += NT) {
@@ -461,6 +508,18 @@ static size_t gemv_need(int nv, int nsb, int nmat, bool q4, bool q6, int max_rt,
         }
     }
     return 0;
+}
+
+int gemv_timeout_check()
+{
+    int v = 0;
+    LLMDOT_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_gemv_timeout, sizeof(int)));
+    if (v) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_gemv_timeout, &zero, sizeof(int));
+        return fail(LLMDOT_E_TIMEOUT, "matvec: a weight tile wait timed out");
+    }
+    return LLMDOT_OK;
 }
 
 bool gemv_fast_supported(const DevMat &W, int nv)

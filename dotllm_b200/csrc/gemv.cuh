@@ -17,6 +17,8 @@ struct GemvTarget {
 
 // Allocate and fill W.tiled (the tensor-core layout) for Q4_K / Q6_K matrices.
 int prepare_tiled(llmdot_model *m, DevMat &W);
+// LLMDOT_E_TIMEOUT (and the flag cleared) when a bounded wait of the matvec kernel gave up.
+int gemv_timeout_check();
 bool gemv_fast_supported(const DevMat &W, int nv);
 int launch_gemv_fast(const DevMat &W, const float *x, int ldx, int nv, float *y, int ldy, bool accumulate,
                      cudaStream_t st);

@@ -268,6 +268,7 @@ __device__ __forceinline__ void issue_next(const StepArgs &a, const PhHdr *hdr, 
     if (c.s >= a.n_steps) return;
     const int slot = ip.slot;
     if (lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slot's last reads come first
         mbar_expect_tx(mb_w + slot, c.tb);
         if (a.evict_first) bulk_load(ring_w + (size_t)slot * SLOT, c.src, c.tb, mb_w + slot, evict_first_policy());
         else bulk_load(ring_w + (size_t)slot * SLOT, c.src, c.tb, mb_w + slot);
@@ -556,11 +557,11 @@ __device__ bool mv_tiles(const StepArgs &a, const StepPhase &ph, int lo, int hi,
             const unsigned long long w1 = tr ? gtimer() : 0;
             TileRegs T;
             read_tile(T, ring_w + (size_t)slot * SLOT, qt, lane);
-            if (qt == QT_Q4K) q4k_tile<NV>(T, L.xs4, L.S, nsb, sb, t, bact, bv, bpart, acc0, acc1, corr0, corr1);
-            else q6k_tile<NV>(T, L.xs6, sb, t, bact, bv, bpart, acc0, acc1);
-            __syncwarp();  // every lane has consumed the slot before it is refilled
+            __syncwarp();  // the tile is in registers: refill its slot before the math
             cp.step(a.ring);
             issue_next(a, hdr, cur, warp, lane, ring_w, mb_w, ip);
+            if (qt == QT_Q4K) q4k_tile<NV>(T, L.xs4, L.S, nsb, sb, t, bact, bv, bpart, acc0, acc1, corr0, corr1);
+            else q6k_tile<NV>(T, L.xs6, sb, t, bact, bv, bpart, acc0, acc1);
             if (tr) {
                 t_wait += w1 - w0;
                 t_comp += gtimer() - w1;
