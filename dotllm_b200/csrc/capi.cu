@@ -1063,9 +1063,15 @@ extern "C" int llmdot_cuda_profile_matvec(llmdot_model *m, const char *tensor, i
         total += W->bytes();
     }
     LLMDOT_CUDA_TRY(cudaSetDevice(m->device));
-    // 5..32 rows run the batched kernel, as in the decode step (input fragments + matmul per launch)
-    bool batched = m->use_fast_gemv && batch >= GEMM_MIN_ROWS && batch <= GEMM_MAX_ROWS;
-    for (const DevMat *W : mats) batched = batched && gemm_supported(*W, batch);
+    // as in the decode step: 5..32 rows run the batched kernel (input fragments + matmul per
+    // launch), and so do 2..4 rows whose input does not fit the matvec kernel's shared memory
+    bool batched = m->use_fast_gemv && batch >= 2 && batch <= GEMM_MAX_ROWS;
+    bool any_wide = batch >= GEMM_MIN_ROWS;
+    for (const DevMat *W : mats) {
+        batched = batched && gemm_supported(*W, batch);
+        any_wide = any_wide || !gemv_fast_supported(*W, batch);
+    }
+    batched = batched && any_wide;
     if (batched) LLMDOT_TRY(ensure_workspace(m, batch));
     float *x = nullptr, *y = nullptr;
     LLMDOT_CUDA_TRY(cudaMalloc(&x, sizeof(float) * (size_t)batch * max_cols));
@@ -1144,7 +1150,8 @@ extern "C" int llmdot_cuda_model_matvec(llmdot_model *m, const char *tensor, con
     if (cudaMemcpyAsync(dx, x, sizeof(float) * nx, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         (norm_w && cudaMemcpyAsync(dn, norm_w, sizeof(float) * W.cols, cudaMemcpyHostToDevice, st) != cudaSuccess))
         rc = cuda_fail(cudaGetLastError(), "model_matvec upload");
-    const bool batched = mode != 1 && m->use_fast_gemv && batch >= GEMM_MIN_ROWS && gemm_supported(W, batch);
+    const bool batched = mode != 1 && m->use_fast_gemv && batch >= 2 && gemm_supported(W, batch) &&
+                         (batch >= GEMM_MIN_ROWS || !gemv_fast_supported(W, batch));
     if (rc == LLMDOT_OK && batched) rc = ensure_workspace(m, batch);
     if (rc == LLMDOT_OK) {
         if (batched) {

@@ -321,7 +321,7 @@ int ensure_workspace(llmdot_model *m, int batch)
     LLMDOT_CUDA_TRY(cudaMemset(w.counters, 0, sizeof(int) * B * c.heads_kv));
     LLMDOT_CUDA_TRY(cudaMemset(w.err, 0, sizeof(int)));
     LLMDOT_CUDA_TRY(cudaMemset(w.hist_step, 0, sizeof(int32_t)));
-    if (batch >= GEMM_MIN_ROWS) {
+    if (batch >= 2) {  // the batched kernel also takes 2..4 rows whose input does not fit the matvec's smem
         const int cols_max = std::max(std::max(c.hidden, (int)qDim), c.ffn);
         const int rows_max = std::max(std::max(c.hidden, (int)(qDim + 2 * kvDim)), c.ffn);
         LLMDOT_TRY(gemm_scratch_alloc(w.gemm, cols_max, rows_max, a));
@@ -359,7 +359,7 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
 
     // y = epilogue(W . [rmsnorm](x)); the tensor-core kernel fuses the norm and the epilogue,
     // the generic kernel runs them as separate launches.
-    const bool batched = fast && batch >= GEMM_MIN_ROWS && batch <= GEMM_MAX_ROWS && w.gemm.xf[0] != nullptr;
+    const bool batched = fast && batch <= GEMM_MAX_ROWS && w.gemm.xf[0] != nullptr;
     auto mv = [&](const DevMat &W, const DevMat *W1, const float *x, int ldx, const float *norm_w, float *y, int ldy,
                   int mode) -> int {
         if (fast && gemv_fast_supported(W, batch) && (!W1 || gemv_fast_supported(*W1, batch)))

@@ -10,7 +10,7 @@ namespace llmdot {
 
 struct DevMat;
 
-constexpr int GEMM_MIN_ROWS = 5;   // below this the matvec kernel (gemv.cu) is used
+constexpr int GEMM_MIN_ROWS = 5;   // below this the matvec kernel (gemv.cu), where its input fits
 constexpr int GEMM_MAX_ROWS = 32;
 
 // Activation fragments of one input, built once and shared by every matrix that reads it.

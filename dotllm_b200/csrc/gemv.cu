@@ -159,6 +159,7 @@ struct GemvArgs {
     const float *norm_w;  // fused RMSNorm weight (nullable)
     float eps;
     int need_q4, need_q6;  // x layouts the segments use
+    int lks;               // log2 of the K split: each row tile is 2^lks units of consecutive super-blocks
 };
 
 // Tiles in flight per warp: each warp streams its tiles through a private ring of RING (2 or 3)
@@ -222,14 +223,17 @@ __device__ __forceinline__ int find_seg(const GemvArgs &a, int gt, int &rt)
     return s;
 }
 
-constexpr int GEMV_WARPS = 16;  // warps per CTA (one CTA per SM)
+#ifndef LLMDOT_GEMV_WARPS
+#define LLMDOT_GEMV_WARPS 16
+#endif
+constexpr int GEMV_WARPS = LLMDOT_GEMV_WARPS;  // warps per CTA (one CTA per SM)
 
 // Shared memory of one CTA (byte offsets; all 16-byte aligned).
 struct GemvSmem {
     int xs4, xs6, S, P, red, stat, wred, ring, total, slot;  // byte offsets (slot: bytes per ring slot)
 };
 __host__ __device__ inline GemvSmem gemv_layout(int nv, int nsb, int nmat, bool q4, bool q6, int max_rt_cta,
-                                                int ring)
+                                                int ks, int ring)
 {
     GemvSmem L;
     const int xsz = nsb * 64 * nv * 16;
@@ -242,8 +246,8 @@ __host__ __device__ inline GemvSmem gemv_layout(int nv, int nsb, int nmat, bool 
     o += q4 ? nv * nsb * 8 * 4 : 0;
     L.P = o;
     o += q4 ? nv * nsb * 32 * 4 : 0;
-    L.red = o;  // [max_rt_cta][nmat][GEMV_WARPS][16][nv]
-    o += (max_rt_cta * nmat * GEMV_WARPS * 16 * nv * 4 + 15) / 16 * 16;
+    L.red = o;  // unit partials [max_rt_cta][ks][nmat][16][nv]
+    o += (max_rt_cta * ks * nmat * 16 * nv * 4 + 15) / 16 * 16;
     L.stat = o;
     o += 16 * ((2 * nv * 4 + 15) / 16);
     L.wred = o;
@@ -255,14 +259,38 @@ __host__ __device__ inline GemvSmem gemv_layout(int nv, int nsb, int nmat, bool 
     return L;
 }
 
-template <int NV, int MODE, int RING>
+// Where a unit's tiles are: unit u of a CTA is K part (u mod ks) of its row tile (u / ks);
+// its tiles run over matrix 0 then matrix 1 (the *_MUL epilogues), super-blocks [sb_lo, sb_hi).
+struct UnitPos {
+    const uint8_t *p0, *p1;  // first tile of the unit in matrix 0 / 1
+    int tb, qt, rtl, kp, sb_lo, n;  // tile bytes, type, local row tile, K part, first super-block, tiles per matrix
+};
+template <int NMAT>
+__device__ __forceinline__ void unit_pos(const GemvArgs &a, int rt_lo, int u, UnitPos &P)
+{
+    const int ks1 = (1 << a.lks) - 1;
+    P.rtl = u >> a.lks;
+    P.kp = u & ks1;
+    P.sb_lo = (P.kp * a.nsb) >> a.lks;
+    P.n = (((P.kp + 1) * a.nsb) >> a.lks) - P.sb_lo;
+    int rt;
+    const GemvSeg &sg = a.seg[find_seg(a, rt_lo + P.rtl, rt)];
+    P.qt = sg.qt;
+    P.tb = sg.qt == QT_Q4K ? Q4K_TILE : Q6K_TILE;
+    const size_t off = ((size_t)rt * a.nsb + P.sb_lo) * P.tb;
+    P.p0 = sg.w + off;
+    P.p1 = NMAT == 2 ? sg.w1 + off : nullptr;
+}
+
+// TM: 0 every segment Q4_K, 1 every segment Q6_K, 2 mixed (the type is read per unit).
+template <int NV, int MODE, int RING, int TM>
 __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, int max_rt_cta)
 {
     constexpr int NMAT = (MODE >= GM_SILU_MUL) ? 2 : 1;
     constexpr int NT = GEMV_WARPS * 32;
     extern __shared__ __align__(16) uint8_t smem[];
-    const int nsb = a.nsb, cols = nsb * 256;
-    const GemvSmem L = gemv_layout(NV, nsb, NMAT, a.need_q4, a.need_q6, max_rt_cta, RING);
+    const int nsb = a.nsb, cols = nsb * 256, ks = 1 << a.lks;
+    const GemvSmem L = gemv_layout(NV, nsb, NMAT, a.need_q4, a.need_q6, max_rt_cta, ks, RING);
     uint4 *xs4 = (uint4 *)(smem + L.xs4), *xs6 = (uint4 *)(smem + L.xs6);
     float *S = (float *)(smem + L.S), *P = (float *)(smem + L.P), *red = (float *)(smem + L.red);
     float *stat = (float *)(smem + L.stat), *wred = (float *)(smem + L.wred);
@@ -270,29 +298,28 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
     const int g = lane >> 2, t = lane & 3;
     uint8_t *ring = smem + L.ring + (size_t)warp * RING * L.slot;
     uint64_t *mb = (uint64_t *)smem + warp * 3;  // this warp's slot mbarriers
-    // this CTA owns row tiles [rt_lo, rt_hi) of the concatenated segments; its flat tile list
-    // is (row tile, matrix, super-block), and warp w takes tiles w, w+16, ...
+    // this CTA owns row tiles [rt_lo, rt_hi) of the concatenated segments, i.e. units
+    // [0, nrt * ks); warp w takes units w, w + 16, ...
     const int rt_lo = (int)((long long)blockIdx.x * a.rt_total / gridDim.x);
     const int rt_hi = (int)((long long)(blockIdx.x + 1) * a.rt_total / gridDim.x);
-    const int nrt = rt_hi - rt_lo, per_rt = NMAT * nsb, ntile = nrt * per_rt;
-    const int F = ntile > warp ? (ntile - warp + GEMV_WARPS - 1) / GEMV_WARPS : 0;
-    // issue cursor: tile f = row tile rtl, position rem (matrix rem / nsb, super-block rem % nsb)
-    int i_f = 0, i_rtl = warp / per_rt, i_rem = warp % per_rt;
-    auto issue = [&]() {  // next tile of the warp into slot i_f % RING
-        if (i_f >= F) return;
+    const int nrt = rt_hi - rt_lo, nunit = nrt * ks;
+    // issue cursor: unit iu, tile ij of it, ring slot islot; i_n tiles issued so far
+    int iu = warp, ij = 0, islot = 0, i_n = 0;
+    UnitPos IP;
+    if (iu < nunit) unit_pos<NMAT>(a, rt_lo, iu, IP);
+    auto issue = [&]() {
+        if (iu >= nunit) return;
         if (lane == 0) {
-            int rt;
-            const GemvSeg &sg = a.seg[find_seg(a, rt_lo + i_rtl, rt)];
-            const uint32_t tb = sg.qt == QT_Q4K ? Q4K_TILE : Q6K_TILE;
-            const int mat = i_rem >= nsb ? 1 : 0, sb = i_rem - mat * nsb;
-            issue_bulk(ring + (i_f % RING) * L.slot, (mat ? sg.w1 : sg.w) + ((size_t)rt * nsb + sb) * tb, tb,
-                       mb + i_f % RING);
+            const int mat = (NMAT == 2 && ij >= IP.n) ? 1 : 0;
+            issue_bulk(ring + islot * L.slot, (mat ? IP.p1 : IP.p0) + (size_t)(ij - mat * IP.n) * IP.tb, IP.tb,
+                       mb + islot);
         }
-        i_f++;
-        i_rem += GEMV_WARPS;
-        while (i_rem >= per_rt) {
-            i_rem -= per_rt;
-            i_rtl++;
+        if (++islot == RING) islot = 0;
+        i_n++;
+        if (++ij == NMAT * IP.n) {
+            ij = 0;
+            iu += GEMV_WARPS;
+            if (iu < nunit) unit_pos<NMAT>(a, rt_lo, iu, IP);
         }
     };
     if (tid < GEMV_WARPS * 3) gmbar_init((uint64_t *)smem + tid);
@@ -329,7 +356,6 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
                 wred[warp * 2 * NV + v] = ss[v];
                 wred[warp * 2 * NV + NV + v] = mx[v];
             }
-        for (int i = tid; i < nrt * NMAT * GEMV_WARPS * 16 * NV; i += NT) red[i] = 0.0f;
         __syncthreads();
         if (tid < NV) {
             float s = 0.0f, m = 0.0f;
@@ -410,66 +436,83 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
     }
     __syncthreads();
 
-    // ---- streaming loop: no CTA-wide barrier inside, warps run independently
-    const bool bact = g < 2 * NV;  // lanes whose B column is a real (vector, part)
-    const int bv = g >> 1, bpart = g & 1;
-    int c_rtl = warp / per_rt, c_rem = warp % per_rt;  // consume cursor
+    // ---- streaming loop: no CTA-wide barrier inside, warps run independently.  A warp sums a
+    // whole (unit, matrix) in registers and stores it once; nothing else is written per tile.
+    const int bv = min(g >> 1, NV - 1), bpart = g & 1;  // this lane's B column (vector, part)
+    int cu = warp, cj = 0, cslot = 0, c_n = 0;
+    uint32_t cpar = 0;
+    UnitPos CP;
+    if (cu < nunit) unit_pos<NMAT>(a, rt_lo, cu, CP);
+    float acc0 = 0.0f, acc1 = 0.0f;  // rows g, g+8 for vector t (MMA columns 2t, 2t+1)
+    float corr0[NV], corr1[NV];
+#pragma unroll
+    for (int v = 0; v < NV; v++) corr0[v] = corr1[v] = 0.0f;
     bool ok = true;
-    int f_fail = F;
-    for (int f = 0; f < F; f++) {
-        const int rtl = c_rtl, mat = c_rem >= nsb ? 1 : 0, sb = c_rem - mat * nsb;
-        c_rem += GEMV_WARPS;
-        while (c_rem >= per_rt) {
-            c_rem -= per_rt;
-            c_rtl++;
-        }
-        if (!gmbar_wait(mb + f % RING, (uint32_t)(f / RING) & 1u)) {
+    while (cu < nunit) {
+        if (!gmbar_wait(mb + cslot, cpar)) {
             ok = false;
-            f_fail = f;
             if (lane == 0) atomicExch(&g_gemv_timeout, 1);
             break;
         }
-        int rt;
-        const int qt = a.seg[find_seg(a, rt_lo + rtl, rt)].qt;
-        float acc0 = 0.0f, acc1 = 0.0f;  // rows g, g+8 for vector t (MMA columns 2t, 2t+1)
-        float corr0[NV], corr1[NV];
-#pragma unroll
-        for (int v = 0; v < NV; v++) corr0[v] = corr1[v] = 0.0f;
+        const int qt = TM == 2 ? CP.qt : TM;
         TileRegs T;
-        read_tile(T, ring + (f % RING) * L.slot, qt, lane);
-        __syncwarp();  // the tile is in registers: refill its slot with tile f + RING before the math
-        issue();
-        if (qt == QT_Q4K) q4k_tile<NV>(T, xs4, S, nsb, sb, t, bact, bv, bpart, acc0, acc1, corr0, corr1);
-        else q6k_tile<NV>(T, xs6, sb, t, bact, bv, bpart, acc0, acc1);
-        if (qt == QT_Q4K) {
-            // offset term: each lane of a row group covered 2 sub-blocks; sum over the group
-            float k0 = 0.0f, k1 = 0.0f;
-#pragma unroll
-            for (int v = 0; v < NV; v++) {
-                float c0v = corr0[v], c1v = corr1[v];
-                c0v += __shfl_xor_sync(0xffffffffu, c0v, 1);
-                c0v += __shfl_xor_sync(0xffffffffu, c0v, 2);
-                c1v += __shfl_xor_sync(0xffffffffu, c1v, 1);
-                c1v += __shfl_xor_sync(0xffffffffu, c1v, 2);
-                if (v == t) {
-                    k0 = c0v;
-                    k1 = c1v;
-                }
-            }
-            acc0 -= k0;
-            acc1 -= k1;
+        read_tile(T, ring + cslot * L.slot, qt, lane);
+        __syncwarp();  // the tile is in registers: refill its slot before the math
+        if (++cslot == RING) {
+            cslot = 0;
+            cpar ^= 1u;
         }
-        if (t < NV) {  // this warp's running partial for (row tile, matrix); only this warp writes it
-            float *rp = red + ((size_t)((rtl * NMAT + mat) * GEMV_WARPS + warp) * 16) * NV;
-            rp[g * NV + t] += acc0;
-            rp[(g + 8) * NV + t] += acc1;
+        c_n++;
+        issue();
+        const int mat = (NMAT == 2 && cj >= CP.n) ? 1 : 0;
+        const int sb = CP.sb_lo + cj - mat * CP.n;
+        if (TM != 1 && qt == QT_Q4K) q4k_tile<NV>(T, xs4, S, nsb, sb, t, bv, bpart, acc0, acc1, corr0, corr1);
+        if (TM != 0 && qt == QT_Q6K) q6k_tile<NV>(T, xs6, sb, t, bv, bpart, acc0, acc1);
+        ++cj;
+        if (cj == CP.n || cj == NMAT * CP.n) {  // end of this (unit, matrix): one store of its partial
+            if (TM != 1 && qt == QT_Q4K) {
+                // offset term: each lane of a row group covered 2 sub-blocks; sum over the group
+                float k0 = 0.0f, k1 = 0.0f;
+#pragma unroll
+                for (int v = 0; v < NV; v++) {
+                    float c0v = corr0[v], c1v = corr1[v];
+                    c0v += __shfl_xor_sync(0xffffffffu, c0v, 1);
+                    c0v += __shfl_xor_sync(0xffffffffu, c0v, 2);
+                    c1v += __shfl_xor_sync(0xffffffffu, c1v, 1);
+                    c1v += __shfl_xor_sync(0xffffffffu, c1v, 2);
+                    if (v == t) {
+                        k0 = c0v;
+                        k1 = c1v;
+                    }
+                    corr0[v] = corr1[v] = 0.0f;
+                }
+                acc0 -= k0;
+                acc1 -= k1;
+            }
+            if (t < NV) {
+                float *rp = red + ((size_t)((CP.rtl * ks + CP.kp) * NMAT + mat) * 16) * NV;
+                rp[g * NV + t] = acc0;
+                rp[(g + 8) * NV + t] = acc1;
+            }
+            acc0 = acc1 = 0.0f;
+            if (cj == NMAT * CP.n) {
+                cj = 0;
+                cu += GEMV_WARPS;
+                if (cu < nunit) unit_pos<NMAT>(a, rt_lo, cu, CP);
+            }
         }
     }
     if (!ok)  // bounded drain of this warp's copies still in flight, then leave the output untouched
-        for (int k = f_fail; k < i_f; k++) gmbar_wait(mb + k % RING, (uint32_t)(k / RING) & 1u);
+        for (int k = c_n; k < i_n; k++) {
+            gmbar_wait(mb + cslot, cpar);
+            if (++cslot == RING) {
+                cslot = 0;
+                cpar ^= 1u;
+            }
+        }
     if (!__syncthreads_and(ok)) return;
 
-    // ---- epilogue: every (row tile, row, vector) of the CTA, warps summed in a fixed order
+    // ---- epilogue: every (row tile, row, vector) of the CTA, K parts summed in a fixed order
     for (int it = tid; it < nrt * 16 * NV; it += NT) {
         const int rtl = it / (16 * NV), rr = (it / NV) % 16, v = it % NV;
         int rt;
@@ -480,7 +523,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
 #pragma unroll
         for (int mtx = 0; mtx < NMAT; mtx++) {
             float s = 0.0f;
-            for (int w = 0; w < GEMV_WARPS; w++) s += red[(((rtl * NMAT + mtx) * GEMV_WARPS + w) * 16 + rr) * NV + v];
+            for (int kp = 0; kp < ks; kp++) s += red[(((rtl * ks + kp) * NMAT + mtx) * 16 + rr) * NV + v];
             o[mtx] = s * (1.0f / stat[NV + v]);
         }
         float *yp = sg.y + (size_t)v * sg.ldy + row;
@@ -497,11 +540,11 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
 constexpr int GEMV_SMEM_MAX = 220 * 1024;
 
 // Shared memory needed for `nv` rows through matrices with nsb super-blocks (worst case over the
-// row-tile blocking); 0 when it does not fit even with a 2-deep ring.
-static size_t gemv_need(int nv, int nsb, int nmat, bool q4, bool q6, int max_rt, int *ring)
+// row-tile blocking, K split 2^lks); 0 when it does not fit even with a 2-deep ring.
+static size_t gemv_need(int nv, int nsb, int nmat, bool q4, bool q6, int max_rt, int lks, int *ring)
 {
     for (int r = 3; r >= 2; r--) {
-        const GemvSmem L = gemv_layout(nv, nsb, nmat, q4, q6, max_rt, r);
+        const GemvSmem L = gemv_layout(nv, nsb, nmat, q4, q6, max_rt, 1 << lks, r);
         if (L.total <= GEMV_SMEM_MAX) {
             if (ring) *ring = r;
             return (size_t)L.total;
@@ -526,13 +569,13 @@ bool gemv_fast_supported(const DevMat &W, int nv)
 {
     if (!W.tiled || nv < 1 || nv > 4) return false;
     const bool q4 = W.type == T_Q4_K;
-    return gemv_need(nv, W.cols / 256, 2, q4, !q4, 4, nullptr) != 0;
+    return gemv_need(nv, W.cols / 256, 2, q4, !q4, 4, 0, nullptr) != 0;
 }
 
-template <int NV, int MODE, int RING> static int launch_r(const GemvArgs &a, int grid, int max_rt, size_t sm, bool pdl,
-                                                          cudaStream_t st)
+template <int NV, int MODE, int RING, int TM>
+static int launch_r(const GemvArgs &a, int grid, int max_rt, size_t sm, bool pdl, cudaStream_t st)
 {
-    auto kern = gemv_mma_kernel<NV, MODE, RING>;
+    auto kern = gemv_mma_kernel<NV, MODE, RING, TM>;
     static bool attr_set = false;  // once per instantiation
     if (!attr_set) {
         LLMDOT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_MAX));
@@ -542,23 +585,38 @@ template <int NV, int MODE, int RING> static int launch_r(const GemvArgs &a, int
     return LLMDOT_OK;
 }
 
-template <int NV, int MODE> static int launch_t(const GemvArgs &a, bool pdl, cudaStream_t st)
+template <int NV, int MODE, int RING> static int launch_tm(const GemvArgs &a, int grid, int max_rt, size_t sm, bool pdl,
+                                                           cudaStream_t st)
+{
+    if (a.need_q4 && a.need_q6) return launch_r<NV, MODE, RING, 2>(a, grid, max_rt, sm, pdl, st);
+    if (a.need_q6) return launch_r<NV, MODE, RING, QT_Q6K>(a, grid, max_rt, sm, pdl, st);
+    return launch_r<NV, MODE, RING, QT_Q4K>(a, grid, max_rt, sm, pdl, st);
+}
+
+template <int NV, int MODE> static int launch_t(GemvArgs a, bool pdl, cudaStream_t st)
 {
     constexpr int NMAT = (MODE >= GM_SILU_MUL) ? 2 : 1;
     // one CTA per SM (148 on B200), each with a contiguous block of row tiles; more CTAs only
-    // when the per-row-tile partial sums would not fit in shared memory
+    // when the per-unit partial sums would not fit in shared memory
     int grid = a.rt_total < 148 ? a.rt_total : 148;
     int max_rt = (a.rt_total + grid - 1) / grid, ring = 0;
-    size_t sm = gemv_need(NV, a.nsb, NMAT, a.need_q4, a.need_q6, max_rt, &ring);
+    // K split: enough units per CTA (about 6 per warp) that warps finish together, but at least
+    // one super-block per unit
+    const int min_rt = a.rt_total / grid;
+    int lks = 0;
+    while ((2 << lks) <= a.nsb && (min_rt << lks) < 6 * GEMV_WARPS) lks++;
+    size_t sm = gemv_need(NV, a.nsb, NMAT, a.need_q4, a.need_q6, max_rt, lks, &ring);
+    while (sm == 0 && lks > 0) sm = gemv_need(NV, a.nsb, NMAT, a.need_q4, a.need_q6, max_rt, --lks, &ring);
     while (sm == 0 && grid < a.rt_total) {
         grid += 148;
         if (grid > a.rt_total) grid = a.rt_total;
         max_rt = (a.rt_total + grid - 1) / grid;
-        sm = gemv_need(NV, a.nsb, NMAT, a.need_q4, a.need_q6, max_rt, &ring);
+        sm = gemv_need(NV, a.nsb, NMAT, a.need_q4, a.need_q6, max_rt, lks, &ring);
     }
     if (sm == 0) return fail(LLMDOT_E_UNSUPPORTED, "fast matvec: shared memory");
-    if (ring == 3) return launch_r<NV, MODE, 3>(a, grid, max_rt, sm, pdl, st);
-    return launch_r<NV, MODE, 2>(a, grid, max_rt, sm, pdl, st);
+    a.lks = lks;
+    if (ring == 3) return launch_tm<NV, MODE, 3>(a, grid, max_rt, sm, pdl, st);
+    return launch_tm<NV, MODE, 2>(a, grid, max_rt, sm, pdl, st);
 }
 
 template <int MODE> static int launch_mode(const GemvArgs &a, int nv, bool pdl, cudaStream_t st)

@@ -8,7 +8,9 @@
 //   Q6_K (3360 bytes): planes 0..5 = low nibbles / high bits of rows g and g+8,
 //                      int8 scales at 3072 + g*32, fp16 d at 3328 + g*4.
 // The activation enters as fp16 hi/lo pairs (B operand columns 2v, 2v+1) of an exactly
-// power-of-two-scaled x, so every product is exact and the sums are fp32.
+// power-of-two-scaled x, so every product is exact and the sums are fp32.  Lanes whose B column
+// is past the last vector (g >= 2*NV) load the last vector's fragment again: their C columns are
+// never read, and an unconditional shared load costs no predication.
 #pragma once
 #include "common.cuh"
 
@@ -85,7 +87,7 @@ __device__ __forceinline__ void read_tile(TileRegs &T, const uint8_t *slot, int 
 
 template <int NV>
 __device__ __forceinline__ void q4k_tile(const TileRegs &T, const uint4 *__restrict__ xs, const float *__restrict__ S,
-                                         int nsb, int sb, int t, bool bact, int bv, int bpart, float &acc0, float &acc1,
+                                         int nsb, int sb, int t, int bv, int bpart, float &acc0, float &acc1,
                                          float *corr0, float *corr1)
 {
     float d_r[2], dm_r[2];
@@ -125,8 +127,7 @@ __device__ __forceinline__ void q4k_tile(const TileRegs &T, const uint4 *__restr
     for (int w = 0; w < 8; w++) {
         const int j = w >> 2;  // sub-block 2t + j
         const uint32_t W0 = (&T.r[j].x)[w & 3], W1 = (&T.r[2 + j].x)[w & 3];
-        uint4 b = make_uint4(0, 0, 0, 0);
-        if (bact) b = xs[xunit<NV>(sb, t, w, bv, bpart)];
+        const uint4 b = xs[xunit<NV>(sb, t, w, bv, bpart)];
         float *ca = c[(2 * w) % QC], *cb = c[(2 * w + 1) % QC];
         uint32_t a0 = hfma2(and_or(W0, 0x000F000Fu, 0x64006400u), sc2[0][j], nsc2[0][j]);
         uint32_t a1 = hfma2(and_or(W1, 0x000F000Fu, 0x64006400u), sc2[1][j], nsc2[1][j]);
@@ -159,8 +160,8 @@ __device__ __forceinline__ void q4k_tile(const TileRegs &T, const uint4 *__restr
 }
 
 template <int NV>
-__device__ __forceinline__ void q6k_tile(const TileRegs &T, const uint4 *__restrict__ xs, int sb, int t, bool bact,
-                                         int bv, int bpart, float &acc0, float &acc1)
+__device__ __forceinline__ void q6k_tile(const TileRegs &T, const uint4 *__restrict__ xs, int sb, int t, int bv,
+                                         int bpart, float &acc0, float &acc1)
 {
     const float d0 = half_bits(T.r[8].x & 0xFFFF);
     const float d1 = half_bits(T.r[8].x >> 16);
@@ -183,11 +184,8 @@ __device__ __forceinline__ void q6k_tile(const TileRegs &T, const uint4 *__restr
                 av[kk * 2 + h] = hsub2(q, 0x64206420u);  // - (1024 + 32)
             }
         }
-        uint2 b = make_uint2(0, 0);
-        if (bact) {
-            const uint4 bb = xs[xunit<NV>(sb, t, w, bv, bpart)];
-            b = (s & 1) ? make_uint2(bb.z, bb.w) : make_uint2(bb.x, bb.y);
-        }
+        const uint4 bb = xs[xunit<NV>(sb, t, w, bv, bpart)];
+        const uint2 b = (s & 1) ? make_uint2(bb.z, bb.w) : make_uint2(bb.x, bb.y);
         mma_f16(c0, c1, c2, c3, av[0], av[1], av[2], av[3], b.x, b.y);
         const float s0 = d0 * (float)(int8_t)((&T.r[6].x)[s >> 2] >> (8 * (s & 3)));
         const float s1 = d1 * (float)(int8_t)((&T.r[7].x)[s >> 2] >> (8 * (s & 3)));

@@ -536,8 +536,7 @@ __device__ bool mv_tiles(const StepArgs &a, const StepPhase &ph, int lo, int hi,
 {
     unsigned long long t_wait = 0, t_comp = 0, n_tiles = 0;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
-    const bool bact = g < 2 * NV;  // lanes whose B column is a real (vector, part)
-    const int bv = g >> 1, bpart = g & 1;
+    const int bv = min(g >> 1, NV - 1), bpart = g & 1;  // this lane's B column (vector, part)
     const int ks = ph.ks, tpu = ph.tpu, nsb = ph.nsb;  // registers: the loop stores would force reloads
     const int U = (hi - lo) * ks;
     for (int u = warp; u < U; u += SW) {
@@ -560,8 +559,8 @@ __device__ bool mv_tiles(const StepArgs &a, const StepPhase &ph, int lo, int hi,
             __syncwarp();  // the tile is in registers: refill its slot before the math
             cp.step(a.ring);
             issue_next(a, hdr, cur, warp, lane, ring_w, mb_w, ip);
-            if (qt == QT_Q4K) q4k_tile<NV>(T, L.xs4, L.S, nsb, sb, t, bact, bv, bpart, acc0, acc1, corr0, corr1);
-            else q6k_tile<NV>(T, L.xs6, sb, t, bact, bv, bpart, acc0, acc1);
+            if (qt == QT_Q4K) q4k_tile<NV>(T, L.xs4, L.S, nsb, sb, t, bv, bpart, acc0, acc1, corr0, corr1);
+            else q6k_tile<NV>(T, L.xs6, sb, t, bv, bpart, acc0, acc1);
             if (tr) {
                 t_wait += w1 - w0;
                 t_comp += gtimer() - w1;

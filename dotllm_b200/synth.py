@@ -122,6 +122,15 @@ TEST_CONFIGS: Dict[str, SynthConfig] = {
         prompt_len=8, decode_len=16),
 }
 
+# Full-width, few-layer copies of the BASELINE models: every matrix, head and vocabulary shape
+# of the real config (head_dim 96 / 128 / 256, fused QKV, 256000-row tied head) at a size the
+# CPU oracle checks in seconds.  Prompts of 40 tokens cross one 32-token prefill chunk; the
+# Gemma copy narrows its sliding window so that the window is active within the test.
+for _n, _kw in (("llama1b", {}), ("phi3mini", {}), ("gemma2b", {"sliding_window": 32}), ("llama8b", {"layers": 1})):
+    _c = replace(CONFIGS[_n], name=f"{_n}-shape", prompt_len=40, decode_len=16, batch=1, **{"layers": 2, **_kw})
+    TEST_CONFIGS[_c.name] = _c
+del _n, _kw, _c
+
 ALL_CONFIGS = {**CONFIGS, **TEST_CONFIGS}
 
 
@@ -199,12 +208,23 @@ def tensor_bytes(cfg: SynthConfig, info: TensorInfo, role: str, idx: int) -> byt
         return w.astype("<f4").tobytes()
     cols, rows = info.dims[0], info.dims[1]
     chunk = max(1, (1 << 24) // cols)
-    parts = []
-    for r0 in range(0, rows, chunk):
-        n = min(chunk, rows - r0)
-        x = rng.standard_normal((n, cols), dtype=np.float32) * np.float32(0.02)
-        parts.append(quantize(x, info.ggml_type).tobytes())
-    return b"".join(parts)
+    starts = range(0, rows, chunk)
+    if len(starts) == 1:
+        x = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)
+        return quantize(x, info.ggml_type).tobytes()
+    # the random stream is drawn in order; quantisation of the drawn chunks (row-independent,
+    # numpy releases the GIL) runs on threads, so the bytes do not depend on the thread count
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        futs, parts = [], []
+        for r0 in starts:
+            n = min(chunk, rows - r0)
+            x = rng.standard_normal((n, cols), dtype=np.float32) * np.float32(0.02)
+            futs.append(ex.submit(lambda a: quantize(a, info.ggml_type).tobytes(), x))
+            if len(futs) - len(parts) > 16:  # bound the drawn chunks held in memory
+                parts.append(futs[len(parts)].result())
+        parts += [f.result() for f in futs[len(parts):]]
+        return b"".join(parts)
 
 
 def cache_dir() -> str:
