@@ -28,6 +28,9 @@ struct AttnShape {
 // part_m/part_s [batch][heads][max_ctx/KV_PAGE], part_o [..][head_dim], counters
 // [batch][heads_kv] (zero on entry, left zero).  append_first: append every row's k/v in a
 // separate kernel before the attention, for rows of one session in one step (prompt chunks).
+// LLMDOT_E_TIMEOUT (and the flag cleared) when a bounded wait of the attention kernel gave up.
+int attention_timeout_check();
+
 int launch_attention_step(const float *q, int ldq, const float *k, const float *v, int ldkv, const int32_t *pos,
                           const float *cos_t, const float *sin_t, const KvView *views, int layer, int kv_type,
                           const AttnShape &sh, int batch, float *scores, float *part_m, float *part_s, float *part_o,

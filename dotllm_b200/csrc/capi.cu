@@ -634,6 +634,10 @@ extern "C" int llmdot_cuda_model_free(llmdot_model *m)
 {
     if (!m) return LLMDOT_OK;
     cudaSetDevice(m->device);
+    // sessions still open keep their cache until llmdot_cuda_session_free; every other call on
+    // them fails instead of touching the freed model
+    for (llmdot_session *s : m->sessions) s->m = nullptr;
+    m->sessions.clear();
     drop_graphs(m);
     model_destroy(m);
     return LLMDOT_OK;
@@ -647,7 +651,7 @@ extern "C" int llmdot_cuda_session_create(llmdot_model *m, int max_ctx, int kv_t
     LLMDOT_CUDA_TRY(cudaSetDevice(m->device));
     if (max_ctx <= 0 || max_ctx > m->cfg.context) max_ctx = m->cfg.context;
     auto *s = new llmdot_session();
-    s->m = m;
+    s->device = m->device;
     s->kv_type = kv_type;
     s->n_pages = (max_ctx + KV_PAGE - 1) / KV_PAGE;
     s->max_ctx = max_ctx;
@@ -665,6 +669,8 @@ extern "C" int llmdot_cuda_session_create(llmdot_model *m, int max_ctx, int kv_t
     for (int i = 0; i < s->n_pages; i++) pt[i] = i;
     LLMDOT_CUDA_TRY(cudaMemcpy(s->pages, pt.data(), sizeof(int32_t) * s->n_pages, cudaMemcpyHostToDevice));
     s->view = {s->k, s->v, s->pages, layer_stride};
+    s->m = m;
+    m->sessions.push_back(s);
     *out = s;
     return LLMDOT_OK;
 }
@@ -686,8 +692,14 @@ extern "C" int llmdot_cuda_session_position(const llmdot_session *s, int *pos)
 extern "C" int llmdot_cuda_session_free(llmdot_session *s)
 {
     if (!s) return LLMDOT_OK;
-    cudaSetDevice(s->m->device);
-    cudaStreamSynchronize(s->m->stream);
+    if (s->m) {
+        auto &v = s->m->sessions;
+        v.erase(std::remove(v.begin(), v.end(), s), v.end());
+        cudaSetDevice(s->m->device);
+        cudaStreamSynchronize(s->m->stream);
+    } else {
+        cudaSetDevice(s->device);
+    }
     if (s->k) cudaFree(s->k);
     if (s->v) cudaFree(s->v);
     if (s->pages) cudaFree(s->pages);
@@ -738,6 +750,7 @@ static int read_logits(llmdot_model *m, int batch, int row, float *host, cudaStr
 static int check_err_flag(llmdot_model *m)
 {
     LLMDOT_TRY(gemv_timeout_check());
+    LLMDOT_TRY(attention_timeout_check());
     int e = 0;
     LLMDOT_CUDA_TRY(cudaMemcpy(&e, m->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {
@@ -755,6 +768,7 @@ extern "C" int llmdot_cuda_prefill(llmdot_session *s, const int32_t *tokens, int
 {
     if (!s || (!tokens && n > 0) || n < 0) return fail(LLMDOT_E_INVALID, "prefill: bad arguments");
     llmdot_model *m = s->m;
+    if (!m) return fail(LLMDOT_E_INVALID, "prefill: the session's model was freed");
     LLMDOT_CUDA_TRY(cudaSetDevice(m->device));
     if (s->pos + n > s->max_ctx) return fail(LLMDOT_E_INVALID, "prefill: context length exceeded");
     if (n == 0) return LLMDOT_OK;
@@ -824,7 +838,7 @@ extern "C" int llmdot_cuda_decode(llmdot_session **sessions, int batch, const in
 {
     if (!sessions || batch <= 0 || !tokens || !next_tokens) return fail(LLMDOT_E_INVALID, "decode: bad arguments");
     llmdot_model *m = sessions[0] ? sessions[0]->m : nullptr;
-    if (!m) return fail(LLMDOT_E_INVALID, "decode: null session");
+    if (!m) return fail(LLMDOT_E_INVALID, "decode: null session, or its model was freed");
     const int kv_type = sessions[0]->kv_type;
     for (int i = 0; i < batch; i++) {
         llmdot_session *s = sessions[i];
@@ -871,6 +885,7 @@ extern "C" int llmdot_cuda_generate(llmdot_session *s, const int32_t *prompt, in
     if (!s || !out_tokens || !n_out || max_tokens < 0 || n_prompt < 0 || (n_prompt > 0 && !prompt))
         return fail(LLMDOT_E_INVALID, "generate: bad arguments");
     llmdot_model *m = s->m;
+    if (!m) return fail(LLMDOT_E_INVALID, "generate: the session's model was freed");
     *n_out = 0;
     LLMDOT_TRY(llmdot_cuda_session_reset(s));  // InferenceEngine.cs:79
     int32_t next = 0;
@@ -915,7 +930,7 @@ extern "C" int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
     if (!sessions || batch <= 0 || !tokens || !out_tokens || n_steps < 0)
         return fail(LLMDOT_E_INVALID, "decode_steps: bad arguments");
     llmdot_model *m = sessions[0] ? sessions[0]->m : nullptr;
-    if (!m) return fail(LLMDOT_E_INVALID, "decode_steps: null session");
+    if (!m) return fail(LLMDOT_E_INVALID, "decode_steps: null session, or its model was freed");
     const int kv_type = sessions[0]->kv_type;
     for (int i = 0; i < batch; i++) {
         llmdot_session *s = sessions[i];
@@ -990,7 +1005,7 @@ extern "C" int llmdot_cuda_trace_step(llmdot_session **sessions, int batch, cons
 {
     if (!sessions || batch <= 0 || !tokens || !n_phases || !n_cta) return fail(LLMDOT_E_INVALID, "trace_step: bad arguments");
     llmdot_model *m = sessions[0] ? sessions[0]->m : nullptr;
-    if (!m) return fail(LLMDOT_E_INVALID, "trace_step: null session");
+    if (!m) return fail(LLMDOT_E_INVALID, "trace_step: null session, or its model was freed");
     const int kv_type = sessions[0]->kv_type;
     for (int i = 0; i < batch; i++) {
         llmdot_session *s = sessions[i];

@@ -9,6 +9,7 @@
 
 #include "engine.cuh"
 #include "gemv.cuh"
+#include "gemv_tile.cuh"
 #include "ops.cuh"
 #include "tp.cuh"
 
@@ -360,10 +361,26 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
     // y = epilogue(W . [rmsnorm](x)); the tensor-core kernel fuses the norm and the epilogue,
     // the generic kernel runs them as separate launches.
     const bool batched = fast && batch <= GEMM_MAX_ROWS && w.gemm.xf[0] != nullptr;
+    // the weights of the next matvec, handed to the current one for an L2 prefetch
+    auto tiled_bytes = [](const DevMat *W) -> unsigned long long {
+        if (!W || !W->tiled) return 0;
+        return (unsigned long long)((W->rows + 15) / 16) * (W->cols / 256) * (W->type == T_Q4_K ? Q4K_TILE : Q6K_TILE);
+    };
+    auto prefetch = [&](const DevMat *a, const DevMat *b = nullptr, const DevMat *d = nullptr,
+                        unsigned long long cap = ~0ull) {
+        GemvPrefetch pf = {};
+        const DevMat *ms[GEMV_PREFETCH_MAX] = {a, b, d};
+        for (int i = 0; i < GEMV_PREFETCH_MAX; i++) {
+            const bool i8 = ms[i] && batch <= 2 && ms[i]->tiled8;  // the copy it will read
+            pf.p[i] = ms[i] && ms[i]->tiled ? (i8 ? ms[i]->tiled8 : ms[i]->tiled) : nullptr;
+            pf.n[i] = pf.p[i] ? std::min(tiled_bytes(ms[i]), cap) : 0;
+        }
+        return pf;
+    };
     auto mv = [&](const DevMat &W, const DevMat *W1, const float *x, int ldx, const float *norm_w, float *y, int ldy,
-                  int mode) -> int {
+                  int mode, const GemvPrefetch *pf = nullptr) -> int {
         if (fast && gemv_fast_supported(W, batch) && (!W1 || gemv_fast_supported(*W1, batch)))
-            return launch_gemv_fast_ex(W, W1, norm_w, c.eps, x, ldx, batch, y, ldy, mode, st, pdl);
+            return launch_gemv_fast_ex(W, W1, norm_w, c.eps, x, ldx, batch, y, ldy, mode, st, pdl, pf);
         if (batched && gemm_supported(W, batch) && (!W1 || gemm_supported(*W1, batch))) {
             GemmInput in, in1;
             LLMDOT_TRY(gemm_prepare(x, ldx, batch, W.cols, norm_w, c.eps, W.type, 0, w.gemm, &in, st));
@@ -395,11 +412,22 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
     LLMDOT_TRY(launch_embed(m->emb.raw, m->emb.type, H, c.vocab, tokens, batch, c.emb_scale, w.h, H, w.err, st));
     for (int l = 0; l < c.layers; l++) {
         const LayerW &L = m->layers[l];
+        // L2 prefetches: each matvec pulls in the weights of the one after it (the attention
+        // sits between Q/K/V and the output projection)
+        const GemvPrefetch pf_o = prefetch(&L.o), pf_ffn = prefetch(&L.gate, &L.up), pf_down = prefetch(&L.down);
+        GemvPrefetch pf_next;
+        if (l + 1 < c.layers) {
+            const LayerW &N = m->layers[l + 1];
+            pf_next = N.qkv.valid() ? prefetch(&N.qkv) : prefetch(&N.q, &N.k, &N.v);
+        } else {
+            const DevMat &head = m->out.valid() ? m->out : m->emb;
+            pf_next = prefetch(&head, nullptr, nullptr, 64ull << 20);  // as much of the head as L2 keeps
+        }
         // ApplyNorm(attn_norm) :544-562 fused into the Q/K/V projections :321-353
         float *q, *k, *v;
         int ldq, ldkv;
         if (L.qkv.valid()) {
-            LLMDOT_TRY(mv(L.qkv, nullptr, w.h, H, L.attn_norm, w.qkv, qDim + 2 * kvDim, GEMV_STORE));
+            LLMDOT_TRY(mv(L.qkv, nullptr, w.h, H, L.attn_norm, w.qkv, qDim + 2 * kvDim, GEMV_STORE, &pf_o));
             q = w.qkv;
             k = w.qkv + qDim;
             v = w.qkv + qDim + kvDim;
@@ -411,7 +439,7 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
                 // Q, K and V share the normed input: one launch
                 const GemvTarget tg[3] = {{&L.q, nullptr, w.q, qDim}, {&L.k, nullptr, w.k, kvDim},
                                           {&L.v, nullptr, w.v, kvDim}};
-                qkv_rc = launch_gemv_multi(tg, 3, L.attn_norm, c.eps, w.h, H, batch, GEMV_STORE, pdl, st);
+                qkv_rc = launch_gemv_multi(tg, 3, L.attn_norm, c.eps, w.h, H, batch, GEMV_STORE, pdl, st, &pf_o);
                 if (qkv_rc != LLMDOT_OK && qkv_rc != LLMDOT_E_UNSUPPORTED) return qkv_rc;
             }
             if (qkv_rc != LLMDOT_OK && batched && gemm_supported(L.q, batch) && gemm_supported(L.k, batch) &&
@@ -453,16 +481,16 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
         // tensor parallel: rank 0 adds its partial onto the residual, the others store theirs, and
         // the all-reduce leaves h + the sum of the partials on every rank
         const int res_mode = (m->tp > 1 && m->tp_rank != 0) ? GEMV_STORE : GEMV_ADD;
-        LLMDOT_TRY(mv(L.o, nullptr, w.attn, qDim, nullptr, w.h, H, res_mode));
+        LLMDOT_TRY(mv(L.o, nullptr, w.attn, qDim, nullptr, w.h, H, res_mode, &pf_ffn));
         if (m->tp > 1) LLMDOT_TRY(tp_allreduce_sum(m, w.h, (size_t)batch * H, st));
-        if (gemma && L.post_attn) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_attn, w.h, H, H, batch, c.eps, st));
+        if (gemma && L.post_attn) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_attn, w.h, H, H, batch, c.eps, st, pdl));
         // FfnForward :452-487: ApplyNorm(ffn_norm ?? attn_norm), gate and up, act(gate)*up in one launch
         LLMDOT_TRY(mv(L.gate, &L.up, w.h, H, L.ffn_norm ? L.ffn_norm : L.attn_norm, w.gate, c.ffn,
-                      c.ffn_type == 2 ? GEMV_GELU_MUL : GEMV_SILU_MUL));
+                      c.ffn_type == 2 ? GEMV_GELU_MUL : GEMV_SILU_MUL, &pf_down));
         // down projection + residual add
-        LLMDOT_TRY(mv(L.down, nullptr, w.gate, c.ffn, nullptr, w.h, H, res_mode));
+        LLMDOT_TRY(mv(L.down, nullptr, w.gate, c.ffn, nullptr, w.h, H, res_mode, &pf_next));
         if (m->tp > 1) LLMDOT_TRY(tp_allreduce_sum(m, w.h, (size_t)batch * H, st));
-        if (gemma && L.post_ffw) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_ffw, w.h, H, H, batch, c.eps, st));
+        if (gemma && L.post_ffw) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_ffw, w.h, H, H, batch, c.eps, st, pdl));
     }
     if (flags & STEP_NO_HEAD) return LLMDOT_OK;  // prompt chunk before the last: no logits needed
     // ApplyFinalNorm :575-581 fused into ComputeLogits :583-602

@@ -20,6 +20,7 @@ struct DevMat {
     uint64_t rbytes = 0;
     uint8_t *raw = nullptr;
     uint8_t *tiled = nullptr;
+    uint8_t *tiled8 = nullptr;  // Q4_K only: the same tiles in the int8 tensor-core lane order
     bool valid() const { return raw != nullptr; }
     uint64_t bytes() const { return rbytes * (uint64_t)rows; }
 };
@@ -50,8 +51,10 @@ constexpr int HIST_STEPS = 4096;
 
 }  // namespace llmdot
 
+struct llmdot_session;
 struct llmdot_model {
     int device = 0;
+    std::vector<llmdot_session *> sessions;  // live sessions, detached when the model is freed
     llmdot_config cfg{};
     cudaStream_t stream = nullptr;
     std::vector<llmdot::LayerW> layers;
@@ -77,7 +80,8 @@ struct llmdot_model {
 };
 
 struct llmdot_session {
-    llmdot_model *m = nullptr;
+    llmdot_model *m = nullptr;  // null once the model was freed (the session then only accepts free)
+    int device = 0;
     int max_ctx = 0, kv_type = 0, n_pages = 0, pos = 0;
     void *k = nullptr, *v = nullptr;
     int32_t *pages = nullptr;

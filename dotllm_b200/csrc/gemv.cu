@@ -23,6 +23,8 @@
 //   silu/gelu(gate)*up for the FFN (FfnForward :466-474, both matrices in one launch).
 // * Programmatic dependent launch: each warp fetches its first weight tile before waiting for
 //   the previous kernel, so weight streaming overlaps the predecessor's tail.
+#include <string.h>
+
 #include "gemv.cuh"
 #include "gemv_tile.cuh"
 #include "ops.cuh"
@@ -54,6 +56,60 @@ __global__ void repack_q4k_kernel(const uint8_t *__restrict__ raw, uint8_t *__re
             int row = rt * 16 + g + 8 * h;
             uint4 v = make_uint4(0, 0, 0, 0);
             if (row < rows) v = *(const uint4 *)(raw + (uint64_t)row * rbytes + (uint64_t)sb * 144);
+            *(uint4 *)(dst + 2048 + g * 32 + h * 16) = v;
+        }
+}
+
+// Q4_K tile in the int8 tensor-core lane order (gemv_tile.cuh, q4k_tile_i8): same bytes, nibbles
+// re-paired per lane and the 6-bit (sc, m) pairs re-packed so that sc_j is a byte.
+__global__ void repack_q4k_i8_kernel(const uint8_t *__restrict__ raw, uint8_t *__restrict__ tiled, int rows, int nsb,
+                                     uint64_t rbytes, int ntiles)
+{
+    int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= ntiles * 32) return;
+    int tile = idx >> 5, L = idx & 31, g = L >> 2, t = L & 3;
+    int rt = tile / nsb, sb = tile % nsb;
+    uint8_t *dst = tiled + (uint64_t)tile * Q4K_TILE;
+    for (int p = 0; p < 4; p++) {
+        uint32_t w[4];
+        for (int q = 0; q < 4; q++) {  // A row g, A row g+8, B row g, B row g+8
+            const int row = rt * 16 + g + 8 * (q & 1), half = (q >> 1) * 16;
+            uint32_t word = 0;
+            if (row < rows) {
+                const uint8_t *qs = raw + (uint64_t)row * rbytes + (uint64_t)sb * 144 + 16;
+                for (int b = 0; b < 4; b++) {
+                    // element e of the super-block is nibble (e & 1) of byte e / 2
+                    const int e0 = 32 * (2 * p) + half + 4 * t + b, e1 = e0 + 32;  // sub-blocks 2p and 2p+1
+                    const uint32_t lo = (qs[e0 >> 1] >> ((e0 & 1) * 4)) & 15u, hi = (qs[e1 >> 1] >> ((e1 & 1) * 4)) & 15u;
+                    word |= (lo | (hi << 4)) << (8 * b);
+                }
+            }
+            w[q] = word;
+        }
+        *(uint4 *)(dst + p * 512 + L * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    if (t == 0)
+        for (int h = 0; h < 2; h++) {
+            const int row = rt * 16 + g + 8 * h;
+            uint8_t hd[16] = {0};
+            if (row < rows) {
+                const uint8_t *blk = raw + (uint64_t)row * rbytes + (uint64_t)sb * 144;
+                for (int i = 0; i < 4; i++) hd[i] = blk[i];  // d, dmin
+                uint32_t mhi = 0;
+                for (int j = 0; j < 8; j++) {
+                    auto f6 = [&](int bit) {  // 6 bits of the little-endian bit stream at blk + 4
+                        const int bi = bit >> 3, sh = bit & 7;
+                        const uint32_t v = blk[4 + bi] | (bi + 1 < 12 ? (uint32_t)blk[5 + bi] << 8 : 0u);
+                        return (v >> sh) & 63u;
+                    };
+                    const uint32_t sc = f6(12 * j), m = f6(12 * j + 6);
+                    hd[4 + j] = (uint8_t)(sc | ((m & 3u) << 6));
+                    mhi |= (m >> 2) << (4 * j);
+                }
+                memcpy(hd + 12, &mhi, 4);
+            }
+            uint4 v;
+            memcpy(&v, hd, 16);
             *(uint4 *)(dst + 2048 + g * 32 + h * 16) = v;
         }
 }
@@ -140,6 +196,18 @@ int prepare_tiled(llmdot_model *m, DevMat &W)
     else
         repack_q6k_kernel<<<(threads + 255) / 256, 256, 0, m->stream>>>(W.raw, W.tiled, W.rows, nsb, W.rbytes, ntiles);
     LLMDOT_CUDA_TRY(cudaGetLastError());
+    if (W.type == T_Q4_K && W.rows >= GEMV_I8_MIN_ROWS) {  // the copy the 1..2-vector matvec streams
+        e = cudaMalloc(&W.tiled8, tb * (size_t)ntiles);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            W.tiled8 = nullptr;
+            return fail(LLMDOT_E_NOMEM, "tiled weight allocation failed");
+        }
+        m->allocs.push_back(W.tiled8);
+        repack_q4k_i8_kernel<<<(threads + 255) / 256, 256, 0, m->stream>>>(W.raw, W.tiled8, W.rows, nsb, W.rbytes,
+                                                                            ntiles);
+        LLMDOT_CUDA_TRY(cudaGetLastError());
+    }
     return LLMDOT_OK;
 }
 
@@ -160,6 +228,8 @@ struct GemvArgs {
     float eps;
     int need_q4, need_q6;  // x layouts the segments use
     int lks;               // log2 of the K split: each row tile is 2^lks units of consecutive super-blocks
+    int i8;                // Q4_K segments are int8-order tiles (1..2 vectors)
+    GemvPrefetch pf;       // weights of the next operation, pulled into L2 while this one runs
 };
 
 // Tiles in flight per warp: each warp streams its tiles through a private ring of RING (2 or 3)
@@ -228,9 +298,31 @@ __device__ __forceinline__ int find_seg(const GemvArgs &a, int gt, int &rt)
 #endif
 constexpr int GEMV_WARPS = LLMDOT_GEMV_WARPS;  // warps per CTA (one CTA per SM)
 
+// This CTA's share of the next operation's weights into L2 (bulk prefetch, no data returned):
+// consecutive matvec launches are latency-bound, so while one runs the next one's tiles move
+// from HBM to L2 and its streaming starts from L2.
+__device__ __forceinline__ void l2_prefetch_share(const GemvPrefetch &pf)
+{
+#pragma unroll
+    for (int r = 0; r < GEMV_PREFETCH_MAX; r++) {
+        const unsigned long long n = pf.n[r];
+        if (!pf.p[r] || n == 0) continue;
+        const unsigned long long share = (n / gridDim.x + 15) & ~15ull, lo = (unsigned long long)blockIdx.x * share;
+        if (lo >= n) continue;
+        unsigned long long len = n - lo < share ? n - lo : share;
+        const uint8_t *src = (const uint8_t *)pf.p[r] + lo;
+        while (len > 0) {
+            const uint32_t piece = len > (1u << 20) ? (1u << 20) : (uint32_t)len;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(piece) : "memory");
+            src += piece;
+            len -= piece;
+        }
+    }
+}
+
 // Shared memory of one CTA (byte offsets; all 16-byte aligned).
 struct GemvSmem {
-    int xs4, xs6, S, P, red, stat, wred, ring, total, slot;  // byte offsets (slot: bytes per ring slot)
+    int xs4, xs6, S, P, xi, red, stat, wred, ring, total, slot;  // byte offsets (slot: bytes per ring slot)
 };
 __host__ __device__ inline GemvSmem gemv_layout(int nv, int nsb, int nmat, bool q4, bool q6, int max_rt_cta,
                                                 int ks, int ring)
@@ -246,6 +338,8 @@ __host__ __device__ inline GemvSmem gemv_layout(int nv, int nsb, int nmat, bool 
     o += q4 ? nv * nsb * 8 * 4 : 0;
     L.P = o;
     o += q4 ? nv * nsb * 32 * 4 : 0;
+    L.xi = o;  // int8 form (nv <= 2): per (vector, super-block) max |x| bits, then 2^k, and 2^-k
+    o += q4 && nv <= 2 ? (2 * nv * nsb * 4 + 15) / 16 * 16 : 0;
     L.red = o;  // unit partials [max_rt_cta][ks][nmat][16][nv]
     o += (max_rt_cta * ks * nmat * 16 * nv * 4 + 15) / 16 * 16;
     L.stat = o;
@@ -283,17 +377,20 @@ __device__ __forceinline__ void unit_pos(const GemvArgs &a, int rt_lo, int u, Un
 }
 
 // TM: 0 every segment Q4_K, 1 every segment Q6_K, 2 mixed (the type is read per unit).
-template <int NV, int MODE, int RING, int TM>
+// I8 (1..2 vectors): Q4_K segments run the int8 tensor-core form on the int8-order tile copy.
+template <int NV, int MODE, int RING, int TM, bool I8>
 __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, int max_rt_cta)
 {
     constexpr int NMAT = (MODE >= GM_SILU_MUL) ? 2 : 1;
     constexpr int NT = GEMV_WARPS * 32;
+    static_assert(!I8 || NV <= 2, "int8 form: at most two vectors (4 digit columns each)");
     extern __shared__ __align__(16) uint8_t smem[];
     const int nsb = a.nsb, cols = nsb * 256, ks = 1 << a.lks;
     const GemvSmem L = gemv_layout(NV, nsb, NMAT, a.need_q4, a.need_q6, max_rt_cta, ks, RING);
     uint4 *xs4 = (uint4 *)(smem + L.xs4), *xs6 = (uint4 *)(smem + L.xs6);
     float *S = (float *)(smem + L.S), *P = (float *)(smem + L.P), *red = (float *)(smem + L.red);
     float *stat = (float *)(smem + L.stat), *wred = (float *)(smem + L.wred);
+    float *xsc = (float *)(smem + L.xi), *xinv = xsc + NV * nsb;  // [NV][nsb] each (int8 form)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
     uint8_t *ring = smem + L.ring + (size_t)warp * RING * L.slot;
@@ -323,11 +420,14 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
         }
     };
     if (tid < GEMV_WARPS * 3) gmbar_init((uint64_t *)smem + tid);
+    if (I8 && a.need_q4)
+        for (int i = tid; i < NV * nsb; i += NT) xsc[i] = 0.0f;  // per super-block max |x| (as uint bits)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
     // weights are constant: start streaming before waiting for the previous kernel
 #pragma unroll
     for (int f = 0; f < RING; f++) issue();
+    if (tid == 0) l2_prefetch_share(a.pf);
     pdl_launch();
     pdl_wait();
 
@@ -342,7 +442,12 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
             for (int v = 0; v < NV; v++) {
                 const float h = a.x[(size_t)v * a.ldx + i];
                 ss[v] = fmaf(h, h, ss[v]);
-                mx[v] = fmaxf(mx[v], fabsf(a.norm_w ? __fmul_rn(wn, h) : h));
+                const float ax = fabsf(a.norm_w ? __fmul_rn(wn, h) : h);
+                mx[v] = fmaxf(mx[v], ax);
+                if (I8 && a.need_q4) {  // the warp's 32 consecutive elements share a super-block
+                    const float wm = warp_max(ax);
+                    if (lane == 0) atomicMax((unsigned *)xsc + v * nsb + (i >> 8), __float_as_uint(wm));
+                }
             }
         }
 #pragma unroll
@@ -378,10 +483,59 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
             stat[NV + tid] = sc;
         }
         __syncthreads();
+        if (I8 && a.need_q4)  // X = x * 2^k with the super-block's max |x| * 2^k in [2^29, 2^30)
+            for (int i = tid; i < NV * nsb; i += NT) {
+                float m = __uint_as_float(((const unsigned *)xsc)[i]);
+                if (a.norm_w) m = __fmul_rn(m, stat[i / nsb]);
+                int e = 0;
+                if (m > 0.0f && m < INFINITY) frexpf(m, &e);
+                e = max(e, -90);
+                xsc[i] = ldexpf(1.0f, 30 - e);
+                xinv[i] = ldexpf(1.0f, e - 30);
+            }
     }
     // ---- pass B: fp16 hi/lo fragments of the scaled x for the layouts in use
+    if (I8 && a.need_q4) {
+        __syncthreads();
+        // int8 form: item (v, sb, j, t) = elements 32j + 4t + b and 32j + 16 + 4t + b (b = 0..3) of
+        // super-block sb, as four signed digits of X (one 8-byte unit per digit); P gets the sum
+        // of the 8 normed values for the sub-block sums S
+        uint2 *xs8 = (uint2 *)xs4;
+        for (int it = tid; it < NV * nsb * 32; it += NT) {
+            const int tt = it & 3, j = (it >> 2) & 7, sb = (it >> 5) % nsb, v = it / (nsb * 32);
+            const int e0 = sb * 256 + 32 * j + 4 * tt;
+            const float *h = a.x + (size_t)v * a.ldx;
+            const float4 p0 = *(const float4 *)(h + e0), p1 = *(const float4 *)(h + e0 + 16);
+            float c[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+            if (a.norm_w) {
+                const float inv = stat[v];
+                const float4 n0 = *(const float4 *)(a.norm_w + e0), n1 = *(const float4 *)(a.norm_w + e0 + 16);
+                const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++) c[k] = __fmul_rn(__fmul_rn(nw[k], c[k]), inv);
+            }
+            float psum = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; k++) psum += c[k];
+            P[((v * nsb + sb) * 4 + (j >> 1)) * 8 + 4 * (j & 1) + tt] = psum;
+            const float scale = xsc[v * nsb + sb];
+            uint32_t dg[4][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}};
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                int X = __float2int_rn(c[k] * scale);
+#pragma unroll
+                for (int dd = 0; dd < 4; dd++) {  // balanced base-256 digits
+                    const int dgt = dd < 3 ? (int)(int8_t)(X & 0xFF) : X;
+                    X = (X - dgt) >> 8;
+                    dg[dd][k >> 2] |= ((uint32_t)dgt & 0xFFu) << (8 * (k & 3));
+                }
+            }
+#pragma unroll
+            for (int dd = 0; dd < 4; dd++) xs8[x8unit<NV>(sb, j, tt, 4 * v + dd)] = make_uint2(dg[dd][0], dg[dd][1]);
+        }
+    }
     for (int lay = 0; lay < 2; lay++) {
-        if ((lay == 0 && !a.need_q4) || (lay == 1 && !a.need_q6)) continue;
+        if ((lay == 0 && (I8 || !a.need_q4)) || (lay == 1 && !a.need_q6)) continue;
         uint4 *xs = lay == 0 ? xs4 : xs6;
         for (int it = tid; it < nsb * 32 * NV; it += NT) {
             const int v = it % NV, r = it / NV, w = r & 7, tt = (r >> 3) & 3, sb = r >> 5;
@@ -444,6 +598,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
     UnitPos CP;
     if (cu < nunit) unit_pos<NMAT>(a, rt_lo, cu, CP);
     float acc0 = 0.0f, acc1 = 0.0f;  // rows g, g+8 for vector t (MMA columns 2t, 2t+1)
+    float accf[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // int8 form: rows g, g+8 x this lane's two digit columns
     float corr0[NV], corr1[NV];
 #pragma unroll
     for (int v = 0; v < NV; v++) corr0[v] = corr1[v] = 0.0f;
@@ -466,10 +621,45 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
         issue();
         const int mat = (NMAT == 2 && cj >= CP.n) ? 1 : 0;
         const int sb = CP.sb_lo + cj - mat * CP.n;
-        if (TM != 1 && qt == QT_Q4K) q4k_tile<NV>(T, xs4, S, nsb, sb, t, bv, bpart, acc0, acc1, corr0, corr1);
+        if (TM != 1 && qt == QT_Q4K) {
+            if (I8) q4k_tile_i8<NV>(T, (const uint2 *)xs4, S, xinv, nsb, sb, g, t, accf, corr0, corr1);
+            else q4k_tile<NV>(T, xs4, S, nsb, sb, t, bv, bpart, acc0, acc1, corr0, corr1);
+        }
         if (TM != 0 && qt == QT_Q6K) q6k_tile<NV>(T, xs6, sb, t, bv, bpart, acc0, acc1);
         ++cj;
-        if (cj == CP.n || cj == NMAT * CP.n) {  // end of this (unit, matrix): one store of its partial
+        if (I8 && TM != 1 && qt == QT_Q4K && (cj == CP.n || cj == NMAT * CP.n)) {
+            // int8 form: weight this lane's digit columns (2t, 2t+1 -> digits 2(t&1), 2(t&1)+1 of
+            // vector t/2), add the partner lane's two digits, subtract the offset term
+            const float w0 = (t & 1) ? 65536.0f : 1.0f, w1 = (t & 1) ? 16777216.0f : 256.0f;
+            float r0 = fmaf(accf[1], w1, accf[0] * w0), r1 = fmaf(accf[3], w1, accf[2] * w0);
+            r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
+            r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+            float k0 = 0.0f, k1 = 0.0f;
+#pragma unroll
+            for (int v = 0; v < NV; v++) {
+                float c0v = corr0[v], c1v = corr1[v];
+                c0v += __shfl_xor_sync(0xffffffffu, c0v, 1);
+                c0v += __shfl_xor_sync(0xffffffffu, c0v, 2);
+                c1v += __shfl_xor_sync(0xffffffffu, c1v, 1);
+                c1v += __shfl_xor_sync(0xffffffffu, c1v, 2);
+                if (v == (t >> 1)) {
+                    k0 = c0v;
+                    k1 = c1v;
+                }
+                corr0[v] = corr1[v] = 0.0f;
+            }
+            if ((t & 1) == 0 && (t >> 1) < NV) {
+                float *rp = red + ((size_t)((CP.rtl * ks + CP.kp) * NMAT + mat) * 16) * NV;
+                rp[g * NV + (t >> 1)] = r0 - k0;
+                rp[(g + 8) * NV + (t >> 1)] = r1 - k1;
+            }
+            accf[0] = accf[1] = accf[2] = accf[3] = 0.0f;
+            if (cj == NMAT * CP.n) {
+                cj = 0;
+                cu += GEMV_WARPS;
+                if (cu < nunit) unit_pos<NMAT>(a, rt_lo, cu, CP);
+            }
+        } else if (cj == CP.n || cj == NMAT * CP.n) {  // end of this (unit, matrix): one store of its partial
             if (TM != 1 && qt == QT_Q4K) {
                 // offset term: each lane of a row group covered 2 sub-blocks; sum over the group
                 float k0 = 0.0f, k1 = 0.0f;
@@ -524,7 +714,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
         for (int mtx = 0; mtx < NMAT; mtx++) {
             float s = 0.0f;
             for (int kp = 0; kp < ks; kp++) s += red[(((rtl * ks + kp) * NMAT + mtx) * 16 + rr) * NV + v];
-            o[mtx] = s * (1.0f / stat[NV + v]);
+            o[mtx] = (I8 && sg.qt == QT_Q4K) ? s : s * (1.0f / stat[NV + v]);  // int8 form is in x's units
         }
         float *yp = sg.y + (size_t)v * sg.ldy + row;
         if (MODE == GM_STORE) *yp = o[0];
@@ -572,10 +762,10 @@ bool gemv_fast_supported(const DevMat &W, int nv)
     return gemv_need(nv, W.cols / 256, 2, q4, !q4, 4, 0, nullptr) != 0;
 }
 
-template <int NV, int MODE, int RING, int TM>
+template <int NV, int MODE, int RING, int TM, bool I8>
 static int launch_r(const GemvArgs &a, int grid, int max_rt, size_t sm, bool pdl, cudaStream_t st)
 {
-    auto kern = gemv_mma_kernel<NV, MODE, RING, TM>;
+    auto kern = gemv_mma_kernel<NV, MODE, RING, TM, I8>;
     static bool attr_set = false;  // once per instantiation
     if (!attr_set) {
         LLMDOT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_MAX));
@@ -585,12 +775,19 @@ static int launch_r(const GemvArgs &a, int grid, int max_rt, size_t sm, bool pdl
     return LLMDOT_OK;
 }
 
-template <int NV, int MODE, int RING> static int launch_tm(const GemvArgs &a, int grid, int max_rt, size_t sm, bool pdl,
-                                                           cudaStream_t st)
+template <int NV, int MODE, int RING, bool I8>
+static int launch_tm(const GemvArgs &a, int grid, int max_rt, size_t sm, bool pdl, cudaStream_t st)
 {
-    if (a.need_q4 && a.need_q6) return launch_r<NV, MODE, RING, 2>(a, grid, max_rt, sm, pdl, st);
-    if (a.need_q6) return launch_r<NV, MODE, RING, QT_Q6K>(a, grid, max_rt, sm, pdl, st);
-    return launch_r<NV, MODE, RING, QT_Q4K>(a, grid, max_rt, sm, pdl, st);
+    if (a.need_q4 && a.need_q6) return launch_r<NV, MODE, RING, 2, I8>(a, grid, max_rt, sm, pdl, st);
+    if (a.need_q6) return launch_r<NV, MODE, RING, QT_Q6K, false>(a, grid, max_rt, sm, pdl, st);
+    return launch_r<NV, MODE, RING, QT_Q4K, I8>(a, grid, max_rt, sm, pdl, st);
+}
+template <int NV, int MODE, int RING>
+static int launch_i8(const GemvArgs &a, int grid, int max_rt, size_t sm, bool pdl, cudaStream_t st)
+{
+    if constexpr (NV <= 2)
+        if (a.i8) return launch_tm<NV, MODE, RING, true>(a, grid, max_rt, sm, pdl, st);
+    return launch_tm<NV, MODE, RING, false>(a, grid, max_rt, sm, pdl, st);
 }
 
 template <int NV, int MODE> static int launch_t(GemvArgs a, bool pdl, cudaStream_t st)
@@ -615,8 +812,8 @@ template <int NV, int MODE> static int launch_t(GemvArgs a, bool pdl, cudaStream
     }
     if (sm == 0) return fail(LLMDOT_E_UNSUPPORTED, "fast matvec: shared memory");
     a.lks = lks;
-    if (ring == 3) return launch_tm<NV, MODE, 3>(a, grid, max_rt, sm, pdl, st);
-    return launch_tm<NV, MODE, 2>(a, grid, max_rt, sm, pdl, st);
+    if (ring == 3) return launch_i8<NV, MODE, 3>(a, grid, max_rt, sm, pdl, st);
+    return launch_i8<NV, MODE, 2>(a, grid, max_rt, sm, pdl, st);
 }
 
 template <int MODE> static int launch_mode(const GemvArgs &a, int nv, bool pdl, cudaStream_t st)
@@ -630,11 +827,16 @@ template <int MODE> static int launch_mode(const GemvArgs &a, int nv, bool pdl, 
 }
 
 int launch_gemv_multi(const GemvTarget *tg, int ntarget, const float *norm_w, float eps, const float *x, int ldx,
-                      int nv, int mode, bool pdl, cudaStream_t st)
+                      int nv, int mode, bool pdl, cudaStream_t st, const GemvPrefetch *pf)
 {
     if (ntarget < 1 || ntarget > 3 || (mode >= GEMV_SILU_MUL && ntarget != 1))
         return fail(LLMDOT_E_INVALID, "fast matvec: bad target list");
     GemvArgs a = {};
+    if (pf) {
+        for (int r = 0; r < GEMV_PREFETCH_MAX; r++)  // bulk prefetches want 16-byte aligned, 16-byte multiples
+            if (((uintptr_t)pf->p[r] & 15) || (pf->n[r] & 15)) return fail(LLMDOT_E_INVALID, "fast matvec: prefetch range");
+        a.pf = *pf;
+    }
     a.nseg = ntarget;
     a.nsb = tg[0].W->cols / 256;
     a.x = x;
@@ -660,6 +862,18 @@ int launch_gemv_multi(const GemvTarget *tg, int ntarget, const float *norm_w, fl
         a.need_q4 |= s.qt == QT_Q4K;
         a.need_q6 |= s.qt == QT_Q6K;
     }
+    // the int8 form when every Q4_K segment has its int8-order copy (the large logits matrices)
+    bool i8 = nv <= 2 && a.need_q4;
+    for (int i = 0; i < ntarget; i++)
+        if (tg[i].W->type == T_Q4_K) i8 = i8 && tg[i].W->tiled8 && (!tg[i].W1 || tg[i].W1->tiled8);
+    if (i8) {
+        a.i8 = 1;
+        for (int i = 0; i < ntarget; i++)
+            if (tg[i].W->type == T_Q4_K) {
+                a.seg[i].w = tg[i].W->tiled8;
+                if (tg[i].W1) a.seg[i].w1 = tg[i].W1->tiled8;
+            }
+    }
     switch (mode) {
     case GM_STORE: return launch_mode<GM_STORE>(a, nv, pdl, st);
     case GM_ADD: return launch_mode<GM_ADD>(a, nv, pdl, st);
@@ -669,10 +883,10 @@ int launch_gemv_multi(const GemvTarget *tg, int ntarget, const float *norm_w, fl
 }
 
 int launch_gemv_fast_ex(const DevMat &W0, const DevMat *W1, const float *norm_w, float eps, const float *x, int ldx,
-                        int nv, float *y, int ldy, int mode, cudaStream_t st, bool pdl)
+                        int nv, float *y, int ldy, int mode, cudaStream_t st, bool pdl, const GemvPrefetch *pf)
 {
     GemvTarget tg = {&W0, W1, y, ldy};
-    return launch_gemv_multi(&tg, 1, norm_w, eps, x, ldx, nv, mode, pdl, st);
+    return launch_gemv_multi(&tg, 1, norm_w, eps, x, ldx, nv, mode, pdl, st, pf);
 }
 
 int launch_gemv_fast(const DevMat &W, const float *x, int ldx, int nv, float *y, int ldy, bool accumulate,

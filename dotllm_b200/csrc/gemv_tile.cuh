@@ -159,6 +159,109 @@ __device__ __forceinline__ void q4k_tile(const TileRegs &T, const uint4 *__restr
     }
 }
 
+// ---------------------------------------------------------------- Q4_K, int8 tensor-core form
+// For one or two input vectors.  x enters as four signed 8-bit digits of X = x * 2^k (k per
+// super-block, |X| <= 2^30), one MMA column per (vector, digit); the nibbles are the unsigned
+// A operand of mma.m16n8k32 (one 32-weight sub-block per MMA, so its 6-bit scale multiplies
+// the int32 result exactly).  Every product and sum of a super-block is exact integer
+// arithmetic; the float result differs from the fp32 dot only by x's rounding at 2^-30 of the
+// block's largest |x|.
+// Tile (2304 bytes), lane L = 4g + t: plane p (0..3) at p*512 + L*16 holds the words
+// {A row g, A row g+8, B row g, B row g+8} of sub-blocks j = 2p (low nibbles) and j' = 2p+1
+// (high nibbles): byte b of A holds weight 4t+b, byte b of B weight 16+4t+b.  The low nibbles
+// (W & 0x0F0F0F0F) are j's operand as they are, the high ones (W & 0xF0F0F0F0) are j''s times
+// 16 (exact; divided out once per tile).  Headers at 2048 + g*32 (row g, then row g+8), 16
+// bytes each: d, dmin (fp16), bytes 4..11: sc_j | (m_j & 3) << 6, bytes 12..15: m_j >> 2 in
+// nibble j.
+__device__ __forceinline__ void mma_u8s8_zero(int &d0, int &d1, int &d2, int &d3, uint32_t a0, uint32_t a1,
+                                              uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1)
+{
+    const int z = 0;
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(z));
+}
+
+// x digit fragments: unit (sb, j, t, col) of 8 bytes, col = 4v + digit; lane (g, t) reads
+// col g mod (4 NV).
+template <int NV> __device__ __forceinline__ int x8unit(int sb, int j, int t, int col)
+{
+    return ((sb * 8 + j) * 4 + t) * (4 * NV) + col;
+}
+
+// One tile: accf[0..1] += rows g (columns 2t, 2t+1), accf[2..3] the same for row g+8, in units of
+// d * 2^-k (the digit weights are applied when a unit ends); corr*[v] += the offset term of this
+// lane's sub-blocks 2t, 2t+1 (coef = 8 d sc + dmin m, times the sub-block sums S of x).
+template <int NV>
+__device__ __forceinline__ void q4k_tile_i8(const TileRegs &T, const uint2 *__restrict__ xs8, const float *__restrict__ S,
+                                            const float *__restrict__ xinv, int nsb, int sb, int g, int t,
+                                            float (&accf)[4], float *corr0, float *corr1)
+{
+    const uint4 h0 = T.r[4], h1 = T.r[5];
+    const uint32_t s0a = h0.y & 0x3F3F3F3Fu, s0b = h0.z & 0x3F3F3F3Fu;
+    const uint32_t s1a = h1.y & 0x3F3F3F3Fu, s1b = h1.z & 0x3F3F3F3Fu;
+    const uint2 *xp = xs8 + x8unit<NV>(sb, 0, t, g % (4 * NV));
+    int ai0 = 0, ai1 = 0, ai2 = 0, ai3 = 0;  // low-nibble sub-blocks
+    int ah0 = 0, ah1 = 0, ah2 = 0, ah3 = 0;  // high-nibble sub-blocks, times 16
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+        const uint4 W = T.r[p];  // A row g, A row g+8, B row g, B row g+8
+#pragma unroll
+        for (int hi = 0; hi < 2; hi++) {
+            const int j = 2 * p + hi;
+            const uint32_t mk = hi ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+            const uint2 b = xp[j * 4 * (4 * NV)];
+            int c0, c1, c2, c3;
+            mma_u8s8_zero(c0, c1, c2, c3, W.x & mk, W.y & mk, W.z & mk, W.w & mk, b.x, b.y);
+            const int sg = (int)__byte_perm(j < 4 ? s0a : s0b, 0u, 0x4440u | (j & 3));
+            const int sg8 = (int)__byte_perm(j < 4 ? s1a : s1b, 0u, 0x4440u | (j & 3));
+            if (hi) {
+                ah0 += sg * c0;
+                ah1 += sg * c1;
+                ah2 += sg8 * c2;
+                ah3 += sg8 * c3;
+            } else {
+                ai0 += sg * c0;
+                ai1 += sg * c1;
+                ai2 += sg8 * c2;
+                ai3 += sg8 * c3;
+            }
+        }
+    }
+    ai0 += ah0 >> 4;  // exact: every high-nibble product is a multiple of 16
+    ai1 += ah1 >> 4;
+    ai2 += ah2 >> 4;
+    ai3 += ah3 >> 4;
+    const float d0 = half_bits(h0.x & 0xFFFF), d1 = half_bits(h1.x & 0xFFFF);
+    const int v = min(t >> 1, NV - 1);
+    const float xi = xinv[v * nsb + sb];
+    const float f0 = d0 * xi, f1 = d1 * xi;
+    accf[0] = fmaf(f0, (float)ai0, accf[0]);
+    accf[1] = fmaf(f0, (float)ai1, accf[1]);
+    accf[2] = fmaf(f1, (float)ai2, accf[2]);
+    accf[3] = fmaf(f1, (float)ai3, accf[3]);
+    // offset term of sub-blocks 2t, 2t+1
+    const float dm0 = half_bits(h0.x >> 16), dm1 = half_bits(h1.x >> 16);
+    const uint32_t r0 = t < 2 ? h0.y : h0.z, r1 = t < 2 ? h1.y : h1.z;  // bytes of sub-blocks 4*(t>=2) ..
+#pragma unroll
+    for (int jj = 0; jj < 2; jj++) {
+        const int j = 2 * t + jj;
+        const uint32_t bsel = (uint32_t)(j & 3);
+        const uint32_t by0 = __byte_perm(r0, 0u, 0x4440u | bsel), by1 = __byte_perm(r1, 0u, 0x4440u | bsel);
+        const float m0 = (float)((by0 >> 6) | (((h0.w >> (4 * j)) & 15u) << 2));
+        const float m1 = (float)((by1 >> 6) | (((h1.w >> (4 * j)) & 15u) << 2));
+        const float cf0 = fmaf(8.0f * d0, (float)(by0 & 63u), dm0 * m0);
+        const float cf1 = fmaf(8.0f * d1, (float)(by1 & 63u), dm1 * m1);
+#pragma unroll
+        for (int vv = 0; vv < NV; vv++) {
+            const float sj = S[(vv * nsb + sb) * 8 + j];
+            corr0[vv] = fmaf(cf0, sj, corr0[vv]);
+            corr1[vv] = fmaf(cf1, sj, corr1[vv]);
+        }
+    }
+}
+
 template <int NV>
 __device__ __forceinline__ void q6k_tile(const TileRegs &T, const uint4 *__restrict__ xs, int sb, int t, int bv,
                                          int bpart, float &acc0, float &acc1)

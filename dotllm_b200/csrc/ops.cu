@@ -107,6 +107,8 @@ __global__ void rmsnorm_kernel(const float *__restrict__ in, int ldin, const flo
     const float *x = in + (uint64_t)blockIdx.x * ldin;
     float *o = out + (uint64_t)blockIdx.x * ldout;
     __shared__ float red[32];
+    pdl_launch();  // no-ops unless launched with programmatic dependent launch
+    pdl_wait();
     float ss = 0.0f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
     ss = warp_sum(ss);
@@ -129,10 +131,9 @@ __global__ void rmsnorm_kernel(const float *__restrict__ in, int ldin, const flo
 }
 
 int launch_rmsnorm(const float *in, int ldin, const float *w, float *out, int ldout, int n, int nv, float eps,
-                   cudaStream_t st)
+                   cudaStream_t st, bool pdl)
 {
-    rmsnorm_kernel<<<nv, 256, 0, st>>>(in, ldin, w, out, ldout, n, eps);
-    LLMDOT_CUDA_TRY(cudaGetLastError());
+    LLMDOT_CUDA_TRY(launch_kernel(pdl, rmsnorm_kernel, dim3(nv), dim3(256), 0, st, in, ldin, w, out, ldout, n, eps));
     return LLMDOT_OK;
 }
 

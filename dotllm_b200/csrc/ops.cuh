@@ -10,7 +10,7 @@ int launch_dequant(const uint8_t *src, float *dst, uint32_t type, int rows, int 
 int launch_gemv_ref(const uint8_t *W, uint32_t type, int rows, int cols, const float *x, int ldx, int nv, float *y,
                     int ldy, bool accumulate, cudaStream_t st);
 int launch_rmsnorm(const float *in, int ldin, const float *w, float *out, int ldout, int n, int nv, float eps,
-                   cudaStream_t st);
+                   cudaStream_t st, bool pdl = false);
 int launch_layernorm(const float *x, const float *w, const float *b, float *o, int n, float eps, cudaStream_t st);
 int launch_eltwise(int op, const float *a, const float *b, float *o, int n, float s, cudaStream_t st, int row = 0);
 int launch_act_mul(bool gelu, const float *gate, const float *up, float *out, int ffn, int batch, cudaStream_t st);

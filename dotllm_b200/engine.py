@@ -9,6 +9,7 @@ in the native library on the GPU; there is no CPU path here.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 from typing import List, Optional, Sequence, Tuple
 
 import numpy as np
@@ -18,6 +19,7 @@ from .native import (KV_F16, KV_F32, LlmdotConfig, TensorDesc, VP, F32P, I32P, c
 
 class CudaModel:
     def __init__(self, handle: int, device: int):
+        self._sessions = weakref.WeakSet()
         self._h = C.c_void_p(handle)
         self.device = device
         cfg = LlmdotConfig()
@@ -90,10 +92,15 @@ class CudaModel:
         return a.value, b.value
 
     def session(self, max_ctx: int = 0, kv: str = "f16") -> "CudaSession":
-        return CudaSession(self, max_ctx, KV_F16 if kv == "f16" else KV_F32)
+        s = CudaSession(self, max_ctx, KV_F16 if kv == "f16" else KV_F32)
+        self._sessions.add(s)
+        return s
 
     def close(self) -> None:
+        """Free the model; sessions still open are closed first."""
         if self._h:
+            for s in list(self._sessions):
+                s.close()
             lib().llmdot_cuda_model_free(self._h)
             self._h = None
 

@@ -205,6 +205,8 @@ LLMDOT_API int llmdot_cuda_model_config(const llmdot_model *m, llmdot_config *ou
 /* Quantised weight bytes the decode step streams per token (layers + logits head). */
 LLMDOT_API int llmdot_cuda_model_weight_bytes(const llmdot_model *m, uint64_t *layer_bytes,
                                               uint64_t *head_bytes);
+/* Sessions of the model that are still open stay valid for llmdot_cuda_session_free only;
+ * every other call on them returns LLMDOT_E_INVALID. */
 LLMDOT_API int llmdot_cuda_model_free(llmdot_model *m);
 
 /* A session = one InferenceEngine's KvCache (src/Llmdot.Core/Inference/KvCache.cs), held on

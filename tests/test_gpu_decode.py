@@ -169,3 +169,20 @@ def test_large_batch_decode_matches_single(gpu, B):
             if top2[1] - top2[0] > 1e-3:
                 assert int(nxt[i]) == int(n1)
         cur = [int(t) for t in nxt]
+
+
+def test_session_outlives_model(gpu):
+    """Freeing a model detaches its open sessions: calls on them fail cleanly, free still works."""
+    from dotllm_b200 import native
+    cfg = synth.get("micro")
+    m = CudaModel.load(synth.build_model(cfg))
+    s = m.session(kv="f32")
+    s.prefill(synth.prompt_tokens(cfg))
+    h = native.VP(s._h.value)
+    s._h = None  # keep the native session open past the model
+    m.close()
+    nxt = native.C.c_int32()
+    toks = np.zeros(1, dtype=np.int32)
+    rc = native.lib().llmdot_cuda_prefill(h, toks.ctypes.data_as(native.I32P), 1, None, native.C.byref(nxt))
+    assert rc == -1  # LLMDOT_E_INVALID
+    assert native.lib().llmdot_cuda_session_free(h) == 0
