@@ -586,9 +586,13 @@ static bool cluster_plan(const AttnShape &sh, int batch, size_t esz, int *C_out,
     if (sh.sliding_window > 0) npg = std::min(npg, (sh.sliding_window + KV_PAGE - 1) / KV_PAGE + 1);
     // the score buffer holds AC_SBUF bytes: that many pages per CTA
     const int maxp_lim = std::max(1, AC_SBUF / (G * KV_PAGE * 4));
+    static const int c_cap = [] {  // LLMDOT_ATTN_CLUSTER: upper bound on the cluster size (tuning)
+        const char *e = getenv("LLMDOT_ATTN_CLUSTER");
+        return e ? std::min(8, std::max(1, atoi(e))) : 8;
+    }();
     int C = 1;
     while (C < 8 && (npg + C - 1) / C > maxp_lim) C++;
-    while (C < 8 && (long long)batch * sh.heads_kv * C < 2 * 148) C++;  // enough CTAs for every SM
+    while (C < c_cap && (long long)batch * sh.heads_kv * C < 2 * 148) C++;  // enough CTAs for every SM
     const int maxp = (npg + C - 1) / C;
     if (maxp > maxp_lim) return false;
     // page slots: as many pages in flight as the CTAs sharing an SM leave room for (at most
