@@ -600,7 +600,11 @@ static bool cluster_plan(const AttnShape &sh, int batch, size_t esz, int *C_out,
     const long long ctas = (long long)batch * sh.heads_kv * C;
     const int per_sm = (int)std::min<long long>(4, std::max<long long>(1, (ctas + 147) / 148));
     const int budget = std::min(200 * 1024, 220 * 1024 / per_sm - 2048);
-    int slots = 2 * maxp;
+    // Large pages (24 KB and up: head_dim 256 in fp16) stream best two at a time with the CTAs
+    // small enough to pair up on an SM; small pages are latency-bound, and their CTAs run best
+    // one per SM with every page in flight (measured on Gemma-2-2B and Llama-3.2-1B shapes).
+    const bool big_pages = (size_t)KV_PAGE * (sh.head_dim * esz + 16) >= 24 * 1024;
+    int slots = big_pages ? 2 : 2 * maxp;
     static const int slots_cap = [] {  // LLMDOT_ATTN_SLOTS: upper bound on the page slots (tuning)
         const char *e = getenv("LLMDOT_ATTN_SLOTS");
         return e ? std::max(2, atoi(e)) : 1 << 20;

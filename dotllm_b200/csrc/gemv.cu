@@ -400,18 +400,20 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
     const int rt_lo = (int)((long long)blockIdx.x * a.rt_total / gridDim.x);
     const int rt_hi = (int)((long long)(blockIdx.x + 1) * a.rt_total / gridDim.x);
     const int nrt = rt_hi - rt_lo, nunit = nrt * ks;
-    // issue cursor: unit iu, tile ij of it, ring slot islot; i_n tiles issued so far
-    int iu = warp, ij = 0, islot = 0, i_n = 0;
+    // issue cursor: unit iu, tile ij of it; i_n tiles issued so far
+    // tiles go through the ring in order, so the slot of a warp's k-th tile is k mod RING: both
+    // loops below walk the slots with compile-time indices (ring slot bytes = L.slot)
+    constexpr int SLOTB = TM == QT_Q4K ? Q4K_TILE : Q6K_TILE;
+    int iu = warp, ij = 0, i_n = 0;
     UnitPos IP;
     if (iu < nunit) unit_pos<NMAT>(a, rt_lo, iu, IP);
-    auto issue = [&]() {
+    auto issue = [&](int slot) {  // the warp's next tile into ring slot `slot`
         if (iu >= nunit) return;
         if (lane == 0) {
             const int mat = (NMAT == 2 && ij >= IP.n) ? 1 : 0;
-            issue_bulk(ring + islot * L.slot, (mat ? IP.p1 : IP.p0) + (size_t)(ij - mat * IP.n) * IP.tb, IP.tb,
-                       mb + islot);
+            issue_bulk(ring + slot * SLOTB, (mat ? IP.p1 : IP.p0) + (size_t)(ij - mat * IP.n) * IP.tb, IP.tb,
+                       mb + slot);
         }
-        if (++islot == RING) islot = 0;
         i_n++;
         if (++ij == NMAT * IP.n) {
             ij = 0;
@@ -426,7 +428,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
     __syncthreads();
     // weights are constant: start streaming before waiting for the previous kernel
 #pragma unroll
-    for (int f = 0; f < RING; f++) issue();
+    for (int f = 0; f < RING; f++) issue(f);
     if (tid == 0) l2_prefetch_share(a.pf);
     pdl_launch();
     pdl_wait();
@@ -593,7 +595,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
     // ---- streaming loop: no CTA-wide barrier inside, warps run independently.  A warp sums a
     // whole (unit, matrix) in registers and stores it once; nothing else is written per tile.
     const int bv = min(g >> 1, NV - 1), bpart = g & 1;  // this lane's B column (vector, part)
-    int cu = warp, cj = 0, cslot = 0, c_n = 0;
+    int cu = warp, cj = 0, c_n = 0, s_fail = 0;
     uint32_t cpar = 0;
     UnitPos CP;
     if (cu < nunit) unit_pos<NMAT>(a, rt_lo, cu, CP);
@@ -603,22 +605,22 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
 #pragma unroll
     for (int v = 0; v < NV; v++) corr0[v] = corr1[v] = 0.0f;
     bool ok = true;
-    while (cu < nunit) {
-        if (!gmbar_wait(mb + cslot, cpar)) {
+    while (ok && cu < nunit) {
+#pragma unroll
+      for (int slot = 0; slot < RING; slot++) {  // one lap of the ring per iteration
+        if (cu >= nunit) break;
+        if (!gmbar_wait(mb + slot, cpar)) {
             ok = false;
+            s_fail = slot;
             if (lane == 0) atomicExch(&g_gemv_timeout, 1);
             break;
         }
         const int qt = TM == 2 ? CP.qt : TM;
         TileRegs T;
-        read_tile(T, ring + cslot * L.slot, qt, lane);
+        read_tile(T, ring + slot * SLOTB, qt, lane);
         __syncwarp();  // the tile is in registers: refill its slot before the math
-        if (++cslot == RING) {
-            cslot = 0;
-            cpar ^= 1u;
-        }
         c_n++;
-        issue();
+        issue(slot);
         const int mat = (NMAT == 2 && cj >= CP.n) ? 1 : 0;
         const int sb = CP.sb_lo + cj - mat * CP.n;
         if (TM != 1 && qt == QT_Q4K) {
@@ -691,15 +693,19 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
                 if (cu < nunit) unit_pos<NMAT>(a, rt_lo, cu, CP);
             }
         }
+      }
+        if (ok) cpar ^= 1u;  // the next lap waits for the slots' next phases
     }
-    if (!ok)  // bounded drain of this warp's copies still in flight, then leave the output untouched
+    if (!ok) {  // bounded drain of this warp's copies still in flight, then leave the output untouched
+        int ds = s_fail;
         for (int k = c_n; k < i_n; k++) {
-            gmbar_wait(mb + cslot, cpar);
-            if (++cslot == RING) {
-                cslot = 0;
+            gmbar_wait(mb + ds, cpar);
+            if (++ds == RING) {
+                ds = 0;
                 cpar ^= 1u;
             }
         }
+    }
     if (!__syncthreads_and(ok)) return;
 
     // ---- epilogue: every (row tile, row, vector) of the CTA, K parts summed in a fixed order
