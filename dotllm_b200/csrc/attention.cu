@@ -384,7 +384,9 @@ __global__ void __launch_bounds__(AC_THREADS) attn_cluster_kernel(const float *_
     const KvView vw = views[b];
     const size_t lbase = (size_t)layer * vw.layer_stride;
     // stream f = 0..2n-1: K pages 0..n-1 then V pages 0..n-1, page f in slot f % slots; every
-    // thread's copies of a page arrive on the slot's mbarrier (cp.async.mbarrier.arrive.noinc)
+    // thread's copies of a page arrive on the slot's mbarrier (cp.async.mbarrier.arrive.noinc).
+    // Thread tid copies 16-byte chunk tid % cpr of rows tid / cpr, + rpp, ... (no division per copy)
+    const int rpp = AC_THREADS / cpr, crow = tid / cpr, cchunk = tid % cpr;
     auto issue = [&](int f) {
         const int i = f < n ? f : f - n;
         const int s0 = (pg_lo + i) * KV_PAGE, jlo = max(start - s0, 0), jhi = min(seq_len - s0, KV_PAGE);
@@ -392,10 +394,9 @@ __global__ void __launch_bounds__(AC_THREADS) attn_cluster_kernel(const float *_
                        ((size_t)vw.pages[pg_lo + i] * sh.heads_kv + kvh) * KV_PAGE * hd;
         const int slot = f % slots;
         uint8_t *dst = ring + (size_t)slot * KV_PAGE * L.rstride;
-        for (int c = tid; c < (jhi - jlo) * cpr; c += AC_THREADS) {
-            const int j = jlo + c / cpr, ch = c % cpr;
-            cp_async16(dst + j * L.rstride + ch * 16, src + (size_t)j * hd + ch * E);
-        }
+        if (crow < rpp)
+            for (int j = jlo + crow; j < jhi; j += rpp)
+                cp_async16(dst + j * L.rstride + cchunk * 16, src + (size_t)j * hd + cchunk * E);
         asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(mbar + slot)) : "memory");
     };
     bool ok = true;
@@ -449,7 +450,7 @@ __global__ void __launch_bounds__(AC_THREADS) attn_cluster_kernel(const float *_
     const int len = seq_len - start, nvec = len - len % 8;
     const float inv_cap = sh.has_cap ? __fdiv_rn(1.0f, sh.cap) : 0.0f;
     // threads per dot product: 256 threads over G x 64 dots
-    const int TPD = G >= 4 ? 1 : (G == 2 ? 2 : 4);
+    const int LTPD = G >= 4 ? 0 : (G == 2 ? 1 : 2), TPD = 1 << LTPD;
     // ---- pass 1: scores of this CTA's positions
     for (int f = 0; f < n; f++) {
         uint8_t *slot = consume(f);
@@ -459,7 +460,7 @@ __global__ void __launch_bounds__(AC_THREADS) attn_cluster_kernel(const float *_
             __syncthreads();
         }
         for (int base = 0; base < G * KV_PAGE * TPD; base += AC_THREADS) {
-            const int idx = base + tid, dot = idx / TPD, part = idx % TPD, hg = dot / KV_PAGE, j = dot % KV_PAGE;
+            const int idx = base + tid, dot = idx >> LTPD, part = idx & (TPD - 1), hg = dot / KV_PAGE, j = dot % KV_PAGE;
             const bool valid = idx < G * KV_PAGE * TPD && j >= jlo && j < jhi;
             float acc = 0.0f;
             if (valid) {
