@@ -165,3 +165,20 @@ class CudaBackend:
         r = C.c_int()
         check(lib().llmdot_cuda_argmax(self._h, _f(x), x.size, C.byref(r)))
         return r.value
+
+    def sample(self, logits, options, recent=(), r=None) -> int:
+        """Sampler.Sample (Sampler.cs:24-62) on the device.  options: native.LlmdotSampling;
+        r: the uniform draw (the seeded draw of options.seed when omitted and seed >= 0)."""
+        from .native import LlmdotSampling
+        x = _f32(logits)
+        rec = np.ascontiguousarray(recent, dtype=np.int32)
+        if r is None:
+            if options.seed < 0:
+                raise ValueError("an unseeded sample needs its draw r")
+            r = lib().llmdot_cuda_sampling_seeded_draw(options.seed)
+        out = C.c_int32()
+        o = LlmdotSampling(options.top_k, options.top_p, options.temperature, options.repeat_penalty,
+                           options.repeat_window, options.seed)
+        check(lib().llmdot_cuda_sample(self._h, _f(x), x.size, C.byref(o), rec.ctypes.data_as(I32P), rec.size,
+                                       float(r), C.byref(out)))
+        return out.value

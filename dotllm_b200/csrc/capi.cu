@@ -2,6 +2,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <random>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -9,6 +10,7 @@
 #include <vector>
 
 #include "engine.cuh"
+#include "sample.cuh"
 #include "gemv.cuh"
 #include "gguf_loader.h"
 #include "tp.cuh"
@@ -428,6 +430,77 @@ extern "C" int llmdot_cuda_argmax(llmdot_backend *h, const float *x, int n, int 
     return LLMDOT_OK;
 }
 
+// new System.Random(seed).NextSingle(): Knuth's subtractive generator as the .NET-5-compatible
+// seeded Random implements it (55-entry state, MSEED 161803398, modulus int.MaxValue), first
+// sample divided by int.MaxValue, then rounded to float.
+extern "C" float llmdot_cuda_sampling_seeded_draw(int32_t seed)
+{
+    const int MBIG = 2147483647, MSEED = 161803398;
+    int sa[56] = {0};
+    const int sub = seed == INT32_MIN ? MBIG : (seed < 0 ? -seed : seed);
+    int mj = MSEED - sub, mk = 1;
+    sa[55] = mj;
+    for (int i = 1; i < 55; i++) {
+        const int ii = (21 * i) % 55;
+        sa[ii] = mk;
+        mk = mj - mk;
+        if (mk < 0) mk += MBIG;
+        mj = sa[ii];
+    }
+    for (int k = 1; k < 5; k++)
+        for (int i = 1; i < 56; i++) {
+            sa[i] -= sa[1 + (i + 30) % 55];
+            if (sa[i] < 0) sa[i] += MBIG;
+        }
+    int v = sa[1] - sa[22];  // the first draw reads entries 1 and 22
+    if (v == MBIG) v--;
+    if (v < 0) v += MBIG;
+    return (float)(v * (1.0 / MBIG));
+}
+
+namespace llmdot {
+static SampleArgs sample_args(const llmdot_sampling &o, int n)
+{
+    SampleArgs a = {};
+    a.n = n;
+    a.ld = n;
+    a.temperature = o.temperature;
+    a.inv_temp = o.temperature > 0.0f ? 1.0f / o.temperature : 0.0f;  // 1f / options.Temperature
+    a.top_k = o.top_k;
+    a.penalty = o.repeat_penalty;
+    a.window = o.repeat_window > 0 ? o.repeat_window : 0;
+    return a;
+}
+}  // namespace llmdot
+
+extern "C" int llmdot_cuda_sample(llmdot_backend *h, const float *logits, int n, const llmdot_sampling *opt,
+                                  const int32_t *recent, int n_recent, float r, int32_t *index)
+{
+    LLMDOT_TRY(enter(h));
+    if (!logits || !opt || !index || n <= 0 || n_recent < 0 || (n_recent > 0 && !recent))
+        return fail(LLMDOT_E_INVALID, "sample: bad arguments");
+    SampleArgs a = sample_args(*opt, n);
+    void *dl, *dr, *dp;
+    LLMDOT_TRY(up(h, 0, logits, sizeof(float) * n, &dl));
+    if (n_recent > 0) LLMDOT_TRY(up(h, 1, recent, sizeof(int32_t) * n_recent, &dr));
+    const int32_t hp[4] = {n_recent, 0, 0, 0};  // [recent length, out, pad, r]
+    int32_t hpr[4];
+    memcpy(hpr, hp, sizeof(hp));
+    memcpy(&hpr[3], &r, sizeof(float));
+    LLMDOT_TRY(up(h, 2, hpr, sizeof(hpr), &dp));
+    a.logits = (const float *)dl;
+    a.recent = n_recent > 0 ? (const int32_t *)dr : nullptr;
+    a.recent_len = (const int32_t *)dp;
+    a.recent_ld = n_recent;
+    a.out = (int32_t *)dp + 1;
+    a.r = (const float *)((int32_t *)dp + 3);
+    LLMDOT_TRY(launch_sample(a, 1, h->st));
+    int32_t out = 0;
+    LLMDOT_TRY(down(h, &out, (int32_t *)dp + 1, sizeof(int32_t)));
+    *index = out;
+    return LLMDOT_OK;
+}
+
 // ===================================================================== Tier B
 namespace llmdot {
 
@@ -764,7 +837,17 @@ static int check_err_flag(llmdot_model *m)
     return LLMDOT_OK;
 }
 
+static int prefill_rows(llmdot_session *s, const int32_t *tokens, int n, float *logits, int32_t *next_token,
+                        int *last_row_out);
+
 extern "C" int llmdot_cuda_prefill(llmdot_session *s, const int32_t *tokens, int n, float *logits, int32_t *next_token)
+{
+    return prefill_rows(s, tokens, n, logits, next_token, nullptr);
+}
+
+// The prefill; *last_row_out (nullable) receives the workspace row of the last token's logits.
+static int prefill_rows(llmdot_session *s, const int32_t *tokens, int n, float *logits, int32_t *next_token,
+                        int *last_row_out)
 {
     if (!s || (!tokens && n > 0) || n < 0) return fail(LLMDOT_E_INVALID, "prefill: bad arguments");
     llmdot_model *m = s->m;
@@ -830,6 +913,7 @@ extern "C" int llmdot_cuda_prefill(llmdot_session *s, const int32_t *tokens, int
     LLMDOT_TRY(check_err_flag(m));
     s->pos += n;
     if (next_token) *next_token = nt;
+    if (last_row_out) *last_row_out = last_row;
     return LLMDOT_OK;
 }
 
@@ -922,6 +1006,102 @@ extern "C" int llmdot_cuda_generate(llmdot_session *s, const int32_t *prompt, in
     }
     *n_out = produced;
     return LLMDOT_OK;
+}
+
+extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *prompt, int n_prompt, int max_tokens,
+                                            const llmdot_sampling *opt, const float *draws, int32_t *out_tokens,
+                                            int *n_out)
+{
+    if (!s || !opt || !out_tokens || !n_out || max_tokens < 0 || n_prompt < 0 || (n_prompt > 0 && !prompt))
+        return fail(LLMDOT_E_INVALID, "generate_sampled: bad arguments");
+    llmdot_model *m = s->m;
+    if (!m) return fail(LLMDOT_E_INVALID, "generate_sampled: the session's model was freed");
+    if (m->tp > 1) return fail(LLMDOT_E_UNSUPPORTED, "generate_sampled: not under tensor parallelism");
+    const llmdot_config &c = m->cfg;
+    SampleArgs a = sample_args(*opt, c.vocab);
+    if (a.temperature > 0.0f && (a.top_k <= 0 || a.top_k >= c.vocab || a.top_k > SAMPLE_MAX_TOP_K))
+        return fail(LLMDOT_E_UNSUPPORTED, "generate_sampled: temperature > 0 needs 0 < top_k < vocabulary, <= 1024");
+    if (a.window > SAMPLE_MAX_WINDOW) return fail(LLMDOT_E_UNSUPPORTED, "generate_sampled: repeat window above 1024");
+    *n_out = 0;
+    LLMDOT_TRY(llmdot_cuda_session_reset(s));  // InferenceEngine.cs:79
+    int last_row = 0;
+    int32_t first = 0;
+    if (n_prompt > 0) {
+        LLMDOT_TRY(prefill_rows(s, prompt, n_prompt, nullptr, &first, &last_row));
+    } else {
+        const int32_t init = c.bos > 0 ? c.bos : 0;  // InferenceEngine.cs:90-95
+        LLMDOT_TRY(prefill_rows(s, &init, 1, nullptr, &first, &last_row));
+    }
+    if (max_tokens == 0) return LLMDOT_OK;
+    LLMDOT_CUDA_TRY(cudaSetDevice(m->device));
+    Workspace &w = m->ws;
+    cudaStream_t st = m->stream;
+    cudaGraphExec_t g = nullptr;
+    LLMDOT_TRY(step_graph(m, 1, s->kv_type, &g));
+    // history: the prompt, then every generated token, the last window + 1 kept (:100, :109-111)
+    const int keep = a.window + 1;
+    std::vector<int32_t> recent(prompt, prompt + n_prompt);
+    // device: [history (keep)] [length] [out] [r]
+    int32_t *dbuf = nullptr;
+    LLMDOT_CUDA_TRY(cudaMallocAsync(&dbuf, sizeof(int32_t) * (keep + 3), st));
+    std::vector<int32_t> hbuf(keep + 3);
+    std::mt19937 rng(std::random_device{}());
+    const float seeded = opt->seed >= 0 ? llmdot_cuda_sampling_seeded_draw(opt->seed) : 0.0f;
+    a.has_cap = c.has_final_cap;
+    a.cap = c.final_cap;
+    a.inv_cap = c.has_final_cap ? 1.0f / c.final_cap : 0.0f;
+    a.recent = dbuf;
+    a.recent_ld = keep;
+    a.recent_len = dbuf + keep;
+    a.out = dbuf + keep + 1;
+    a.r = (const float *)(dbuf + keep + 2);
+    a.next = w.next;  // the next decode step's input token
+    ModelExtra &x = extra(m);
+    LLMDOT_TRY(ensure_pinned(m, 1));
+    x.h_pinned[x.cap] = s->pos;
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.views, &s->view, sizeof(KvView), cudaMemcpyHostToDevice, st));
+    int rc = LLMDOT_OK, produced = 0;
+    for (int i = 0; i < max_tokens && rc == LLMDOT_OK; i++) {
+        // the logits: the last prompt row after the prefill, row 0 after each decode step
+        a.logits = w.logits + (size_t)(i == 0 ? last_row : 0) * c.vocab;
+        const int len = (int)std::min<size_t>(recent.size(), (size_t)keep);
+        std::copy(recent.end() - len, recent.end(), hbuf.begin());
+        hbuf[keep] = len;
+        float r = draws ? draws[i] : (opt->seed >= 0 ? seeded : (float)(rng() >> 8) * (1.0f / 16777216.0f));
+        memcpy(&hbuf[keep + 2], &r, sizeof(float));
+        if (cudaMemcpyAsync(dbuf, hbuf.data(), sizeof(int32_t) * (keep + 3), cudaMemcpyHostToDevice, st) != cudaSuccess) {
+            rc = cuda_fail(cudaGetLastError(), "generate_sampled upload");
+            break;
+        }
+        rc = launch_sample(a, 1, st);
+        if (rc != LLMDOT_OK) break;
+        int32_t tok = 0;
+        if (cudaMemcpyAsync(x.h_pinned + 2 * x.cap, a.out, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess) {
+            rc = cuda_fail(cudaGetLastError(), "generate_sampled step");
+            break;
+        }
+        tok = x.h_pinned[2 * x.cap];
+        out_tokens[produced++] = tok;
+        recent.push_back(tok);
+        if (recent.size() > (size_t)keep) recent.erase(recent.begin(), recent.end() - keep);
+        if (tok == c.eos || produced == max_tokens) break;
+        if (s->pos >= s->max_ctx) {
+            rc = fail(LLMDOT_E_INVALID, "generate_sampled: context length exceeded");
+            break;
+        }
+        if (cudaGraphLaunch(g, st) != cudaSuccess) {
+            rc = cuda_fail(cudaGetLastError(), "generate_sampled decode");
+            break;
+        }
+        s->pos += 1;
+    }
+    cudaFreeAsync(dbuf, st);
+    cudaStreamSynchronize(st);
+    if (rc == LLMDOT_OK) rc = check_err_flag(m);
+    *n_out = produced;
+    return rc;
 }
 
 extern "C" int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, const int32_t *tokens, int n_steps,

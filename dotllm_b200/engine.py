@@ -147,6 +147,21 @@ class CudaSession:
                                          out.ctypes.data_as(I32P), C.byref(n)))
         return out[:n.value]
 
+    def generate_sampled(self, prompt, max_tokens: int, options, draws=None) -> np.ndarray:
+        """Generate with Sampler.Sample on the device (llmdot_cuda_generate_sampled).  options:
+        native.LlmdotSampling; draws: per-token uniform draws (default: seeded / fresh)."""
+        from .native import LlmdotSampling
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max(max_tokens, 1), dtype=np.int32)
+        n = C.c_int()
+        o = LlmdotSampling(options.top_k, options.top_p, options.temperature, options.repeat_penalty,
+                           options.repeat_window, options.seed)
+        d = None if draws is None else np.ascontiguousarray(draws, dtype=np.float32)
+        check(lib().llmdot_cuda_generate_sampled(self._h, p.ctypes.data_as(I32P), p.size, max_tokens, C.byref(o),
+                                                 d.ctypes.data_as(F32P) if d is not None else None,
+                                                 out.ctypes.data_as(I32P), C.byref(n)))
+        return out[:n.value]
+
     def close(self) -> None:
         if self._h:
             lib().llmdot_cuda_session_free(self._h)

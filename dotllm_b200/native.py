@@ -48,6 +48,15 @@ class TensorDesc(C.Structure):
                 ("data", C.c_void_p), ("n_bytes", C.c_uint64)]
 
 
+class LlmdotSampling(C.Structure):
+    """llmdot_sampling = SamplingOptions (SamplingOptions.cs:7-14), the reference's defaults."""
+    _fields_ = [("top_k", C.c_int32), ("top_p", C.c_float), ("temperature", C.c_float),
+                ("repeat_penalty", C.c_float), ("repeat_window", C.c_int32), ("seed", C.c_int32)]
+
+    def __init__(self, top_k=40, top_p=0.95, temperature=0.8, repeat_penalty=1.1, repeat_window=64, seed=-1):
+        super().__init__(top_k, top_p, temperature, repeat_penalty, repeat_window, seed)
+
+
 F32P = C.POINTER(C.c_float)
 U8P = C.POINTER(C.c_uint8)
 I32P = C.POINTER(C.c_int32)
@@ -92,6 +101,11 @@ _SIGS = {
     "llmdot_cuda_prefill": (C.c_int, [VP, I32P, C.c_int, F32P, I32P]),
     "llmdot_cuda_decode": (C.c_int, [C.POINTER(VP), C.c_int, I32P, I32P, F32P]),
     "llmdot_cuda_generate": (C.c_int, [VP, I32P, C.c_int, C.c_int, I32P, C.POINTER(C.c_int)]),
+    "llmdot_cuda_sampling_seeded_draw": (C.c_float, [C.c_int32]),
+    "llmdot_cuda_sample": (C.c_int, [VP, F32P, C.c_int, C.POINTER(LlmdotSampling), I32P, C.c_int, C.c_float,
+                                     C.POINTER(C.c_int32)]),
+    "llmdot_cuda_generate_sampled": (C.c_int, [VP, I32P, C.c_int, C.c_int, C.POINTER(LlmdotSampling), F32P, I32P,
+                                               C.POINTER(C.c_int)]),
     "llmdot_cuda_decode_steps": (C.c_int, [C.POINTER(VP), C.c_int, I32P, C.c_int, I32P, F32P, C.POINTER(C.c_int)]),
     "llmdot_cuda_model_load_gguf_tp": (C.c_int, [C.c_int, C.c_char_p, C.c_int, C.c_int, C.POINTER(VP)]),
     "llmdot_cuda_tp_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),

@@ -237,6 +237,41 @@ LLMDOT_API int llmdot_cuda_decode(llmdot_session **sessions, int batch, const in
 LLMDOT_API int llmdot_cuda_generate(llmdot_session *s, const int32_t *prompt, int n_prompt,
                                     int max_tokens, int32_t *out_tokens, int *n_out);
 
+/* SamplingOptions (src/Llmdot.Core/Sampling/SamplingOptions.cs:7-14); the reference's defaults are
+ * top_k 40, top_p 0.95, temperature 0.8, repeat_penalty 1.1, repeat_window 64, seed -1. */
+typedef struct llmdot_sampling {
+    int32_t top_k;
+    float top_p;
+    float temperature;
+    float repeat_penalty;
+    int32_t repeat_window;
+    int32_t seed; /* >= 0: every draw is new System.Random(seed).NextSingle(); < 0: fresh draws */
+} llmdot_sampling;
+
+/* new System.Random(seed).NextSingle(): the draw Sampler.SampleFromProbabilities uses for
+ * seed >= 0 (Sampler.cs:155-157).  Host only. */
+LLMDOT_API float llmdot_cuda_sampling_seeded_draw(int32_t seed);
+
+/* Sampler.Sample (Sampler.cs:24-62) for one row of host logits (vocabulary n), on the device:
+ * repeat penalty over the last repeat_window entries of recent (oldest first), scaling by
+ * 1/temperature, top-k, softmax, and the first index whose running probability reaches r (the
+ * uniform draw in [0, 1)).  temperature <= 0 is the argmax.  With temperature > 0 the device
+ * needs 0 < top_k < n and top_k <= 1024 (the top-p-only path, top_k <= 0, is
+ * LLMDOT_E_UNSUPPORTED); repeat_window <= 1024.  Exactly tied logits at the k-th place are taken
+ * lowest index first. */
+LLMDOT_API int llmdot_cuda_sample(llmdot_backend *h, const float *logits, int n, const llmdot_sampling *opt,
+                                  const int32_t *recent, int n_recent, float r, int32_t *index);
+
+/* InferenceEngine.Generate (InferenceEngine.cs:74-131) with Sampler.Sample: reset, prefill, then
+ * per token the final softcap, the sample over the device logits (history = the prompt, then every
+ * generated token, the last repeat_window + 1 kept) and the decode step, stopping after EOS or
+ * max_tokens.  draws (nullable, max_tokens entries) are the uniform draws of the tokens; null means
+ * the seeded draw for seed >= 0 and a fresh draw per token (host generator) for seed < 0.
+ * Same device limits as llmdot_cuda_sample; not under tensor parallelism. */
+LLMDOT_API int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *prompt, int n_prompt,
+                                            int max_tokens, const llmdot_sampling *opt, const float *draws,
+                                            int32_t *out_tokens, int *n_out);
+
 /* Device-resident greedy decode of n_steps tokens for `batch` sessions in lockstep (the decode
  * loop of Generate without the per-token EOS / stop-sequence check): tokens[b] is fed first, and
  * out_tokens[step * batch + b] receives every step's argmax.  Steps run as back-to-back CUDA-graph

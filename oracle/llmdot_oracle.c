@@ -1375,3 +1375,190 @@ EXPORT int orc_generate(osess *s, const int *prompt, int nPrompt, int maxTokens,
     free(lg);
     return generated;
 }
+
+
+/* ---------------------------------------------------------------- sampling
+ * Sampler.Sample (src/Llmdot.Core/Sampling/Sampler.cs:24-62) with SamplingOptions
+ * (SamplingOptions.cs:7-14).  The uniform draw r is the caller's: Sampler takes
+ * Random(seed).NextSingle() for seed >= 0 (orc_net_random_single) and Random.Shared otherwise. */
+
+/* ApplyRepeatPenalty :64-81: the last `window` tokens of the history, in order, each applied once */
+static void repeat_penalty(float *x, int n, float penalty, int window, const int *recent, int nRecent)
+{
+    if (penalty == 1.0f || nRecent == 0 || window <= 0) return;
+    int start = nRecent - window > 0 ? nRecent - window : 0;
+    for (int i = start; i < nRecent; i++) {
+        int t = recent[i];
+        if (t >= 0 && t < n) {
+            if (x[t] > 0) x[t] = x[t] / penalty;
+            else x[t] = x[t] * penalty;
+        }
+    }
+}
+
+/* FindTopK :83-127: the first k entries seed the set; a later entry replaces the first minimum
+ * of the set when it is strictly larger; then an insertion sort, descending */
+static void find_top_k(const float *x, int n, int k, int *idx, float *val)
+{
+    for (int i = 0; i < k; i++) { idx[i] = i; val[i] = x[i]; }
+    for (int i = k; i < n; i++) {
+        int mi = 0;
+        for (int j = 1; j < k; j++) if (val[j] < val[mi]) mi = j;
+        if (x[i] > val[mi]) { idx[mi] = i; val[mi] = x[i]; }
+    }
+    for (int i = 1; i < k; i++) {
+        int ki = idx[i];
+        float kv = val[i];
+        int j = i - 1;
+        while (j >= 0 && val[j] < kv) { idx[j + 1] = idx[j]; val[j + 1] = val[j]; j--; }
+        idx[j + 1] = ki;
+        val[j + 1] = kv;
+    }
+}
+
+/* FindNucleus :129-151: selection sort by probability, descending, then the prefix whose
+ * running sum first reaches top_p */
+static int find_nucleus(const float *p, int n, float topP, int *idx, float *val)
+{
+    for (int i = 0; i < n; i++) idx[i] = i;
+    for (int i = 0; i < n - 1; i++) {
+        int mx = i;
+        for (int j = i + 1; j < n; j++) if (p[idx[j]] > p[idx[mx]]) mx = j;
+        if (mx != i) { int t = idx[i]; idx[i] = idx[mx]; idx[mx] = t; }
+    }
+    float cum = 0.0f;
+    int count = 0;
+    for (int i = 0; i < n; i++) {
+        val[i] = p[idx[i]];
+        cum += val[i];
+        count++;
+        if (cum >= topP) break;
+    }
+    return count;
+}
+
+/* SampleFromProbabilities :153-165 */
+static int pick(const float *p, int n, float r)
+{
+    float cum = 0.0f;
+    for (int i = 0; i < n; i++) {
+        cum += p[i];
+        if (r <= cum) return i;
+    }
+    return n - 1;
+}
+
+EXPORT int orc_sample(const float *logits, int n, int topK, float topP, float temperature, float penalty, int window,
+                      const int *recent, int nRecent, float r)
+{
+    if (temperature <= 0.0f) return orc_argmax(logits, n);
+    float *x = (float *)malloc(sizeof(float) * n * 2);
+    int *idx = (int *)malloc(sizeof(int) * n);
+    memcpy(x, logits, sizeof(float) * n);
+    repeat_penalty(x, n, penalty, window, recent, nRecent);
+    float s = 1.0f / temperature;
+    for (int i = 0; i < n; i++) x[i] = x[i] * s; /* VectorMath.Scale: x * s in every lane */
+    int out;
+    if (topK > 0 && topK < n) {
+        float *val = x + n;
+        find_top_k(x, n, topK, idx, val);
+        orc_softmax(val, topK, 0, 0.0f);
+        out = idx[pick(val, topK, r)];
+    } else {
+        orc_softmax(x, n, 0, 0.0f);
+        out = -1;
+        if (topP < 1.0f) {
+            float *val = x + n;
+            int ns = find_nucleus(x, n, topP, idx, val);
+            if (ns < n) {
+                float sum = 0.0f;
+                for (int i = 0; i < ns; i++) sum += val[i];
+                float inv = 1.0f / sum;
+                for (int i = 0; i < ns; i++) val[i] = val[i] * inv;
+                out = idx[pick(val, ns, r)];
+            }
+        }
+        if (out < 0) out = pick(x, n, r);
+    }
+    free(x);
+    free(idx);
+    return out;
+}
+
+/* new System.Random(seed).NextSingle(): the seeded generator is Knuth's subtractive generator
+ * (the .NET 5-compatible seeded implementation), NextSingle = (float)(sample / int.MaxValue).
+ * Restated from the published algorithm; not checked against .NET here (no runtime). */
+EXPORT float orc_net_random_single(int seed)
+{
+    const int MBIG = 2147483647, MSEED = 161803398;
+    int sa[56];
+    memset(sa, 0, sizeof(sa));
+    int sub = seed == (-2147483647 - 1) ? 2147483647 : (seed < 0 ? -seed : seed);
+    int mj = MSEED - sub;
+    sa[55] = mj;
+    int mk = 1;
+    for (int i = 1; i < 55; i++) {
+        int ii = (21 * i) % 55;
+        sa[ii] = mk;
+        mk = mj - mk;
+        if (mk < 0) mk += MBIG;
+        mj = sa[ii];
+    }
+    for (int k = 1; k < 5; k++)
+        for (int i = 1; i < 56; i++) {
+            sa[i] -= sa[1 + (i + 30) % 55];
+            if (sa[i] < 0) sa[i] += MBIG;
+        }
+    int inext = 1, inextp = 22; /* 0 and 21, advanced once */
+    int ret = sa[inext] - sa[inextp];
+    if (ret == MBIG) ret--;
+    if (ret < 0) ret += MBIG;
+    return (float)(ret * (1.0 / MBIG));
+}
+
+/* Generate (InferenceEngine.cs:74-131) with Sampler.Sample: the history starts as the prompt
+ * and keeps the last window + 1 tokens; r[i] is the draw for generated token i */
+EXPORT int orc_generate_sampled(osess *s, const int *prompt, int nPrompt, int maxTokens, int topK, float topP,
+                                float temperature, float penalty, int window, const float *r, int *outTokens)
+{
+    omodel *m = s->m;
+    orc_config *c = &m->cfg;
+    s->pos = 0;
+    int have = 0;
+    for (int i = 0; i < nPrompt; i++) {
+        if (orc_process_token(s, prompt[i], i)) return -1;
+        s->pos++;
+        have = 1;
+    }
+    if (!have) {
+        int init = c->bos > 0 ? c->bos : 0;
+        if (orc_process_token(s, init, 0)) return -1;
+        s->pos++;
+    }
+    int cap = nPrompt + maxTokens + 1;
+    int *recent = (int *)malloc(sizeof(int) * (cap > 1 ? cap : 1));
+    int nRecent = 0;
+    for (int i = 0; i < nPrompt; i++) recent[nRecent++] = prompt[i];
+    float *lg = (float *)malloc(sizeof(float) * c->vocab);
+    int generated = 0;
+    while (generated < maxTokens) {
+        memcpy(lg, s->logits, sizeof(float) * c->vocab);
+        if (c->has_final_cap) orc_softcap(lg, c->vocab, c->final_cap);
+        int next = orc_sample(lg, c->vocab, topK, topP, temperature, penalty, window, recent, nRecent, r[generated]);
+        recent[nRecent++] = next;
+        if (nRecent > window + 1) {
+            int drop = nRecent - window - 1;
+            memmove(recent, recent + drop, sizeof(int) * (nRecent - drop));
+            nRecent -= drop;
+        }
+        outTokens[generated] = next;
+        if (next == c->eos) { generated++; break; }
+        if (generated + 1 == maxTokens) { generated++; break; }
+        if (orc_process_token(s, next, s->pos)) { free(lg); free(recent); return -1; }
+        s->pos++;
+        generated++;
+    }
+    free(lg);
+    free(recent);
+    return generated;
+}

@@ -94,6 +94,12 @@ def lib():
         L.orc_session_hidden.restype = F32P
         L.orc_session_hidden.argtypes = [C.c_void_p]
         L.orc_generate.argtypes = [C.c_void_p, I32P, C.c_int, C.c_int, I32P, F32P]
+        L.orc_sample.argtypes = [F32P, C.c_int, C.c_int, C.c_float, C.c_float, C.c_float, C.c_int, I32P, C.c_int,
+                                 C.c_float]
+        L.orc_net_random_single.restype = C.c_float
+        L.orc_net_random_single.argtypes = [C.c_int]
+        L.orc_generate_sampled.argtypes = [C.c_void_p, I32P, C.c_int, C.c_int, C.c_int, C.c_float, C.c_float,
+                                           C.c_float, C.c_int, F32P, I32P]
         _lib = L
     return _lib
 
@@ -284,6 +290,31 @@ class Model:
             pass
 
 
+class SamplingOptions:
+    """SamplingOptions (src/Llmdot.Core/Sampling/SamplingOptions.cs:7-14), same defaults."""
+
+    def __init__(self, top_k=40, top_p=0.95, temperature=0.8, repeat_penalty=1.1, repeat_window=64, seed=-1):
+        self.top_k, self.top_p, self.temperature = int(top_k), float(top_p), float(temperature)
+        self.repeat_penalty, self.repeat_window, self.seed = float(repeat_penalty), int(repeat_window), int(seed)
+
+
+def net_random_single(seed: int) -> float:
+    """new System.Random(seed).NextSingle() (restated, see the C source)."""
+    return float(lib().orc_net_random_single(int(seed)))
+
+
+def sample(logits, opts: SamplingOptions, recent=(), r: float = None) -> int:
+    """Sampler.Sample (Sampler.cs:24-62).  r defaults to the seeded draw (opts.seed >= 0)."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    rec = np.ascontiguousarray(recent, dtype=np.int32)
+    if r is None:
+        if opts.seed < 0:
+            raise ValueError("an unseeded draw needs r")
+        r = net_random_single(opts.seed)
+    return int(lib().orc_sample(_f(x), x.size, opts.top_k, opts.top_p, opts.temperature, opts.repeat_penalty,
+                                opts.repeat_window, rec.ctypes.data_as(I32P), rec.size, float(r)))
+
+
 class Session:
     """One InferenceEngine's KvCache + buffers over a Model."""
 
@@ -298,6 +329,20 @@ class Session:
             raise RuntimeError(lib().orc_last_error().decode())
         V = self.model.config["vocab"]
         return np.ctypeslib.as_array(lib().orc_session_logits(self._h), shape=(V,)).copy()
+
+    def generate_sampled(self, prompt, max_tokens: int, opts: SamplingOptions, r=None):
+        """Generate with Sampler.Sample; r[i] is the draw for token i (the seeded draw when omitted)."""
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        if r is None:
+            r = np.full(max(max_tokens, 1), net_random_single(opts.seed), dtype=np.float32)
+        r = np.ascontiguousarray(r, dtype=np.float32)
+        out = np.zeros(max(max_tokens, 1), dtype=np.int32)
+        n = lib().orc_generate_sampled(self._h, prompt.ctypes.data_as(I32P), prompt.size, max_tokens, opts.top_k,
+                                       opts.top_p, opts.temperature, opts.repeat_penalty, opts.repeat_window, _f(r),
+                                       out.ctypes.data_as(I32P))
+        if n < 0:
+            raise RuntimeError(lib().orc_last_error().decode())
+        return out[:n]
 
     def generate(self, prompt, max_tokens: int, want_logits: bool = False):
         prompt = np.ascontiguousarray(prompt, dtype=np.int32)

@@ -1,0 +1,101 @@
+"""Sampler.Sample on the device (llmdot_cuda_sample, llmdot_cuda_generate_sampled) against the
+oracle's restatement (Sampler.cs:24-165), on the same logits, history and uniform draws.
+
+Logits are continuous random values, so no two tie; the sampled index must be identical.  A draw
+that lands within float rounding of a cumulative-probability boundary could in principle pick
+the neighbour, so the draws are kept away from the boundaries the oracle reports.
+"""
+import numpy as np
+import pytest
+
+from dotllm_b200 import synth
+from dotllm_b200.native import CudaBackendError, LlmdotSampling
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _opts(**kw):
+    return LlmdotSampling(**kw)
+
+
+def _oracle_opts(o):
+    return O.SamplingOptions(o.top_k, o.top_p, o.temperature, o.repeat_penalty, o.repeat_window, o.seed)
+
+
+CASES = [
+    dict(top_k=40, top_p=0.95, temperature=0.8, repeat_penalty=1.1, repeat_window=64),  # the defaults
+    dict(top_k=1, top_p=1.0, temperature=1.0, repeat_penalty=1.0, repeat_window=0),
+    dict(top_k=5, top_p=1.0, temperature=0.5, repeat_penalty=2.0, repeat_window=8),
+    dict(top_k=200, top_p=1.0, temperature=1.5, repeat_penalty=1.3, repeat_window=64),
+    dict(top_k=1024, top_p=1.0, temperature=2.0, repeat_penalty=1.0, repeat_window=64),
+    dict(top_k=3, top_p=1.0, temperature=0.0, repeat_penalty=1.5, repeat_window=64),  # greedy
+]
+
+
+@pytest.mark.parametrize("vocab", [1000, 32064, 128256])
+@pytest.mark.parametrize("case", range(len(CASES)))
+def test_sample_matches_oracle(backend, vocab, case):
+    rng = np.random.default_rng(1000 * case + vocab)
+    o = _opts(**CASES[case])
+    if o.top_k >= vocab:
+        pytest.skip("top_k beyond the vocabulary")
+    for trial in range(4):
+        logits = (rng.standard_normal(vocab) * 3.0).astype(np.float32)
+        # a history with repeats and negative logits among the penalised tokens
+        recent = rng.integers(0, vocab, size=30).astype(np.int32)
+        recent[5] = recent[9] = recent[20]
+        logits[recent[:4]] = -np.abs(logits[recent[:4]])
+        r = float(rng.uniform(0.02, 0.98))
+        want = O.sample(logits, _oracle_opts(o), recent, r)
+        got = backend.sample(logits, o, recent, r)
+        assert got == want, (vocab, CASES[case], trial, got, want)
+
+
+def test_sample_seeded_draw_and_errors(backend):
+    logits = np.random.default_rng(5).standard_normal(5000).astype(np.float32)
+    o = _opts(seed=42)
+    want = O.sample(logits, _oracle_opts(o), [])
+    assert backend.sample(logits, o, []) == want
+    with pytest.raises(CudaBackendError):  # top-p only: not on the device
+        backend.sample(logits, _opts(top_k=0, top_p=0.9, temperature=1.0), [], 0.5)
+    with pytest.raises(CudaBackendError):  # top_k must stay below the vocabulary
+        backend.sample(logits, _opts(top_k=5000, temperature=1.0), [], 0.5)
+
+
+@pytest.mark.parametrize("name", ["micro", "micro-gemma", "tiny"])
+def test_generate_sampled_matches_oracle(gpu, name):
+    from dotllm_b200.engine import CudaModel
+    cfg = synth.get(name)
+    path = synth.build_model(cfg)
+    prompt = synth.prompt_tokens(cfg)
+    steps = 24
+    rng = np.random.default_rng(77)
+    draws = rng.uniform(0.02, 0.98, size=steps).astype(np.float32)
+    o = _opts(top_k=40, top_p=0.95, temperature=0.8, repeat_penalty=1.1, repeat_window=16)
+    om = O.Model(path)
+    os_ = O.Session(om)
+    try:
+        want = list(os_.generate_sampled(prompt, steps, _oracle_opts(o), draws))
+    finally:
+        os_.close()
+        om.close()
+    m = CudaModel.load(path)
+    try:
+        s = m.session(kv="f32")
+        got = list(s.generate_sampled(prompt, steps, o, draws))
+        assert got == want
+        # a second call resets the session and draws the same tokens
+        assert list(s.generate_sampled(prompt, steps, o, draws)) == want
+        # the seeded draw when no draws are given
+        seeded = _opts(top_k=40, top_p=0.95, temperature=0.8, repeat_penalty=1.1, repeat_window=16, seed=7)
+        os_ = O.Session(om := O.Model(path))
+        try:
+            want7 = list(os_.generate_sampled(prompt, 8, _oracle_opts(seeded)))
+        finally:
+            os_.close()
+            om.close()
+        assert list(s.generate_sampled(prompt, 8, seeded)) == want7
+        s.close()
+    finally:
+        m.close()
