@@ -246,6 +246,7 @@ def main():
                          f"llmdot's managed CPU path (oracle/), 1 thread"}
 
     from dotllm_b200.engine import CudaModel, decode_batch, tp_unique_id
+    t_load = time.perf_counter()
     if args.tp:
         m = CudaModel.load_tp(path, world, rank, device=local)
         uid = [tp_unique_id() if rank == 0 else None]
@@ -253,6 +254,7 @@ def main():
         m.tp_init(uid[0])
     else:
         m = CudaModel.load(path, device=local)
+    load_s = time.perf_counter() - t_load
     ctx = min(cfg.context, 4096) if args.config == "llama1b" else cfg.context
     B = args.batch
     sessions, cur, dev_ms, kps, prefill_s, clk = measure(m, cfg, args, B, n_prompt, ctx, rank, args.steps, dist,
@@ -344,6 +346,7 @@ def main():
         "kernels_per_step": kps,
         "clocks": clk.summary(),
         "prefill_tok_s": B * ranks_tokens * n_prompt / prefill_s,
+        "load_s": load_s,
         "sharded_batch32": b32,
     }
     m.close()
