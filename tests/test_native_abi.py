@@ -46,3 +46,10 @@ def test_no_cpu_fallback_without_device():
     with pytest.raises(native.CudaBackendError):
         from dotllm_b200.backend import CudaBackend
         CudaBackend(0)
+
+
+def test_seeded_draw_matches_oracle():
+    """llmdot_cuda_sampling_seeded_draw (host only) is the oracle's new Random(seed).NextSingle()."""
+    from oracle import oracle as O
+    for seed in (0, 1, 7, 42, 99, 12345, -5, 2147483647):
+        assert native.lib().llmdot_cuda_sampling_seeded_draw(seed) == O.net_random_single(seed)
