@@ -21,10 +21,14 @@
 
 namespace llmdot {
 
-constexpr int SMP_THREADS = 256;
+constexpr int SMP_THREADS = 1024;
+constexpr int SMP_UNROLL = 4;  // row values loaded per thread before any is used (loads in flight)
+
+constexpr int SMP_CAND = 4096;     // candidates the sampled threshold may collect
+constexpr int SMP_SAMPLES = 2048;  // keys of the strided sample that places the threshold
 
 struct SampleSmem {
-    int bitmap, ptok, pval, hist, cand, prob, total;  // byte offsets
+    int bitmap, ptok, pval, hist, cand, skey, prob, total;  // byte offsets
 };
 __host__ __device__ inline SampleSmem sample_layout(int n, int window, int k2)
 {
@@ -38,8 +42,10 @@ __host__ __device__ inline SampleSmem sample_layout(int n, int window, int k2)
     o += (window * 4 + 15) / 16 * 16;
     L.hist = o;  // radix histogram, then scan state
     o += 260 * 4;
-    L.cand = o;  // k2 (key << 32 | ~index) pairs
-    o += k2 * 8;
+    L.cand = o;  // (key << 32 | ~index) pairs: the candidates, at least k2
+    o += (k2 > SMP_CAND ? k2 : SMP_CAND) * 8;
+    L.skey = o;  // strided sample of the row's keys
+    o += SMP_SAMPLES * 4;
     L.prob = o;  // k probabilities
     o += k2 * 4;
     L.total = o;
@@ -57,6 +63,7 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
     float *pval = (float *)(smem + L.pval);
     int *hist = (int *)(smem + L.hist);
     unsigned long long *cand = (unsigned long long *)(smem + L.cand);
+    uint32_t *skey = (uint32_t *)(smem + L.skey);
     float *prob = (float *)(smem + L.prob);
     const float *x = a.logits + (size_t)row * a.ld;
     const int nvec = n - n % 8;
@@ -67,9 +74,20 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
 
     if (a.temperature <= 0.0f) {  // Temperature <= 0: ArgMax (Sampler.cs:26-27)
         unsigned long long best = 0;
-        for (int i = tid; i < n; i += SMP_THREADS) {
-            const unsigned long long kk = ((unsigned long long)float_key(capped(i)) << 32) | (uint32_t)~i;
-            best = kk > best ? kk : best;
+        for (int base = 0; base < n; base += SMP_THREADS * SMP_UNROLL) {
+            float vals[SMP_UNROLL];
+#pragma unroll
+            for (int u = 0; u < SMP_UNROLL; u++) {
+                const int i = base + u * SMP_THREADS + tid;
+                vals[u] = i < n ? capped(i) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < SMP_UNROLL; u++) {
+                const int i = base + u * SMP_THREADS + tid;
+                if (i >= n) continue;
+                const unsigned long long kk = ((unsigned long long)float_key(vals[u]) << 32) | (uint32_t)~i;
+                best = kk > best ? kk : best;
+            }
         }
         for (int o = 16; o > 0; o >>= 1) {
             const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
@@ -125,16 +143,92 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
         return __fmul_rn(v, a.inv_temp);
     };
 
-    // ---- radix select of the k-th largest key
     const int k = a.top_k;
+    int sort_n = k2;  // entries of cand to sort
+    bool fast = false;
+    // ---- fast path: a threshold tau from a strided sample, then one pass collecting every key
+    // >= tau.  When at least k keys reach tau, the k largest (ties included) are all among them,
+    // so sorting the candidates gives exactly the radix select's answer; otherwise (tau above
+    // the k-th key, or more than SMP_CAND candidates) the radix select below runs.
+    {
+        const int ns = n < SMP_SAMPLES ? n : SMP_SAMPLES;
+        for (int j = tid; j < SMP_SAMPLES; j += SMP_THREADS)
+            skey[j] = j < ns ? float_key(value((int)((long long)j * n / ns))) : 0u;
+        if (tid == 0) {
+            hist[0] = 0;
+            hist[1] = 0;
+        }
+        __syncthreads();
+        for (int size = 2; size <= SMP_SAMPLES; size <<= 1)  // sort the sample, descending
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                for (int i = tid; i < SMP_SAMPLES / 2; i += SMP_THREADS) {
+                    const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+                    const bool desc = (lo & size) == 0;
+                    const uint32_t A = skey[lo], B = skey[hi];
+                    if ((A < B) == desc) {
+                        skey[lo] = B;
+                        skey[hi] = A;
+                    }
+                }
+                __syncthreads();
+            }
+        // about 2k + a margin of the row's keys are expected at or above the sample's r-th key
+        const int rk = (int)(((long long)2 * k * ns + n - 1) / n) + 4;
+        const uint32_t tau = skey[rk < ns ? rk : ns - 1];
+        for (int base = 0; base < n; base += SMP_THREADS * SMP_UNROLL) {
+            uint32_t keys[SMP_UNROLL];
+#pragma unroll
+            for (int u = 0; u < SMP_UNROLL; u++) {
+                const int i = base + u * SMP_THREADS + tid;
+                keys[u] = i < n ? float_key(value(i)) : 0u;
+            }
+#pragma unroll
+            for (int u = 0; u < SMP_UNROLL; u++) {
+                const int i = base + u * SMP_THREADS + tid;
+                if (i < n && keys[u] >= tau) {
+                    const int slot = atomicAdd(&hist[0], 1);
+                    if (slot < SMP_CAND) cand[slot] = ((unsigned long long)keys[u] << 32) | (uint32_t)~i;
+                }
+            }
+        }
+        __syncthreads();
+        const int got = hist[0];
+        __syncthreads();
+        if (got >= k && got <= SMP_CAND) {
+            int c2 = k2;
+            while (c2 < got) c2 <<= 1;
+            for (int i = got + tid; i < c2; i += SMP_THREADS) cand[i] = 0ull;
+            __syncthreads();
+            sort_n = c2;
+            fast = true;
+        }
+    }
+    if (!fast) {  // uniform: every thread read the same count
+    // ---- radix select of the k-th largest key
     uint32_t prefix = 0, mask = 0;
     int need = k;  // rank wanted inside the current prefix
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int i = tid; i < 256; i += SMP_THREADS) hist[i] = 0;
         __syncthreads();
-        for (int i = tid; i < n; i += SMP_THREADS) {
-            const uint32_t key = float_key(value(i));
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+        // nearly every logit shares the top key byte: lanes with the same bin add once per warp
+        for (int base = 0; base < n; base += SMP_THREADS * SMP_UNROLL) {
+            uint32_t keys[SMP_UNROLL];
+#pragma unroll
+            for (int u = 0; u < SMP_UNROLL; u++) {
+                const int i = base + u * SMP_THREADS + tid;
+                keys[u] = i < n ? float_key(value(i)) : 0u;
+            }
+#pragma unroll
+            for (int u = 0; u < SMP_UNROLL; u++) {
+                const int i = base + u * SMP_THREADS + tid;
+                const bool act = i < n && (keys[u] & mask) == prefix;
+                const unsigned am = __ballot_sync(0xffffffffu, act);
+                if (act) {
+                    const uint32_t bin = (keys[u] >> shift) & 255u;
+                    const unsigned same = __match_any_sync(am, bin);
+                    if ((tid & 31) == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
+                }
+            }
         }
         __syncthreads();
         if (tid == 0) {
@@ -159,11 +253,20 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
     if (tid == 0) hist[0] = 0;
     for (int i = tid; i < k2; i += SMP_THREADS) cand[i] = 0ull;
     __syncthreads();
-    for (int i = tid; i < n; i += SMP_THREADS) {
-        const uint32_t key = float_key(value(i));
-        if (key > thr || (key == thr && eq_take == eq_total)) {
-            const int slot = atomicAdd(&hist[0], 1);
-            cand[slot] = ((unsigned long long)key << 32) | (uint32_t)~i;
+    for (int base = 0; base < n; base += SMP_THREADS * SMP_UNROLL) {
+        uint32_t keys[SMP_UNROLL];
+#pragma unroll
+        for (int u = 0; u < SMP_UNROLL; u++) {
+            const int i = base + u * SMP_THREADS + tid;
+            keys[u] = i < n ? float_key(value(i)) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < SMP_UNROLL; u++) {
+            const int i = base + u * SMP_THREADS + tid;
+            if (i < n && (keys[u] > thr || (keys[u] == thr && eq_take == eq_total))) {
+                const int slot = atomicAdd(&hist[0], 1);
+                cand[slot] = ((unsigned long long)keys[u] << 32) | (uint32_t)~i;
+            }
         }
     }
     __syncthreads();
@@ -178,10 +281,11 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
         }
         __syncthreads();
     }
-    // ---- bitonic sort, descending: by value, then by lower index
-    for (int size = 2; size <= k2; size <<= 1)
+    }
+    // ---- bitonic sort, descending: by value, then by lower index (the first k are the winners)
+    for (int size = 2; size <= sort_n; size <<= 1)
         for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = tid; i < k2 / 2; i += SMP_THREADS) {
+            for (int i = tid; i < sort_n / 2; i += SMP_THREADS) {
                 const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
                 const bool desc = (lo & size) == 0;
                 const unsigned long long A = cand[lo], B = cand[hi];
