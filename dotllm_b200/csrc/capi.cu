@@ -1044,7 +1044,13 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
     // device: [history (keep)] [length] [out] [r]
     int32_t *dbuf = nullptr;
     LLMDOT_CUDA_TRY(cudaMallocAsync(&dbuf, sizeof(int32_t) * (keep + 3), st));
-    std::vector<int32_t> hbuf(keep + 3);
+    // pinned: the per-token upload is then a plain DMA instead of the driver's pageable staging
+    int32_t *hbuf = nullptr;
+    if (cudaMallocHost(&hbuf, sizeof(int32_t) * (keep + 3)) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFreeAsync(dbuf, st);
+        return fail(LLMDOT_E_NOMEM, "generate_sampled: pinned staging allocation failed");
+    }
     std::mt19937 rng(std::random_device{}());
     const float seeded = opt->seed >= 0 ? llmdot_cuda_sampling_seeded_draw(opt->seed) : 0.0f;
     a.has_cap = c.has_final_cap;
@@ -1066,11 +1072,11 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
         // the logits: the last prompt row after the prefill, row 0 after each decode step
         a.logits = w.logits + (size_t)(i == 0 ? last_row : 0) * c.vocab;
         const int len = (int)std::min<size_t>(recent.size(), (size_t)keep);
-        std::copy(recent.end() - len, recent.end(), hbuf.begin());
+        std::copy(recent.end() - len, recent.end(), hbuf);
         hbuf[keep] = len;
         float r = draws ? draws[i] : (opt->seed >= 0 ? seeded : (float)(rng() >> 8) * (1.0f / 16777216.0f));
         memcpy(&hbuf[keep + 2], &r, sizeof(float));
-        if (cudaMemcpyAsync(dbuf, hbuf.data(), sizeof(int32_t) * (keep + 3), cudaMemcpyHostToDevice, st) != cudaSuccess) {
+        if (cudaMemcpyAsync(dbuf, hbuf, sizeof(int32_t) * (keep + 3), cudaMemcpyHostToDevice, st) != cudaSuccess) {
             rc = cuda_fail(cudaGetLastError(), "generate_sampled upload");
             break;
         }
@@ -1099,6 +1105,7 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
     }
     cudaFreeAsync(dbuf, st);
     cudaStreamSynchronize(st);
+    cudaFreeHost(hbuf);
     if (rc == LLMDOT_OK) rc = check_err_flag(m);
     *n_out = produced;
     return rc;

@@ -104,27 +104,33 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
         return;
     }
 
-    // ---- repeat penalty (ApplyRepeatPenalty :64-81): the last `window` tokens, in order
+    // ---- repeat penalty (ApplyRepeatPenalty :64-81): the last `window` tokens, in order.  The
+    // window's values are loaded in parallel (into the candidate buffer, not yet in use);
+    // one thread then applies the penalty occurrence by occurrence.
     for (int i = tid; i < (n + 31) / 32; i += SMP_THREADS) bitmap[i] = 0u;
+    const bool pen = a.penalty != 1.0f && window > 0 && a.recent;
+    const int plen = pen ? a.recent_len[row] : 0, p0 = max(0, plen - window);
+    const int32_t *rec = pen ? a.recent + (size_t)row * a.recent_ld : nullptr;
+    float *wval = (float *)cand;  // window values, index i - p0 (the candidates come later)
+    for (int i = p0 + tid; i < plen; i += SMP_THREADS) {
+        const int t = rec[i];
+        wval[i - p0] = (t >= 0 && t < n) ? capped(t) : 0.0f;
+    }
     __syncthreads();
     if (tid == 0) {
         int np = 0;
-        if (a.penalty != 1.0f && window > 0 && a.recent) {
-            const int len = a.recent_len[row];
-            const int32_t *rec = a.recent + (size_t)row * a.recent_ld;
-            for (int i = max(0, len - window); i < len; i++) {
-                const int t = rec[i];
-                if (t < 0 || t >= n) continue;
-                int j = 0;
-                while (j < np && ptok[j] != t) j++;
-                if (j == np) {
-                    ptok[np] = t;
-                    pval[np] = capped(t);
-                    np++;
-                    bitmap[t >> 5] |= 1u << (t & 31);
-                }
-                pval[j] = pval[j] > 0.0f ? __fdiv_rn(pval[j], a.penalty) : __fmul_rn(pval[j], a.penalty);
+        for (int i = p0; i < plen; i++) {
+            const int t = rec[i];
+            if (t < 0 || t >= n) continue;
+            int j = 0;
+            while (j < np && ptok[j] != t) j++;
+            if (j == np) {
+                ptok[np] = t;
+                pval[np] = wval[i - p0];
+                np++;
+                bitmap[t >> 5] |= 1u << (t & 31);
             }
+            pval[j] = pval[j] > 0.0f ? __fdiv_rn(pval[j], a.penalty) : __fmul_rn(pval[j], a.penalty);
         }
         hist[256] = np;
     }
