@@ -53,3 +53,28 @@ def test_seeded_draw_matches_oracle():
     from oracle import oracle as O
     for seed in (0, 1, 7, 42, 99, 12345, -5, 2147483647):
         assert native.lib().llmdot_cuda_sampling_seeded_draw(seed) == O.net_random_single(seed)
+
+
+def test_header_is_plain_c99(tmp_path):
+    """The boundary is a C ABI: the header compiles as strict C99 and the sampling struct has
+    the layout the ctypes binding uses."""
+    import os
+    hdr = native.HEADER
+    out = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-fsyntax-only", "-x", "c", hdr],
+                         capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
+    src = tmp_path / "size.c"
+    src.write_text(f'#include "{os.path.abspath(hdr)}"\n#include <stdio.h>\n'
+                   'int main(void) { printf("%zu %zu", sizeof(llmdot_sampling), sizeof(llmdot_config)); return 0; }\n')
+    exe = tmp_path / "size"
+    subprocess.run(["gcc", "-std=c99", str(src), "-o", str(exe)], check=True)
+    s_sampling, s_config = map(int, subprocess.run([str(exe)], capture_output=True, text=True).stdout.split())
+    assert s_sampling == C.sizeof(native.LlmdotSampling)
+    assert s_config == C.sizeof(native.LlmdotConfig)
+
+
+def test_sampling_defaults_are_the_references():
+    """SamplingOptions.cs:7-14: TopK 40, TopP 0.95, Temperature 0.8, RepeatPenalty 1.1, window 64, Seed -1."""
+    o = native.LlmdotSampling()
+    assert (o.top_k, o.repeat_window, o.seed) == (40, 64, -1)
+    assert (o.top_p, o.temperature, o.repeat_penalty) == (pytest.approx(0.95), pytest.approx(0.8), pytest.approx(1.1))
