@@ -10,8 +10,12 @@
   greedy_tokens.json  greedy token ids and logit checksums produced by the CPU
                     oracle for the small synthetic models (regression pins for
                     the oracle itself).
+  sampled_tokens.json  token ids of the oracle's Generate with Sampler.Sample on
+                    the same models: seeded (one draw, new Random(42).NextSingle())
+                    and with per-token draws listed in the file.
 
-Run:  python tests/golden/make_golden.py
+Run:  python tests/golden/make_golden.py            (every fixture)
+      python tests/golden/make_golden.py sampled    (sampled_tokens.json only)
 """
 from __future__ import annotations
 
@@ -283,9 +287,35 @@ def make_greedy() -> dict:
     return res
 
 
+SAMPLED_OPTIONS = dict(top_k=40, top_p=0.95, temperature=0.8, repeat_penalty=1.1, repeat_window=16)
+
+
+def make_sampled() -> dict:
+    from dotllm_b200 import synth
+    from oracle import oracle as O
+    O.set_threads(max(1, O.max_threads()))
+    res = {"options": SAMPLED_OPTIONS}
+    for name, steps in [("micro", 16), ("micro-gemma", 16), ("tiny", 32)]:
+        cfg = synth.get(name)
+        m = O.Model(synth.build_model(cfg))
+        s = O.Session(m)
+        prompt = synth.prompt_tokens(cfg)
+        seeded = s.generate_sampled(prompt, steps, O.SamplingOptions(seed=42, **SAMPLED_OPTIONS))
+        draws = np.random.default_rng(2024).uniform(0.0, 1.0, size=steps).astype(np.float32)
+        drawn = s.generate_sampled(prompt, steps, O.SamplingOptions(**SAMPLED_OPTIONS), draws)
+        res[name] = dict(steps=steps, seed=42, seeded_tokens=[int(t) for t in seeded],
+                         draws=[float(x) for x in draws], drawn_tokens=[int(t) for t in drawn])
+        s.close()
+        m.close()
+    return res
+
+
 if __name__ == "__main__":
-    with open(os.path.join(HERE, "kquant_kat.json"), "w") as f:
-        json.dump(make_kquant(), f, indent=1)
-    with open(os.path.join(HERE, "greedy_tokens.json"), "w") as f:
-        json.dump(make_greedy(), f, indent=1)
+    if len(sys.argv) < 2 or sys.argv[1] != "sampled":
+        with open(os.path.join(HERE, "kquant_kat.json"), "w") as f:
+            json.dump(make_kquant(), f, indent=1)
+        with open(os.path.join(HERE, "greedy_tokens.json"), "w") as f:
+            json.dump(make_greedy(), f, indent=1)
+    with open(os.path.join(HERE, "sampled_tokens.json"), "w") as f:
+        json.dump(make_sampled(), f, indent=1)
     print("wrote", os.listdir(HERE))

@@ -98,3 +98,29 @@ def test_pick_is_the_first_cumulative_probability_reaching_r():
     assert O.sample(x, o, [], r=p0 - 1e-3) == 3
     assert O.sample(x, o, [], r=p0 + 1e-3) == 7
     assert O.sample(x, o, [], r=1.0) == 7
+
+
+def test_sampled_generation_matches_golden():
+    """The oracle's Generate with Sampler.Sample against tests/golden/sampled_tokens.json (made by
+    tests/golden/make_golden.py): a regression pin for the restatement."""
+    import json
+    import os
+
+    from dotllm_b200 import synth
+    gold = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "sampled_tokens.json")))
+    so = gold["options"]
+    O.set_threads(max(1, O.max_threads()))
+    for name in ("micro", "micro-gemma", "tiny"):
+        g = gold[name]
+        cfg = synth.get(name)
+        m = O.Model(synth.build_model(cfg))
+        s = O.Session(m)
+        try:
+            prompt = synth.prompt_tokens(cfg)
+            seeded = s.generate_sampled(prompt, g["steps"], O.SamplingOptions(seed=g["seed"], **so))
+            drawn = s.generate_sampled(prompt, g["steps"], O.SamplingOptions(**so), np.asarray(g["draws"], np.float32))
+        finally:
+            s.close()
+            m.close()
+        assert list(seeded) == g["seeded_tokens"], name
+        assert list(drawn) == g["drawn_tokens"], name
