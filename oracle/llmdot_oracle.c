@@ -1417,7 +1417,10 @@ static void find_top_k(const float *x, int n, int k, int *idx, float *val)
 }
 
 /* FindNucleus :129-151: selection sort by probability, descending, then the prefix whose
- * running sum first reaches top_p */
+ * running sum first reaches top_p.  Sample (:48-50) passes its samplingBuf both as the
+ * probabilities and as `values`, so the caller passes val == p: each `val[i] = p[idx[i]]` may
+ * read a slot an earlier iteration already overwrote (when idx[i] < i), as the reference's
+ * aliased spans do.  No restrict: the aliasing is the behaviour being restated. */
 static int find_nucleus(const float *p, int n, float topP, int *idx, float *val)
 {
     for (int i = 0; i < n; i++) idx[i] = i;
@@ -1468,7 +1471,9 @@ EXPORT int orc_sample(const float *logits, int n, int topK, float topP, float te
         orc_softmax(x, n, 0, 0.0f);
         out = -1;
         if (topP < 1.0f) {
-            float *val = x + n;
+            /* values alias the softmax row (Sample :48-50); when the nucleus is the whole row the
+             * fall-through pick below reads the overwritten row and returns a position */
+            float *val = x;
             int ns = find_nucleus(x, n, topP, idx, val);
             if (ns < n) {
                 float sum = 0.0f;

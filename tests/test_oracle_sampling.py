@@ -124,3 +124,89 @@ def test_sampled_generation_matches_golden():
             m.close()
         assert list(seeded) == g["seeded_tokens"], name
         assert list(drawn) == g["drawn_tokens"], name
+
+
+def _nucleus_literal(p, top_p, r, aliased=True):
+    """Sample :46-58 with FindNucleus :129-151 and SampleFromProbabilities :153-165, restated
+    line by line in numpy float32.  With aliased=True `values` is the softmax row itself (the
+    reference passes samplingBuf for both); aliased=False is what a separate buffer would give."""
+    f32 = np.float32
+    buf = np.array(p, dtype=np.float32)
+    vals = buf if aliased else np.zeros_like(buf)
+    n = buf.size
+    idx = list(range(n))
+    for i in range(n - 1):
+        mx = i
+        for j in range(i + 1, n):
+            if buf[idx[j]] > buf[idx[mx]]:
+                mx = j
+        if mx != i:
+            idx[i], idx[mx] = idx[mx], idx[i]
+    cum, count = f32(0), 0
+    for i in range(n):
+        vals[i] = buf[idx[i]]
+        cum = f32(cum + vals[i])
+        count += 1
+        if cum >= f32(top_p):
+            break
+
+    def pick(q):
+        c = f32(0)
+        for i in range(q.size):
+            c = f32(c + q[i])
+            if f32(r) <= c:
+                return i
+        return q.size - 1
+
+    if count < n:
+        s = f32(0)
+        for i in range(count):
+            s = f32(s + vals[i])
+        inv = f32(1) / s
+        return idx[pick((vals[:count] * inv).astype(np.float32))]
+    return pick(buf)
+
+
+def test_top_p_only_reads_the_overwritten_row():
+    """TopK <= 0 (or >= the vocabulary) with TopP < 1: FindNucleus writes its values into the
+    softmax row it is still reading (Sample :48-50 passes samplingBuf as both), so a token whose
+    id is below its rank reads an already-overwritten slot.  Hand-worked on probabilities about
+    [0.3, 0.4, 0.2, 0.05, 0.05], TopP 0.85: the order is ids [1, 0, 2, 3, 4]; the aliased values
+    are [0.4, 0.4, 0.2] (id 0 reads slot 0, which already holds id 1's 0.4), a separate buffer
+    would give [0.4, 0.3, 0.2].  And on [0.1, 0.55, 0.35] with TopP 0.95 the nucleus is the
+    whole row, so the fall-through pick reads the overwritten row [0.55, 0.35, 0.55] and returns
+    a position."""
+    cases = [(np.log(np.array([0.3, 0.4, 0.2, 0.05, 0.05])), 0.85),
+             (np.log(np.array([0.1, 0.55, 0.35])), 0.95)]
+    for logits, top_p in cases:
+        logits = logits.astype(np.float32)
+        p = O.softmax(logits.copy())
+        differs = False
+        for top_k in (0, -3, logits.size):
+            o = opts(temperature=1, top_k=top_k, top_p=top_p, repeat_penalty=1, repeat_window=0)
+            for r in np.linspace(0.01, 0.99, 99):
+                want = _nucleus_literal(p, top_p, r)
+                assert O.sample(logits, o, [], r=float(r)) == want, (top_k, top_p, r)
+                differs |= want != _nucleus_literal(p, top_p, r, aliased=False)
+        assert differs, "the case does not separate the aliased reading from a separate buffer"
+
+
+def test_top_p_only_random_rows_with_ties():
+    """The same restatement on random rows whose logits are coarse (many exact ties, so the
+    selection sort's unstable tie order matters), with temperature and repeat penalty applied
+    first (Sample :33-34)."""
+    rng = np.random.default_rng(11)
+    for trial in range(60):
+        n = int(rng.integers(3, 40))
+        logits = (np.round(rng.standard_normal(n) * 4) / 2).astype(np.float32)
+        top_p = float(rng.uniform(0.2, 0.999))
+        temp = float(rng.uniform(0.5, 1.5))
+        recent = rng.integers(0, n, size=5).astype(np.int32)
+        o = opts(temperature=temp, top_k=0, top_p=top_p, repeat_penalty=1.3, repeat_window=4)
+        x = logits.copy()
+        for t in recent[-4:]:  # ApplyRepeatPenalty :64-81
+            x[t] = x[t] / np.float32(1.3) if x[t] > 0 else x[t] * np.float32(1.3)
+        x = (x * (np.float32(1) / np.float32(temp))).astype(np.float32)
+        p = O.softmax(x)
+        for r in rng.uniform(0, 1, size=8):
+            assert O.sample(logits, o, recent, r=float(r)) == _nucleus_literal(p, top_p, r), trial
