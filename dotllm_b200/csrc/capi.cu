@@ -740,7 +740,11 @@ extern "C" int llmdot_cuda_session_create(llmdot_model *m, int max_ctx, int kv_t
     }
     std::vector<int32_t> pt(s->n_pages);
     for (int i = 0; i < s->n_pages; i++) pt[i] = i;
-    LLMDOT_CUDA_TRY(cudaMemcpy(s->pages, pt.data(), sizeof(int32_t) * s->n_pages, cudaMemcpyHostToDevice));
+    if (cudaMemcpy(s->pages, pt.data(), sizeof(int32_t) * s->n_pages, cudaMemcpyHostToDevice) != cudaSuccess) {
+        const int rc = cuda_fail(cudaGetLastError(), "page table upload");
+        llmdot_cuda_session_free(s);
+        return rc;
+    }
     s->view = {s->k, s->v, s->pages, layer_stride};
     s->m = m;
     m->sessions.push_back(s);
@@ -1038,6 +1042,13 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
     cudaStream_t st = m->stream;
     cudaGraphExec_t g = nullptr;
     LLMDOT_TRY(step_graph(m, 1, s->kv_type, &g));
+    // the decode step's position and KV view, set before the history buffers exist so that an
+    // early return leaks nothing
+    ModelExtra &x = extra(m);
+    LLMDOT_TRY(ensure_pinned(m, 1));
+    x.h_pinned[x.cap] = s->pos;
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.views, &s->view, sizeof(KvView), cudaMemcpyHostToDevice, st));
     // history: the prompt, then every generated token, the last window + 1 kept (:100, :109-111)
     const int keep = a.window + 1;
     std::vector<int32_t> recent(prompt, prompt + n_prompt);
@@ -1062,11 +1073,6 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
     a.out = dbuf + keep + 1;
     a.r = (const float *)(dbuf + keep + 2);
     a.next = w.next;  // the next decode step's input token
-    ModelExtra &x = extra(m);
-    LLMDOT_TRY(ensure_pinned(m, 1));
-    x.h_pinned[x.cap] = s->pos;
-    LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t), cudaMemcpyHostToDevice, st));
-    LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.views, &s->view, sizeof(KvView), cudaMemcpyHostToDevice, st));
     int rc = LLMDOT_OK, produced = 0;
     for (int i = 0; i < max_tokens && rc == LLMDOT_OK; i++) {
         // the logits: the last prompt row after the prefill, row 0 after each decode step
@@ -1151,7 +1157,11 @@ extern "C" int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.views, x.h_views, sizeof(KvView) * batch, cudaMemcpyHostToDevice, st));
     cudaEvent_t e0, e1;
     LLMDOT_CUDA_TRY(cudaEventCreate(&e0));
-    LLMDOT_CUDA_TRY(cudaEventCreate(&e1));
+    if (cudaEventCreate(&e1) != cudaSuccess) {
+        const int erc = cuda_fail(cudaGetLastError(), "cudaEventCreate");
+        cudaEventDestroy(e0);
+        return erc;
+    }
     float total_ms = 0.0f;
     int rc = LLMDOT_OK;
     for (int done = 0; done < n_steps && rc == LLMDOT_OK;) {
