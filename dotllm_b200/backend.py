@@ -24,6 +24,18 @@ def _f32(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.float32)
 
 
+def _need(name: str, a: np.ndarray, n: int) -> None:
+    """The C entry points take one length for all their spans and read that many elements of
+    each; a shorter host array would be read past its end (the C# spans throw instead)."""
+    if a.size < n:
+        raise ValueError(f"{name}: {a.size} elements, {n} needed")
+
+
+def _inplace(name: str, a) -> None:
+    if not (isinstance(a, np.ndarray) and a.dtype == np.float32 and a.flags.c_contiguous and a.flags.writeable):
+        raise TypeError(f"{name}: needs a writeable C-contiguous float32 array")
+
+
 class CudaBackend:
     def __init__(self, device: int = 0):
         self._h = VP()
@@ -66,14 +78,18 @@ class CudaBackend:
 
     def rms_norm(self, x, w, eps: float) -> np.ndarray:
         x, w = _f32(x), _f32(w)
+        _need("rms_norm weight", w, x.size)
         out = np.empty_like(x)
         check(lib().llmdot_cuda_rmsnorm(self._h, _f(x), _f(w), _f(out), x.size, eps))
         return out
 
     def layer_norm(self, x, w, bias, eps: float) -> np.ndarray:
         x, w = _f32(x), _f32(w)
+        _need("layer_norm weight", w, x.size)
         out = np.empty_like(x)
         b = _f32(bias) if bias is not None and len(bias) else None
+        if b is not None:
+            _need("layer_norm bias", b, x.size)
         check(lib().llmdot_cuda_layernorm(self._h, _f(x), _f(w), _f(b) if b is not None else None, _f(out), x.size, eps))
         return out
 
@@ -103,7 +119,7 @@ class CudaBackend:
         return out
 
     def silu_in_place(self, x: np.ndarray) -> None:
-        assert x.dtype == np.float32 and x.flags.c_contiguous
+        _inplace("silu_in_place", x)
         check(lib().llmdot_cuda_silu_inplace(self._h, _f(x), x.size))
 
     def gelu(self, x) -> np.ndarray:
@@ -119,12 +135,15 @@ class CudaBackend:
 
     def add(self, a, b) -> np.ndarray:
         a, b = _f32(a), _f32(b)
+        _need("add b", b, a.size)
         out = np.empty_like(a)
         check(lib().llmdot_cuda_add(self._h, _f(a), _f(b), _f(out), a.size))
         return out
 
     def add_in_place(self, a: np.ndarray, b) -> None:
+        _inplace("add_in_place", a)
         b = _f32(b)
+        _need("add_in_place b", b, a.size)
         check(lib().llmdot_cuda_add_inplace(self._h, _f(a), _f(b), a.size))
 
     def scale(self, x, s: float) -> np.ndarray:
@@ -134,10 +153,12 @@ class CudaBackend:
         return out
 
     def scale_in_place(self, x: np.ndarray, s: float) -> None:
+        _inplace("scale_in_place", x)
         check(lib().llmdot_cuda_scale_inplace(self._h, _f(x), x.size, s))
 
     def mul(self, a, b) -> np.ndarray:
         a, b = _f32(a), _f32(b)
+        _need("mul b", b, a.size)
         out = np.empty_like(a)
         check(lib().llmdot_cuda_mul(self._h, _f(a), _f(b), _f(out), a.size))
         return out
@@ -149,6 +170,9 @@ class CudaBackend:
 
     def conv1d(self, x, w, kernel_size: int, input_dim: int) -> np.ndarray:
         x, w = _f32(x), _f32(w)
+        span = input_dim if kernel_size == 1 else kernel_size * input_dim
+        _need("conv1d input", x, span)
+        _need("conv1d weights", w, span)
         out = np.empty(input_dim, dtype=np.float32)
         check(lib().llmdot_cuda_conv1d(self._h, _f(x), _f(w), _f(out), kernel_size, input_dim))
         return out

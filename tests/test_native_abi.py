@@ -78,3 +78,30 @@ def test_sampling_defaults_are_the_references():
     o = native.LlmdotSampling()
     assert (o.top_k, o.repeat_window, o.seed) == (40, 64, -1)
     assert (o.top_p, o.temperature, o.repeat_penalty) == (pytest.approx(0.95), pytest.approx(0.8), pytest.approx(1.1))
+
+
+def test_backend_rejects_short_host_arrays_before_the_call():
+    """Entry points that take one length for several host spans would read a shorter array past
+    its end; the binding refuses it first (no device is needed to see that)."""
+    from dotllm_b200.backend import CudaBackend
+    b = CudaBackend.__new__(CudaBackend)  # no device handle: every case must fail before the call
+    b._h = None
+    x = np.ones(16, np.float32)
+    with pytest.raises(ValueError):
+        b.rms_norm(x, np.ones(8, np.float32), 1e-5)
+    with pytest.raises(ValueError):
+        b.layer_norm(x, np.ones(16, np.float32), np.ones(4, np.float32), 1e-5)
+    with pytest.raises(ValueError):
+        b.add(x, np.ones(15, np.float32))
+    with pytest.raises(ValueError):
+        b.mul(x, np.ones(3, np.float32))
+    with pytest.raises(ValueError):
+        b.add_in_place(x.copy(), np.ones(15, np.float32))
+    with pytest.raises(ValueError):
+        b.conv1d(np.ones(8, np.float32), np.ones(12, np.float32), 3, 4)
+    with pytest.raises(TypeError):
+        b.add_in_place(np.ones(16, np.float64), x)
+    with pytest.raises(TypeError):
+        b.scale_in_place(np.ones(16, np.float64), 2.0)
+    with pytest.raises(TypeError):
+        b.silu_in_place(x[::2])
