@@ -157,6 +157,8 @@ class CudaSession:
         o = LlmdotSampling(options.top_k, options.top_p, options.temperature, options.repeat_penalty,
                            options.repeat_window, options.seed)
         d = None if draws is None else np.ascontiguousarray(draws, dtype=np.float32)
+        if d is not None and d.size < max_tokens:  # the library reads one draw per token
+            raise ValueError(f"generate_sampled: {d.size} draws for {max_tokens} tokens")
         check(lib().llmdot_cuda_generate_sampled(self._h, p.ctypes.data_as(I32P), p.size, max_tokens, C.byref(o),
                                                  d.ctypes.data_as(F32P) if d is not None else None,
                                                  out.ctypes.data_as(I32P), C.byref(n)))
@@ -174,12 +176,20 @@ class CudaSession:
             pass
 
 
+def _batch_tokens(name: str, tokens, batch: int) -> np.ndarray:
+    """One input token per session: the library reads exactly `batch` of them."""
+    toks = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+    if toks.size != batch:
+        raise ValueError(f"{name}: {toks.size} tokens for {batch} sessions")
+    return toks
+
+
 def decode_steps(sessions: List[CudaSession], tokens, n_steps: int):
     """Device-resident greedy decode of n_steps tokens for sessions in lockstep.
     Returns (ids [n_steps, batch], device ms, kernel launches per step)."""
     B = len(sessions)
     arr = (VP * B)(*[s._h for s in sessions])
-    toks = np.ascontiguousarray(tokens, dtype=np.int32)
+    toks = _batch_tokens("decode_steps", tokens, B)
     out = np.zeros((max(n_steps, 1), B), dtype=np.int32)
     ms = C.c_float()
     kps = C.c_int()
@@ -193,7 +203,7 @@ def trace_step(sessions: List[CudaSession], tokens):
     Returns (events [phases, ctas, 16], kinds [phases]); see llmdot_cuda_trace_step."""
     B = len(sessions)
     arr = (VP * B)(*[s._h for s in sessions])
-    toks = np.ascontiguousarray(tokens, dtype=np.int32)
+    toks = _batch_tokens("trace_step", tokens, B)
     nph, ncta = C.c_int(), C.c_int()
     check(lib().llmdot_cuda_trace_step(arr, B, toks.ctypes.data_as(I32P), None, None, C.byref(nph), C.byref(ncta)))
     ev = np.zeros((nph.value, ncta.value, 16), dtype=np.uint64)
@@ -207,7 +217,7 @@ def decode_batch(sessions: List[CudaSession], tokens, want_logits: bool = False)
     """One greedy step for several sessions of one model (batched decode)."""
     B = len(sessions)
     arr = (VP * B)(*[s._h for s in sessions])
-    toks = np.ascontiguousarray(tokens, dtype=np.int32)
+    toks = _batch_tokens("decode", tokens, B)
     nxt = np.zeros(B, dtype=np.int32)
     V = sessions[0].model.config["vocab"]
     logits = np.empty((B, V), dtype=np.float32) if want_logits else None

@@ -105,3 +105,21 @@ def test_backend_rejects_short_host_arrays_before_the_call():
         b.scale_in_place(np.ones(16, np.float64), 2.0)
     with pytest.raises(TypeError):
         b.silu_in_place(x[::2])
+
+
+def test_engine_rejects_token_and_draw_counts_the_library_would_overrun():
+    """decode / decode_steps / trace_step read one token per session and generate_sampled one
+    draw per token: other counts are refused before the call (no device needed)."""
+    from types import SimpleNamespace
+
+    from dotllm_b200 import engine
+    fake = [SimpleNamespace(_h=None), SimpleNamespace(_h=None)]
+    for call in (lambda: engine.decode_batch(fake, [1]),
+                 lambda: engine.decode_steps(fake, [1, 2, 3], 4),
+                 lambda: engine.trace_step(fake, [])):
+        with pytest.raises(ValueError):
+            call()
+    s = engine.CudaSession.__new__(engine.CudaSession)
+    s._h = None
+    with pytest.raises(ValueError):
+        s.generate_sampled([1, 2], 8, native.LlmdotSampling(), draws=np.full(7, 0.5, np.float32))
