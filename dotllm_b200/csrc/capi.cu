@@ -646,6 +646,16 @@ extern "C" int llmdot_cuda_model_load_gguf(int device, const char *path, llmdot_
     return rc;
 }
 
+extern "C" int llmdot_cuda_gguf_config(const char *path, llmdot_config *out)
+{
+    if (!out || !path) return fail(LLMDOT_E_INVALID, "null argument");
+    GgufModelFile f;
+    LLMDOT_TRY(gguf_open(path, &f));  // host only: parse and resolve, no device touched
+    *out = f.cfg;
+    gguf_close(&f);
+    return LLMDOT_OK;
+}
+
 extern "C" int llmdot_cuda_model_load_gguf_tp(int device, const char *path, int tp_size, int tp_rank,
                                               llmdot_model **out)
 {

@@ -226,6 +226,14 @@ def decode_batch(sessions: List[CudaSession], tokens, want_logits: bool = False)
     return nxt, logits
 
 
+def gguf_config(path: str) -> dict:
+    """GgufReader.Read + ArchitectureResolver.Resolve of a GGUF file, natively and without a
+    device (llmdot_cuda_gguf_config)."""
+    c = LlmdotConfig()
+    check(lib().llmdot_cuda_gguf_config(path.encode(), C.byref(c)))
+    return c.as_dict()
+
+
 def tp_unique_id() -> bytes:
     """An NCCL unique id (128 bytes) for llmdot_cuda_tp_init."""
     buf = (C.c_uint8 * 128)()

@@ -92,6 +92,7 @@ _SIGS = {
     "llmdot_cuda_model_load": (C.c_int, [C.c_int, C.POINTER(LlmdotConfig), C.POINTER(TensorDesc), C.c_int, C.POINTER(VP)]),
     "llmdot_cuda_model_load_gguf": (C.c_int, [C.c_int, C.c_char_p, C.POINTER(VP)]),
     "llmdot_cuda_model_config": (C.c_int, [VP, C.POINTER(LlmdotConfig)]),
+    "llmdot_cuda_gguf_config": (C.c_int, [C.c_char_p, C.POINTER(LlmdotConfig)]),
     "llmdot_cuda_model_weight_bytes": (C.c_int, [VP, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "llmdot_cuda_model_free": (C.c_int, [VP]),
     "llmdot_cuda_session_create": (C.c_int, [VP, C.c_int, C.c_int, C.POINTER(VP)]),

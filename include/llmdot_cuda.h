@@ -201,6 +201,11 @@ LLMDOT_API int llmdot_cuda_model_load(int device, const llmdot_config *cfg,
 /* Parse a GGUF file natively (GgufReader + ArchitectureResolver restated in C++),
  * stream its tensors to the device and upload the model. */
 LLMDOT_API int llmdot_cuda_model_load_gguf(int device, const char *path, llmdot_model **out);
+/* The same parse and ArchitectureResolver.Resolve (ArchitectureResolver.cs:14-112) without
+ * loading anything: host only, no device needed.  Fails with LLMDOT_E_FORMAT and the
+ * reference's message for a missing or unsupported general.architecture or a missing norm
+ * epsilon. */
+LLMDOT_API int llmdot_cuda_gguf_config(const char *path, llmdot_config *out);
 LLMDOT_API int llmdot_cuda_model_config(const llmdot_model *m, llmdot_config *out);
 /* Quantised weight bytes the decode step streams per token (layers + logits head). */
 LLMDOT_API int llmdot_cuda_model_weight_bytes(const llmdot_model *m, uint64_t *layer_bytes,

@@ -1,0 +1,154 @@
+"""ArchitectureResolver.Resolve (src/Llmdot.Core/Loading/ArchitectureResolver.cs:14-112) in the
+library's native GGUF parser (llmdot_cuda_gguf_config, host only) and in the oracle, on the
+metadata-only files of the reference's tests/Llmdot.Core.Tests/Loading/ArchitectureResolverTests.cs
+(line of each test cited) and against each other.  CPU only.
+
+The files are written byte for byte as that test's WriteGguf helper (:179-245) writes them:
+GGUF v3, no tensors, UInt32 / Float32 / String values, and Bool written as a 4-byte UInt32
+(the reader takes its first byte; the other three fall into the empty data section).
+"""
+import struct
+
+import numpy as np
+import pytest
+
+from dotllm_b200.engine import gguf_config
+from dotllm_b200.native import CudaBackendError
+from oracle import oracle as O
+
+U32, F32, BOOL, STR = 4, 6, 7, 8  # GgufValueType
+
+
+def _s(v: str) -> bytes:
+    b = v.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def write_meta_gguf(path, entries):
+    out = b"GGUF" + struct.pack("<IQQ", 3, 0, len(entries))
+    for key, t, v in entries:
+        out += _s(key) + struct.pack("<I", t)
+        if t == U32:
+            out += struct.pack("<I", v)
+        elif t == F32:
+            out += struct.pack("<f", v)
+        elif t == STR:
+            out += _s(v)
+        elif t == BOOL:
+            out += struct.pack("<I", 1 if v else 0)
+    with open(path, "wb") as f:
+        f.write(out)
+    return str(path)
+
+
+def _arch(name, hidden, layers, ctx, ffn, heads, heads_kv, eps):
+    return [("general.architecture", STR, name), (f"{name}.embedding_length", U32, hidden),
+            (f"{name}.block_count", U32, layers), (f"{name}.context_length", U32, ctx),
+            (f"{name}.feed_forward_length", U32, ffn), (f"{name}.attention.head_count", U32, heads),
+            (f"{name}.attention.head_count_kv", U32, heads_kv),
+            (f"{name}.attention.layer_norm_rms_epsilon", F32, eps)]
+
+
+LLAMA = _arch("llama", 4096, 32, 4096, 11008, 32, 32, 1e-5)                             # :34-58
+PHI2 = _arch("phi2", 2560, 32, 2048, 10240, 32, 32, 1e-5) + [("phi2.use_parallel_residual", BOOL, True)]  # :61-82
+GEMMA = _arch("gemma", 2048, 18, 8192, 16384, 8, 1, 1e-6)                               # :85-106
+GQA = _arch("llama", 4096, 32, 8192, 14336, 32, 8, 1e-5)                                # :109-128
+LFM2 = _arch("lfm2", 2048, 16, 32768, 6656, 16, 8, 1e-5) + [("lfm2.conv_L_cache", U32, 3)]  # :131-155
+
+
+def attention_type(c):  # DetermineAttentionType :123-128
+    return "MHA" if c["heads"] == c["heads_kv"] else ("MQA" if c["heads_kv"] == 1 else "GQA")
+
+
+def both(path):
+    """The library's resolution, and the oracle's (which must agree field for field)."""
+    c = gguf_config(path)
+    m = O.Model(path)
+    try:
+        o = m.config
+    finally:
+        m.close()
+    for k, v in o.items():
+        assert c[k] == pytest.approx(v, rel=0, abs=0), k
+    return c
+
+
+def test_missing_architecture(tmp_path):  # :11-19
+    p = write_meta_gguf(tmp_path / "a.gguf", [])
+    with pytest.raises(CudaBackendError, match="missing 'general.architecture'"):
+        gguf_config(p)
+    with pytest.raises(ValueError, match="missing 'general.architecture'"):
+        O.Model(p)
+
+
+def test_unsupported_architecture(tmp_path):  # :21-31
+    p = write_meta_gguf(tmp_path / "a.gguf", [("general.architecture", STR, "fancy_new_model")])
+    with pytest.raises(CudaBackendError, match="Unsupported GGUF architecture"):
+        gguf_config(p)
+    with pytest.raises(ValueError, match="Unsupported GGUF architecture"):
+        O.Model(p)
+
+
+def test_llama_is_llama_like(tmp_path):  # :34-58
+    c = both(write_meta_gguf(tmp_path / "a.gguf", LLAMA))
+    assert c["template_id"] == 0 and c["hidden"] == 4096 and c["layers"] == 32
+    assert attention_type(c) == "MHA"
+    assert c["norm_is_rms"] == 1 and c["eps"] == np.float32(1e-5)
+    # the defaults the test file leaves to the resolver
+    assert (c["vocab"], c["bos"], c["eos"], c["head_dim"], c["rope_dim"]) == (0, 1, 2, 128, 128)
+    assert c["rope_base"] == 10000.0 and c["emb_scale"] == 1.0 and c["tied"] == 1
+    assert c["parallel_residual"] == 0 and c["ffn_type"] == 0 and c["qkv_fused"] == 0
+
+
+def test_phi2_is_neox_like_with_parallel_residual(tmp_path):  # :61-82
+    c = both(write_meta_gguf(tmp_path / "a.gguf", PHI2))
+    assert c["template_id"] == 1 and c["parallel_residual"] == 1
+
+
+def test_gemma_is_gemma_like_mqa_with_embedding_scale(tmp_path):  # :85-106
+    c = both(write_meta_gguf(tmp_path / "a.gguf", GEMMA))
+    assert c["template_id"] == 2 and attention_type(c) == "MQA"
+    assert c["emb_scale"] == np.sqrt(np.float32(2048), dtype=np.float32)
+
+
+def test_gqa_detected(tmp_path):  # :109-128
+    c = both(write_meta_gguf(tmp_path / "a.gguf", GQA))
+    assert attention_type(c) == "GQA" and c["heads_kv"] == 8
+
+
+def test_lfm2_is_lfm2_like(tmp_path):  # :131-155 (the oracle stops at LFM2: outside its path)
+    c = gguf_config(write_meta_gguf(tmp_path / "a.gguf", LFM2))
+    assert c["template_id"] == 3 and c["layers"] == 16 and attention_type(c) == "GQA"
+
+
+def test_non_lfm2_has_no_conv_template(tmp_path):  # :158-178
+    c = both(write_meta_gguf(tmp_path / "a.gguf", LLAMA))
+    assert c["template_id"] != 3
+
+
+def test_no_norm_epsilon_is_refused(tmp_path):  # ResolveNormType :131-141
+    p = write_meta_gguf(tmp_path / "a.gguf", LLAMA[:-1])
+    with pytest.raises(CudaBackendError, match="No norm epsilon"):
+        gguf_config(p)
+    with pytest.raises(ValueError, match="No norm epsilon"):
+        O.Model(p)
+
+
+def test_layer_norm_epsilon_and_rope_scaling(tmp_path):
+    """ResolveNormType's LayerNorm branch and ResolveRopeScaling (:169-183), case-insensitive."""
+    e = LLAMA[:-1] + [("llama.attention.layer_norm_epsilon", F32, 1e-6),
+                      ("llama.rope.scaling.type", STR, "Linear"), ("llama.rope.scaling.factor", F32, 4.0),
+                      ("llama.rope.freq_base", F32, 500000.0), ("llama.attention.sliding_window", U32, 4096),
+                      ("llama.final_logit_softcapping", F32, 30.0), ("tokenizer.ggml.eos_token_id", U32, 7)]
+    c = both(write_meta_gguf(tmp_path / "a.gguf", e))
+    assert c["norm_is_rms"] == 0 and c["eps"] == np.float32(1e-6)
+    assert c["rope_scaling"] == 1 and c["rope_factor"] == 4.0 and c["rope_base"] == 500000.0
+    assert c["sliding_window"] == 4096 and c["has_final_cap"] == 1 and c["final_cap"] == 30.0
+    assert c["has_attn_cap"] == 0 and c["eos"] == 7
+
+
+def test_synthetic_models_resolve_alike(tmp_path):
+    """Full generated models (tensors included: fused QKV, gate, post-norms, tied heads)."""
+    from dotllm_b200 import synth
+    for name in ("micro", "micro-gemma", "micro-phi3", "micro-q5q8"):
+        both(synth.build_model(synth.get(name)))
