@@ -152,3 +152,28 @@ def test_synthetic_models_resolve_alike(tmp_path):
     from dotllm_b200 import synth
     for name in ("micro", "micro-gemma", "micro-phi3", "micro-q5q8"):
         both(synth.build_model(synth.get(name)))
+
+
+def test_gguf_reader_cases(tmp_path):
+    """tests/Llmdot.Core.Tests/Loading/GgufReaderTests.cs through the resolving entry points:
+    bad magic is refused by the reader (:8-18); the minimal v3 header (:20-31) parses and then
+    stops at the resolver's missing-architecture check; the one-string metadata file (:33-55)
+    parses its value, which the resolver names in its missing-epsilon message."""
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"\0\0\0\0")
+    with pytest.raises(CudaBackendError, match="Invalid GGUF magic"):
+        gguf_config(str(bad))
+    with pytest.raises(ValueError, match="Invalid GGUF magic"):
+        O.Model(str(bad))
+    p = write_meta_gguf(tmp_path / "min.gguf", [])
+    with pytest.raises(CudaBackendError, match="missing 'general.architecture'"):
+        gguf_config(p)
+    p = write_meta_gguf(tmp_path / "phi2.gguf", [("general.architecture", STR, "phi2")])
+    with pytest.raises(CudaBackendError, match="architecture 'phi2'"):
+        gguf_config(p)
+    with pytest.raises(ValueError, match="architecture 'phi2'"):
+        O.Model(p)
+    old = tmp_path / "v1.gguf"  # GgufReader.cs: versions below 2 are refused
+    old.write_bytes(b"GGUF" + struct.pack("<IQQ", 1, 0, 0))
+    with pytest.raises(CudaBackendError, match="Unsupported GGUF version"):
+        gguf_config(str(old))
