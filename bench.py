@@ -21,6 +21,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 
 import numpy as np
@@ -50,15 +51,56 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """Clock / throttle sampling during the timed region: an NVML polling thread (read-only
+    queries every 10 ms) and, as a fallback, `nvidia-smi -lms 200`.  The summary uses the NVML
+    samples when there are any."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    PERIOD_S = 0.01
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.samples = []  # (sm_mhz, sm_max_mhz, [reason names]) from NVML
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _nvml_loop(self, nv):
+        try:
+            nv.nvmlInit()
+        except Exception:
+            return
+        try:
+            h = nv.nvmlDeviceGetHandleByIndex(self.idx)
+            mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            bits = {name: getattr(nv, "nvmlClocksEventReason" + tag, None) or getattr(nv, "nvmlClocksThrottleReason" + tag)
+                    for name, tag in zip(self.REASONS, ("HwSlowdown", "HwThermalSlowdown", "SwThermalSlowdown",
+                                                        "SwPowerCap"))}
+            while not self._stop.is_set():
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                r = int(get_reasons(h))
+                self.samples.append((sm, mx, [n for n, b in bits.items() if r & int(b)]))
+                self._stop.wait(self.PERIOD_S)
+        except Exception:
+            pass
+        finally:
+            try:
+                nv.nvmlShutdown()
+            except Exception:
+                pass
 
     def __enter__(self):
+        if self.idx < 0:
+            return self
+        try:
+            import pynvml
+            self._thread = threading.Thread(target=self._nvml_loop, args=(pynvml,), daemon=True)
+            self._thread.start()
+        except Exception:
+            self._thread = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
@@ -69,6 +111,9 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         self.out = ""
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=5)
         if self.proc:
             self.proc.terminate()
             try:
@@ -77,16 +122,20 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if self.samples:
+            sm = [s[0] for s in self.samples]
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(s[1] for s in self.samples),
+                    "reasons": sorted({n for s in self.samples for n in s[2]}), "samples": len(self.samples),
+                    "source": "nvml"}
         rows = [r.split(",") for r in (getattr(self, "out", "") or "").strip().splitlines()]
         rows = [[c.strip() for c in r] for r in rows if len(r) >= 9]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        reasons = sorted({self.REASONS[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi"}
 
 
 def cpu_baseline_sample(path: str, cfg, threads: int, n_prompt: int, n_decode: int):
