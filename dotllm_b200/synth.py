@@ -53,6 +53,14 @@ class SynthConfig:
     attn_softcap: Optional[float] = None
     final_softcap: Optional[float] = None
     sliding_window: int = 0
+    # Lfm2Like: layers whose operator is the short conv (the others are attention), its kernel
+    conv_layers: Tuple[int, ...] = ()
+    conv_kernel: int = 3
+    qk_norm: bool = False
+    # MoE FFN: expert count, experts used per token, each expert's FFN width
+    experts: int = 0
+    experts_used: int = 0
+    expert_ffn: int = 0
     seed: int = 1
     # workload
     prompt_len: int = 64
@@ -72,6 +80,8 @@ class SynthConfig:
 
 
 Q6 = GGML_Q6_K
+# F32 tensors and the std of their random values (norm vectors are 1 + N(0, 0.01))
+F32_ROLES = {"norm": None, "conv": 0.5, "router": 0.1}
 
 # BASELINE.json configs[0..4]
 CONFIGS: Dict[str, SynthConfig] = {
@@ -120,6 +130,19 @@ TEST_CONFIGS: Dict[str, SynthConfig] = {
         vocab=1000, context=256, default_type=GGML_Q5_K,
         overrides=(("attn_v", GGML_Q8_0), ("ffn_down", GGML_Q8_0), ("output", Q6)), seed=14,
         prompt_len=8, decode_len=16),
+    # the templates the device does not run yet (checked by the oracle only): LFM2's short-conv
+    # layers with QK-normed attention layers, a Llama-like MoE, and LFM2 with MoE
+    "micro-lfm2": SynthConfig(
+        name="micro-lfm2", arch="lfm2", layers=4, hidden=256, heads=4, heads_kv=2, head_dim=64, ffn=512,
+        vocab=1000, context=256, tied=True, conv_layers=(0, 2), qk_norm=True, seed=15,
+        prompt_len=8, decode_len=16),
+    "micro-moe": SynthConfig(
+        name="micro-moe", arch="llama", layers=2, hidden=256, heads=4, heads_kv=2, head_dim=64, ffn=512,
+        vocab=1000, context=256, experts=4, experts_used=2, expert_ffn=256, seed=16, prompt_len=8, decode_len=16),
+    "micro-lfm2moe": SynthConfig(
+        name="micro-lfm2moe", arch="lfm2_moe", layers=3, hidden=256, heads=4, heads_kv=2, head_dim=64, ffn=512,
+        vocab=1000, context=256, tied=True, conv_layers=(0,), qk_norm=True, experts=4, experts_used=2,
+        expert_ffn=256, seed=17, prompt_len=8, decode_len=16),
 }
 
 # Full-width, few-layer copies of the BASELINE models: every matrix, head and vocabulary shape
@@ -140,26 +163,46 @@ def tensor_plan(cfg: SynthConfig) -> List[Tuple[TensorInfo, str]]:
     out: List[Tuple[TensorInfo, str]] = []
 
     def add(name: str, dims: List[int], role: str):
-        t = GGML_F32 if role == "norm" else cfg.type_of(role)
+        t = GGML_F32 if role in F32_ROLES else cfg.type_of(role)
         out.append((TensorInfo(name, dims, t), role))
 
     add("token_embd.weight", [d, V], "token_embd")
     for l in range(cfg.layers):
         p = f"blk.{l}."
         add(p + "attn_norm.weight", [d], "norm")
-        if cfg.qkv_fused:
-            add(p + "attn_qkv.weight", [d, q + 2 * kv], "attn_qkv")
+        if l in cfg.conv_layers:
+            # TensorNameResolver.cs:79-89: in_proj -> (B, C, x), the depthwise kernel [K][d], out_proj
+            add(p + "shortconv.in_proj.weight", [d, 3 * d], "conv_in")
+            add(p + "shortconv.conv.weight", [cfg.conv_kernel, d], "conv")
+            add(p + "shortconv.out_proj.weight", [d, d], "conv_out")
         else:
-            add(p + "attn_q.weight", [d, q], "attn_q")
-            add(p + "attn_k.weight", [d, kv], "attn_k")
-            add(p + "attn_v.weight", [d, kv], "attn_v")
-        add(p + "attn_output.weight", [q, d], "attn_output")
+            if cfg.qkv_fused:
+                add(p + "attn_qkv.weight", [d, q + 2 * kv], "attn_qkv")
+            else:
+                add(p + "attn_q.weight", [d, q], "attn_q")
+                add(p + "attn_k.weight", [d, kv], "attn_k")
+                add(p + "attn_v.weight", [d, kv], "attn_v")
+            if cfg.qk_norm:
+                add(p + "attn_q_norm.weight", [cfg.head_dim], "norm")
+                add(p + "attn_k_norm.weight", [cfg.head_dim], "norm")
+            add(p + "attn_output.weight", [q, d], "attn_output")
         if cfg.post_norm:
             add(p + "post_attention_norm.weight", [d], "norm")
         add(p + "ffn_norm.weight", [d], "norm")
-        add(p + "ffn_gate.weight", [d, f], "ffn_gate")
-        add(p + "ffn_up.weight", [d, f], "ffn_up")
-        add(p + "ffn_down.weight", [f, d], "ffn_down")
+        if cfg.experts:
+            # MoeFfnForward (InferenceEngine.cs:489-542): the router and per-expert SwiGLU
+            # tensors; the dense ffn_up / ffn_down exist only because ResolveLayer requires them
+            add(p + "ffn_gate_inp.weight", [d, cfg.experts], "router")
+            for e in range(cfg.experts):
+                add(p + f"ffn_gate.{e}.weight", [d, cfg.expert_ffn], "ffn_gate")
+                add(p + f"ffn_up.{e}.weight", [d, cfg.expert_ffn], "ffn_up")
+                add(p + f"ffn_down.{e}.weight", [cfg.expert_ffn, d], "ffn_down")
+            add(p + "ffn_up.weight", [d, f], "ffn_up")
+            add(p + "ffn_down.weight", [f, d], "ffn_down")
+        else:
+            add(p + "ffn_gate.weight", [d, f], "ffn_gate")
+            add(p + "ffn_up.weight", [d, f], "ffn_up")
+            add(p + "ffn_down.weight", [f, d], "ffn_down")
         if cfg.post_norm:
             add(p + "post_ffw_norm.weight", [d], "norm")
     add("output_norm.weight", [d], "norm")
@@ -178,7 +221,15 @@ def metadata_for(cfg: SynthConfig) -> Metadata:
     md.add(f"{a}.context_length", U32, cfg.context)
     md.add(f"{a}.feed_forward_length", U32, cfg.ffn)
     md.add(f"{a}.attention.head_count", U32, cfg.heads)
-    md.add(f"{a}.attention.head_count_kv", U32, cfg.heads_kv)
+    if cfg.conv_layers:  # per-layer kv heads, 0 for the conv layers (HeadCountKvPerLayer)
+        md.add(f"{a}.attention.head_count_kv", ARR,
+               [0 if l in cfg.conv_layers else cfg.heads_kv for l in range(cfg.layers)], U32)
+        md.add(f"{a}.shortconv.l_cache", U32, cfg.conv_kernel)
+    else:
+        md.add(f"{a}.attention.head_count_kv", U32, cfg.heads_kv)
+    if cfg.experts:
+        md.add(f"{a}.expert_count", U32, cfg.experts)
+        md.add(f"{a}.expert_used_count", U32, cfg.experts_used)
     md.add(f"{a}.attention.key_length", U32, cfg.head_dim)
     md.add(f"{a}.attention.value_length", U32, cfg.head_dim)
     md.add(f"{a}.attention.layer_norm_rms_epsilon", F32, cfg.eps)
@@ -206,6 +257,9 @@ def tensor_bytes(cfg: SynthConfig, info: TensorInfo, role: str, idx: int) -> byt
     if role == "norm":
         w = 1.0 + 0.01 * rng.standard_normal(info.dims[0], dtype=np.float32)
         return w.astype("<f4").tobytes()
+    if role in F32_ROLES:  # the conv kernel and the MoE router stay F32, as in released GGUFs
+        n = int(np.prod(info.dims))
+        return (rng.standard_normal(n, dtype=np.float32) * np.float32(F32_ROLES[role])).astype("<f4").tobytes()
     cols, rows = info.dims[0], info.dims[1]
     chunk = max(1, (1 << 24) // cols)
     starts = range(0, rows, chunk)

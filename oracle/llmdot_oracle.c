@@ -29,6 +29,7 @@
  * accumulation order never changes, so results are identical for any thread
  * count.
  */
+#include <float.h>
 #include <math.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -868,6 +869,9 @@ typedef struct {
     float *rope_freq;
     int rope_half;
     char arch[64];
+    int conv_kernel;      /* ConvKernelSize (0 unless HasConvLayers) */
+    int expert_used;      /* ExpertUsedCount */
+    uint8_t *layer_attn;  /* LayerTypes: 1 Attention, 0 Conv */
 } omodel;
 
 static okv *find_kv(omodel *m, const char *key)
@@ -908,6 +912,14 @@ static otensor *find_tf(omodel *m, const char *fmt, int layer)
     snprintf(buf, sizeof buf, fmt, layer);
     return find_t(m, buf);
 }
+/* a tensor of that name exists in TensorInfos, data or not (case-insensitive) */
+static int has_name(omodel *m, const char *fmt, int layer)
+{
+    char buf[128];
+    snprintf(buf, sizeof buf, fmt, layer);
+    for (int i = 0; i < m->nt; i++) if (strcasecmp(m->t[i].name, buf) == 0) return 1;
+    return 0;
+}
 static int any_name_contains(omodel *m, const char *sub)
 {
     for (int i = 0; i < m->nt; i++) if (strstr(m->t[i].name, sub)) return 1;
@@ -922,7 +934,7 @@ EXPORT void orc_model_free(omodel *m)
     if (!m) return;
     for (int i = 0; i < m->nkv; i++) { free(m->kv[i].key); free(m->kv[i].str); free(m->kv[i].arr_num); }
     for (int i = 0; i < m->nt; i++) free(m->t[i].name);
-    free(m->kv); free(m->t); free(m->file); free(m->hkv_per_layer); free(m->rope_freq);
+    free(m->kv); free(m->t); free(m->file); free(m->hkv_per_layer); free(m->rope_freq); free(m->layer_attn);
     free(m);
 }
 
@@ -1055,6 +1067,18 @@ EXPORT omodel *orc_model_load(const char *path)
     c->final_cap = get_float(m, "final_logit_softcapping", 0, &present);
     c->has_final_cap = present;
     c->expert_count = get_int(m, "expert_count", 0);
+    m->expert_used = get_int(m, "expert_used_count", 0);
+    /* HasConvLayers / ConvKernelSize / LayerTypes (:66-70); ResolveLayerTypes :226-238: a layer
+     * is Attention when blk.N.attn_q, attn_k or attn_qkv is among the tensor infos */
+    m->layer_attn = (uint8_t *)malloc(c->layers > 0 ? (size_t)c->layers : 1);
+    m->conv_kernel = 0;
+    for (int l = 0; l < c->layers; l++) m->layer_attn[l] = 1;
+    if (c->template_id == TPL_LFM2) {
+        m->conv_kernel = get_int(m, "shortconv.l_cache", 3);
+        for (int l = 0; l < c->layers; l++)
+            m->layer_attn[l] = (uint8_t)(has_name(m, "blk.%d.attn_q.weight", l) || has_name(m, "blk.%d.attn_k.weight", l) ||
+                                         has_name(m, "blk.%d.attn_qkv.weight", l));
+    }
     {
         okv *b = find_kv(m, "tokenizer.ggml.bos_token_id");
         okv *e = find_kv(m, "tokenizer.ggml.eos_token_id");
@@ -1070,8 +1094,8 @@ EXPORT omodel *orc_model_load(const char *path)
         if (c->rope_scaling == ROPE_LINEAR && c->rope_factor > 1.0f) freq /= c->rope_factor;
         m->rope_freq[i] = freq;
     }
-    if (c->template_id == TPL_LFM2 || c->expert_count > 0) {
-        snprintf(g_err, sizeof g_err, "LFM2 / MoE templates are outside the restated path");
+    if (c->template_id == TPL_LFM2 && m->conv_kernel < 1) {
+        snprintf(g_err, sizeof g_err, "conv kernel size %d", m->conv_kernel);
         orc_model_free(m);
         return NULL;
     }
@@ -1080,6 +1104,116 @@ EXPORT omodel *orc_model_load(const char *path)
 
 EXPORT void orc_model_config(omodel *m, orc_config *out) { *out = m->cfg; }
 EXPORT const float *orc_model_rope_freq(omodel *m, int *half) { *half = m->rope_half; return m->rope_freq; }
+
+/* ------------------------------------------------------------------------ */
+/* ConvStateCache (src/Llmdot.Core/Inference/ConvStateCache.cs:3-65): per layer a ring of the
+ * last kernel-1 conv inputs; BuildInput lays the window out channel-major, [c * K + k], zeros
+ * before position 0; Store writes at the layer's head, which counts stores, not positions. */
+typedef struct {
+    int layers, hidden, hist, k;
+    float *buf;      /* [layers][hist][hidden] */
+    float *scratch;  /* [k * hidden] */
+    int *head;       /* [layers] */
+} oconv;
+
+EXPORT void orc_conv_state_free(oconv *cs)
+{
+    if (!cs) return;
+    free(cs->buf); free(cs->scratch); free(cs->head);
+    free(cs);
+}
+
+EXPORT oconv *orc_conv_state_new(int layers, int hidden, int kernel)
+{
+    if (layers < 0 || hidden <= 0 || kernel < 1) return NULL;
+    oconv *cs = (oconv *)calloc(1, sizeof(oconv));
+    cs->layers = layers; cs->hidden = hidden; cs->hist = kernel - 1; cs->k = kernel;
+    size_t nb = (size_t)layers * cs->hist * hidden;
+    cs->buf = (float *)calloc(nb ? nb : 1, sizeof(float));
+    cs->scratch = (float *)calloc((size_t)kernel * hidden, sizeof(float));
+    cs->head = (int *)calloc(layers ? (size_t)layers : 1, sizeof(int));
+    return cs;
+}
+
+EXPORT void orc_conv_state_store(oconv *cs, int layer, const float *x)   /* Store :24-31 */
+{
+    if (cs->hist == 0) return;
+    int pos = cs->head[layer];
+    memcpy(cs->buf + ((size_t)layer * cs->hist + pos) * cs->hidden, x, sizeof(float) * cs->hidden);
+    cs->head[layer] = (pos + 1) % cs->hist;
+}
+
+EXPORT const float *orc_conv_state_build(oconv *cs, int layer, const float *cur, int position)  /* BuildInput :33-56 */
+{
+    const int K = cs->k, H = cs->hist;
+    float *r = cs->scratch;
+    for (int c = 0; c < cs->hidden; c++) {
+        for (int k = 0; k < H; k++) {
+            int req = position - H + k;
+            r[(size_t)c * K + k] = req < 0 ? 0.0f : cs->buf[((size_t)layer * H + req % H) * cs->hidden + c];
+        }
+        r[(size_t)c * K + H] = cur[c];
+    }
+    return r;
+}
+
+EXPORT void orc_conv_state_reset(oconv *cs)   /* Reset :58-62 */
+{
+    memset(cs->buf, 0, sizeof(float) * (size_t)cs->layers * cs->hist * cs->hidden);
+    memset(cs->head, 0, sizeof(int) * (size_t)(cs->layers ? cs->layers : 1));
+}
+
+/* TensorOps.Conv1D (TensorOps.cs:745-778): kernel 1 is an elementwise product; otherwise per
+ * channel 8-lane products summed in lanes, the lanes added (Vector.Dot with One), then the tail
+ * k's added in order -- for kernels below 8 only the tail runs, after a +0 from the empty lanes */
+EXPORT void orc_conv1d(const float *in, const float *w, float *out, int K, int dim)
+{
+    if (K == 1) {
+        for (int i = 0; i < dim; i++) out[i] = in[i] * w[i];
+        return;
+    }
+    for (int c = 0; c < dim; c++) {
+        const float *x = in + (size_t)c * K, *wk = w + (size_t)c * K;
+        float acc[VEC] = {0};
+        int k = 0;
+        for (; k <= K - VEC; k += VEC)
+            for (int l = 0; l < VEC; l++) acc[l] = acc[l] + x[k + l] * wk[k + l];
+        float sum = hsum8(acc);
+        for (; k < K; k++) sum += x[k] * wk[k];
+        out[c] = sum;
+    }
+}
+
+/* MoeRouter.Route (src/Llmdot.Core/Inference/MoeRouter.cs:12-59): gate logits by the backend's
+ * MatMul (the generic dequantise-and-dot path for F32 gates), top-k by repeated first-maximum
+ * scans over the experts not yet taken (strict >, starting from float.MinValue, so an
+ * exhausted scan leaves index -1), then MathF.Exp softmax over the k selected values. */
+EXPORT int orc_moe_route(const float *hidden_state, const uint8_t *gate, uint32_t gate_type, int hidden, int experts,
+                         int top_k, float *logits, int *selected, float *weights)
+{
+    if (orc_matmul(hidden_state, gate, logits, experts, gate_type, hidden, experts) != 0) return -1;
+    for (int i = 0; i < top_k; i++) {
+        int best = -1;
+        float bv = -FLT_MAX;
+        for (int j = 0; j < experts; j++) {
+            int skip = 0;
+            for (int k = 0; k < i; k++) if (selected[k] == j) { skip = 1; break; }
+            if (skip) continue;
+            if (logits[j] > bv) { bv = logits[j]; best = j; }
+        }
+        selected[i] = best;
+        weights[i] = bv;
+    }
+    float mx = -FLT_MAX;
+    for (int i = 0; i < top_k; i++) if (weights[i] > mx) mx = weights[i];
+    float sum = 0.0f;
+    for (int i = 0; i < top_k; i++) {
+        weights[i] = expf(weights[i] - mx);
+        sum += weights[i];
+    }
+    for (int i = 0; i < top_k; i++) weights[i] /= sum;
+    return 0;
+}
 
 /* ------------------------------------------------------------------------ */
 /* Session: KvCache (src/Llmdot.Core/Inference/KvCache.cs:3-43) and InferenceBuffers
@@ -1091,6 +1225,10 @@ typedef struct {
     int pos;
     float *h, *logits, *norm, *norm2, *normtmp, *q, *k, *v, *attnout, *attnres, *ffn, *ffnres, *score;
     float *scratch;
+    oconv *conv;                         /* ConvStateCache when HasConvLayers */
+    float *convb, *convq, *convw;        /* ConvBuf, the conv output, the dequantised conv weights */
+    float *moe_logits, *moe_w, *moe_acc, *moe_res;
+    int *moe_sel;
 } osess;
 
 EXPORT void orc_session_free(osess *s)
@@ -1099,6 +1237,9 @@ EXPORT void orc_session_free(osess *s)
     free(s->kc); free(s->vc); free(s->h); free(s->logits); free(s->norm); free(s->norm2); free(s->normtmp);
     free(s->q); free(s->k); free(s->v); free(s->attnout); free(s->attnres); free(s->ffn); free(s->ffnres);
     free(s->score); free(s->scratch);
+    orc_conv_state_free(s->conv);
+    free(s->convb); free(s->convq); free(s->convw);
+    free(s->moe_logits); free(s->moe_w); free(s->moe_acc); free(s->moe_res); free(s->moe_sel);
     free(s);
 }
 
@@ -1121,8 +1262,29 @@ EXPORT osess *orc_session_new(omodel *m)
     s->ffn = (float *)calloc(inter, 4); s->ffnres = (float *)calloc(hid, 4);
     s->score = (float *)calloc(hid > (size_t)c->context ? hid : (size_t)c->context, 4);
     s->scratch = (float *)calloc(qDim + 2 * kvDim + hid, 4);
+    if (c->template_id == TPL_LFM2) {   /* InferenceEngine.cs:52 */
+        s->conv = orc_conv_state_new(c->layers, c->hidden, m->conv_kernel);
+        s->convb = (float *)calloc(hid, 4);
+        s->convq = (float *)calloc(hid, 4);
+        s->convw = (float *)calloc((size_t)m->conv_kernel * hid, 4);
+    }
+    if (c->expert_count > 0) {          /* InferenceBuffers.cs:56-60 */
+        int tk = m->expert_used > 0 ? m->expert_used : 1;
+        s->moe_logits = (float *)calloc((size_t)c->expert_count, 4);
+        s->moe_w = (float *)calloc((size_t)tk, 4);
+        s->moe_sel = (int *)calloc((size_t)tk, sizeof(int));
+        s->moe_acc = (float *)calloc(hid, 4);
+        s->moe_res = (float *)calloc(hid, 4);
+    }
     if (!s->kc || !s->vc) { orc_session_free(s); snprintf(g_err, sizeof g_err, "out of memory"); return NULL; }
     return s;
+}
+
+/* Generate's _kvCache.Reset() / _convCache?.Reset() (InferenceEngine.cs:79-80) */
+EXPORT void orc_session_reset(osess *s)
+{
+    s->pos = 0;
+    if (s->conv) orc_conv_state_reset(s->conv);
 }
 
 static float *norm_weights(omodel *m, otensor *t, float *buf)
@@ -1289,6 +1451,84 @@ static int ffn_forward(osess *s, int layer, const float *input)
     return rc;
 }
 
+/* ProcessConvLayer :222-277, the operator half: in_proj -> (B, C, x) chunks; B*x through the
+ * short causal conv over the ConvStateCache window; times C; out_proj; residual add.  A conv
+ * layer without in_proj or conv weights only stores its normed input. */
+static int conv_forward(osess *s, int layer, int position)
+{
+    omodel *m = s->m;
+    orc_config *c = &m->cfg;
+    const int hidden = c->hidden, K = m->conv_kernel;
+    otensor *inp = find_tf(m, "blk.%d.shortconv.in_proj.weight", layer);
+    otensor *cw = find_tf(m, "blk.%d.conv1d.weight", layer);
+    if (!cw) cw = find_tf(m, "blk.%d.shortconv.conv.weight", layer);
+    if (!inp || !cw || !s->conv) {
+        if (s->conv) orc_conv_state_store(s->conv, layer, s->norm);
+        return 0;
+    }
+    /* GetDequantizedConvWeights :279-301 */
+    if (cw->type == T_F32) memcpy(s->convw, cw->data, sizeof(float) * (size_t)K * hidden);
+    else orc_dequantize(cw->data, s->convw, cw->type, cw->ndims > 1 ? (int)cw->dims[1] : 1, (int)cw->dims[0]);
+    int inCols = (int)(inp->nelem / (uint64_t)hidden);
+    size_t ffnLen = 2 * (size_t)c->ffn > 3 * (size_t)hidden ? 2 * (size_t)c->ffn : 3 * (size_t)hidden;
+    float *ib = (size_t)inCols <= ffnLen ? s->ffn : (float *)malloc(sizeof(float) * (size_t)inCols);
+    int rc = matmul_tensor(s->norm, inp, ib, inCols);
+    const float *bch = ib, *cch = ib + hidden, *xch = ib + 2 * hidden;
+    orc_mul(bch, xch, s->convb, hidden);
+    const float *win = orc_conv_state_build(s->conv, layer, s->convb, position);
+    orc_conv1d(win, s->convw, s->convq, K, hidden);
+    orc_conv_state_store(s->conv, layer, s->convb);
+    orc_mul(s->convq, cch, s->convq, hidden);
+    otensor *op = find_tf(m, "blk.%d.shortconv.out_proj.weight", layer);
+    if (op) rc |= matmul_tensor(s->convq, op, s->attnres, (int)(op->nelem / (uint64_t)hidden));
+    else memcpy(s->attnres, s->convq, sizeof(float) * hidden);
+    orc_add(s->h, s->attnres, s->h, hidden);
+    if (ib != s->ffn) free(ib);
+    return rc;
+}
+
+/* MoeFfnForward :489-542: route, then per selected expert a SwiGLU FFN through its own
+ * blk.N.ffn_{gate,up,down}.E tensors, scaled by the routing weight and added in selection
+ * order; experts whose tensors are missing are skipped.  ResolveLayer (TensorNameResolver.cs:
+ * 109-165) requires the dense ffn_up / ffn_down names to exist even though they are unused. */
+static int moe_forward(osess *s, int layer, const float *input)
+{
+    omodel *m = s->m;
+    orc_config *c = &m->cfg;
+    const int hidden = c->hidden, E = c->expert_count, topK = m->expert_used;
+    if (!has_name(m, "blk.%d.ffn_up.weight", layer) || !has_name(m, "blk.%d.ffn_down.weight", layer)) {
+        snprintf(g_err, sizeof g_err, "Tensor 'blk.%d.ffn_up/ffn_down.weight' not found in model.", layer);
+        return -1;
+    }
+    otensor *gate = find_tf(m, "blk.%d.ffn_gate_inp.weight", layer);
+    if (!gate) { snprintf(g_err, sizeof g_err, "missing blk.%d.ffn_gate_inp.weight", layer); return -1; }
+    if (orc_moe_route(input, gate->data, gate->type, hidden, E, topK, s->moe_logits, s->moe_sel, s->moe_w) != 0) return -1;
+    memset(s->moe_acc, 0, sizeof(float) * hidden);
+    int rc = 0;
+    size_t ffnLen = 2 * (size_t)c->ffn > 3 * (size_t)hidden ? 2 * (size_t)c->ffn : 3 * (size_t)hidden;
+    for (int i = 0; i < topK; i++) {
+        int e = s->moe_sel[i];
+        char nb[128];
+        otensor *g, *u, *d;
+        snprintf(nb, sizeof nb, "blk.%d.ffn_gate.%d.weight", layer, e); g = find_t(m, nb);
+        snprintf(nb, sizeof nb, "blk.%d.ffn_up.%d.weight", layer, e); u = find_t(m, nb);
+        snprintf(nb, sizeof nb, "blk.%d.ffn_down.%d.weight", layer, e); d = find_t(m, nb);
+        if (!g || !u || !d) continue;
+        int gc = (int)(g->nelem / (uint64_t)hidden), uc = (int)(u->nelem / (uint64_t)hidden);
+        float *fb = (size_t)gc + uc <= ffnLen ? s->ffn : (float *)malloc(sizeof(float) * ((size_t)gc + uc));
+        rc |= matmul_tensor(input, g, fb, gc);
+        orc_silu(fb, fb, gc);
+        rc |= matmul_tensor(input, u, fb + gc, uc);
+        orc_mul(fb, fb + gc, fb, gc);
+        rc |= matmul_tensor(fb, d, s->moe_res, hidden);
+        orc_scale(s->moe_res, s->moe_w[i], s->moe_res, hidden);
+        orc_add(s->moe_acc, s->moe_res, s->moe_acc, hidden);
+        if (fb != s->ffn) free(fb);
+    }
+    memcpy(s->ffnres, s->moe_acc, sizeof(float) * hidden);
+    return rc;
+}
+
 /* ProcessToken :134-146 with ProcessLayer :158-220 and ComputeLogits :583-602.
  * Writes the raw logits (before any final softcap) to s->logits. */
 EXPORT int orc_process_token(osess *s, int token, int position)
@@ -1310,13 +1550,21 @@ EXPORT int orc_process_token(osess *s, int token, int position)
             rc |= ffn_forward(s, l, s->norm2);
             orc_add(s->attnres, s->ffnres, s->ffnres, hidden);
             orc_add(s->h, s->ffnres, s->h, hidden);
+        } else if (c->template_id == TPL_LFM2 && !m->layer_attn[l]) {   /* ProcessConvLayer :222-277 */
+            apply_norm(s, s->h, s->norm, l, 1);
+            rc |= conv_forward(s, l, position);
+            apply_norm(s, s->h, s->norm2, l, 0);
+            rc |= c->expert_count > 0 ? moe_forward(s, l, s->norm2) : ffn_forward(s, l, s->norm2);
+            orc_add(s->h, s->ffnres, s->h, hidden);
         } else {                                                  /* :184-196, :209-220 */
             apply_norm(s, s->h, s->norm, l, 1);
             rc |= attention_forward(s, l, position, s->norm);
             orc_add(s->h, s->attnres, s->h, hidden);
             if (c->template_id == TPL_GEMMA && c->has_post_norm) apply_post_norm(s, l, 1);
             apply_norm(s, s->h, s->norm, l, 0);
-            rc |= ffn_forward(s, l, s->norm);
+            /* LlamaLike (and Lfm2Like attention layers) route through the experts when present */
+            if (c->template_id != TPL_GEMMA && c->expert_count > 0) rc |= moe_forward(s, l, s->norm);
+            else rc |= ffn_forward(s, l, s->norm);
             orc_add(s->h, s->ffnres, s->h, hidden);
             if (c->template_id == TPL_GEMMA && c->has_post_norm) apply_post_norm(s, l, 0);
         }
@@ -1346,7 +1594,7 @@ EXPORT int orc_generate(osess *s, const int *prompt, int nPrompt, int maxTokens,
 {
     omodel *m = s->m;
     orc_config *c = &m->cfg;
-    s->pos = 0;
+    orc_session_reset(s);
     int have = 0;
     for (int i = 0; i < nPrompt; i++) {
         if (orc_process_token(s, prompt[i], i)) return -1;
@@ -1528,7 +1776,7 @@ EXPORT int orc_generate_sampled(osess *s, const int *prompt, int nPrompt, int ma
 {
     omodel *m = s->m;
     orc_config *c = &m->cfg;
-    s->pos = 0;
+    orc_session_reset(s);
     int have = 0;
     for (int i = 0; i < nPrompt; i++) {
         if (orc_process_token(s, prompt[i], i)) return -1;

@@ -100,6 +100,16 @@ def lib():
         L.orc_net_random_single.argtypes = [C.c_int]
         L.orc_generate_sampled.argtypes = [C.c_void_p, I32P, C.c_int, C.c_int, C.c_int, C.c_float, C.c_float,
                                            C.c_float, C.c_int, F32P, I32P]
+        L.orc_session_reset.argtypes = [C.c_void_p]
+        L.orc_conv_state_new.restype = C.c_void_p
+        L.orc_conv_state_new.argtypes = [C.c_int, C.c_int, C.c_int]
+        L.orc_conv_state_free.argtypes = [C.c_void_p]
+        L.orc_conv_state_store.argtypes = [C.c_void_p, C.c_int, F32P]
+        L.orc_conv_state_build.restype = F32P
+        L.orc_conv_state_build.argtypes = [C.c_void_p, C.c_int, F32P, C.c_int]
+        L.orc_conv_state_reset.argtypes = [C.c_void_p]
+        L.orc_conv1d.argtypes = [F32P, F32P, F32P, C.c_int, C.c_int]
+        L.orc_moe_route.argtypes = [F32P, U8P, C.c_uint32, C.c_int, C.c_int, C.c_int, F32P, I32P, F32P]
         _lib = L
     return _lib
 
@@ -298,6 +308,59 @@ class SamplingOptions:
         self.repeat_penalty, self.repeat_window, self.seed = float(repeat_penalty), int(repeat_window), int(seed)
 
 
+class ConvState:
+    """ConvStateCache (src/Llmdot.Core/Inference/ConvStateCache.cs:3-65)."""
+
+    def __init__(self, layers: int, hidden: int, kernel: int):
+        self.hidden, self.kernel = hidden, kernel
+        self._h = lib().orc_conv_state_new(layers, hidden, kernel)
+        if not self._h:
+            raise ValueError("bad conv state shape")
+
+    def store(self, layer: int, x) -> None:
+        lib().orc_conv_state_store(self._h, layer, _f(np.ascontiguousarray(x, dtype=np.float32)))
+
+    def build_input(self, layer: int, current, position: int) -> np.ndarray:
+        cur = np.ascontiguousarray(current, dtype=np.float32)
+        p = lib().orc_conv_state_build(self._h, layer, _f(cur), position)
+        return np.ctypeslib.as_array(p, shape=(self.kernel * self.hidden,)).copy()
+
+    def reset(self) -> None:
+        lib().orc_conv_state_reset(self._h)
+
+    def close(self):
+        if self._h:
+            lib().orc_conv_state_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def conv1d(x, w, kernel_size: int, dim: int) -> np.ndarray:
+    """TensorOps.Conv1D (TensorOps.cs:745-778)."""
+    x, w = np.ascontiguousarray(x, dtype=np.float32), np.ascontiguousarray(w, dtype=np.float32)
+    out = np.zeros(dim, dtype=np.float32)
+    lib().orc_conv1d(_f(x), _f(w), _f(out), kernel_size, dim)
+    return out
+
+
+def moe_route(hidden_state, gate: np.ndarray, gate_type: int, experts: int, top_k: int):
+    """MoeRouter.Route (MoeRouter.cs:12-59): (gate logits, selected experts, routing weights)."""
+    h = np.ascontiguousarray(hidden_state, dtype=np.float32)
+    g = np.ascontiguousarray(gate).view(np.uint8)
+    logits = np.zeros(experts, dtype=np.float32)
+    sel = np.zeros(max(top_k, 1), dtype=np.int32)
+    w = np.zeros(max(top_k, 1), dtype=np.float32)
+    if lib().orc_moe_route(_f(h), _u8(g), gate_type, h.size, experts, top_k, _f(logits), sel.ctypes.data_as(I32P),
+                           _f(w)) != 0:
+        raise ValueError("unsupported gate type")
+    return logits, sel[:top_k], w[:top_k]
+
+
 def net_random_single(seed: int) -> float:
     """new System.Random(seed).NextSingle() (restated, see the C source)."""
     return float(lib().orc_net_random_single(int(seed)))
@@ -323,6 +386,10 @@ class Session:
         self._h = lib().orc_session_new(model._h)
         if not self._h:
             raise MemoryError(lib().orc_last_error().decode())
+
+    def reset(self) -> None:
+        """Generate's KvCache / ConvStateCache reset (InferenceEngine.cs:79-80)."""
+        lib().orc_session_reset(self._h)
 
     def process_token(self, token: int, position: int) -> np.ndarray:
         if lib().orc_process_token(self._h, int(token), int(position)) != 0:

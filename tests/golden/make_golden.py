@@ -13,9 +13,12 @@
   sampled_tokens.json  token ids of the oracle's Generate with Sampler.Sample on
                     the same models: seeded (one draw, new Random(42).NextSingle())
                     and with per-token draws listed in the file.
+  template_tokens.json  greedy token ids and logit checksums of the oracle on the
+                    LFM2 short-conv and MoE synthetic models.
 
-Run:  python tests/golden/make_golden.py            (every fixture)
-      python tests/golden/make_golden.py sampled    (sampled_tokens.json only)
+Run:  python tests/golden/make_golden.py              (every fixture)
+      python tests/golden/make_golden.py sampled      (sampled_tokens.json only)
+      python tests/golden/make_golden.py templates    (template_tokens.json only)
 """
 from __future__ import annotations
 
@@ -287,6 +290,23 @@ def make_greedy() -> dict:
     return res
 
 
+def make_templates() -> dict:
+    from dotllm_b200 import synth
+    from oracle import oracle as O
+    O.set_threads(max(1, O.max_threads()))
+    res = {}
+    for name in ("micro-lfm2", "micro-moe", "micro-lfm2moe"):
+        cfg = synth.get(name)
+        m = O.Model(synth.build_model(cfg))
+        s = O.Session(m)
+        toks, lg = s.generate(synth.prompt_tokens(cfg), 16, want_logits=True)
+        res[name] = dict(steps=16, tokens=[int(t) for t in toks],
+                         logit_sum=[float(x) for x in lg.astype(np.float64).sum(axis=1)])
+        s.close()
+        m.close()
+    return res
+
+
 SAMPLED_OPTIONS = dict(top_k=40, top_p=0.95, temperature=0.8, repeat_penalty=1.1, repeat_window=16)
 
 
@@ -311,11 +331,16 @@ def make_sampled() -> dict:
 
 
 if __name__ == "__main__":
-    if len(sys.argv) < 2 or sys.argv[1] != "sampled":
+    only = sys.argv[1] if len(sys.argv) > 1 else None
+    if only is None:
         with open(os.path.join(HERE, "kquant_kat.json"), "w") as f:
             json.dump(make_kquant(), f, indent=1)
         with open(os.path.join(HERE, "greedy_tokens.json"), "w") as f:
             json.dump(make_greedy(), f, indent=1)
-    with open(os.path.join(HERE, "sampled_tokens.json"), "w") as f:
-        json.dump(make_sampled(), f, indent=1)
+    if only in (None, "sampled"):
+        with open(os.path.join(HERE, "sampled_tokens.json"), "w") as f:
+            json.dump(make_sampled(), f, indent=1)
+    if only in (None, "templates"):
+        with open(os.path.join(HERE, "template_tokens.json"), "w") as f:
+            json.dump(make_templates(), f, indent=1)
     print("wrote", os.listdir(HERE))
