@@ -57,6 +57,9 @@ class SynthConfig:
     conv_layers: Tuple[int, ...] = ()
     conv_kernel: int = 3
     qk_norm: bool = False
+    # LayerNorm (attention.layer_norm_epsilon, attn_norm.bias) instead of RMSNorm; FFN with a gate
+    layer_norm: bool = False
+    gated_ffn: bool = True
     # MoE FFN: expert count, experts used per token, each expert's FFN width
     experts: int = 0
     experts_used: int = 0
@@ -81,7 +84,7 @@ class SynthConfig:
 
 Q6 = GGML_Q6_K
 # F32 tensors and the std of their random values (norm vectors are 1 + N(0, 0.01))
-F32_ROLES = {"norm": None, "conv": 0.5, "router": 0.1}
+F32_ROLES = {"norm": None, "conv": 0.5, "router": 0.1, "bias": 0.01}
 
 # BASELINE.json configs[0..4]
 CONFIGS: Dict[str, SynthConfig] = {
@@ -136,6 +139,9 @@ TEST_CONFIGS: Dict[str, SynthConfig] = {
         name="micro-lfm2", arch="lfm2", layers=4, hidden=256, heads=4, heads_kv=2, head_dim=64, ffn=512,
         vocab=1000, context=256, tied=True, conv_layers=(0, 2), qk_norm=True, seed=15,
         prompt_len=8, decode_len=16),
+    "micro-neox": SynthConfig(
+        name="micro-neox", arch="phi2", layers=2, hidden=256, heads=4, heads_kv=4, head_dim=64, ffn=512,
+        vocab=1000, context=256, layer_norm=True, gated_ffn=False, seed=18, prompt_len=8, decode_len=16),
     "micro-moe": SynthConfig(
         name="micro-moe", arch="llama", layers=2, hidden=256, heads=4, heads_kv=2, head_dim=64, ffn=512,
         vocab=1000, context=256, experts=4, experts_used=2, expert_ffn=256, seed=16, prompt_len=8, decode_len=16),
@@ -170,6 +176,8 @@ def tensor_plan(cfg: SynthConfig) -> List[Tuple[TensorInfo, str]]:
     for l in range(cfg.layers):
         p = f"blk.{l}."
         add(p + "attn_norm.weight", [d], "norm")
+        if cfg.layer_norm:
+            add(p + "attn_norm.bias", [d], "bias")
         if l in cfg.conv_layers:
             # TensorNameResolver.cs:79-89: in_proj -> (B, C, x), the depthwise kernel [K][d], out_proj
             add(p + "shortconv.in_proj.weight", [d, 3 * d], "conv_in")
@@ -200,7 +208,8 @@ def tensor_plan(cfg: SynthConfig) -> List[Tuple[TensorInfo, str]]:
             add(p + "ffn_up.weight", [d, f], "ffn_up")
             add(p + "ffn_down.weight", [f, d], "ffn_down")
         else:
-            add(p + "ffn_gate.weight", [d, f], "ffn_gate")
+            if cfg.gated_ffn:
+                add(p + "ffn_gate.weight", [d, f], "ffn_gate")
             add(p + "ffn_up.weight", [d, f], "ffn_up")
             add(p + "ffn_down.weight", [f, d], "ffn_down")
         if cfg.post_norm:
@@ -232,7 +241,8 @@ def metadata_for(cfg: SynthConfig) -> Metadata:
         md.add(f"{a}.expert_used_count", U32, cfg.experts_used)
     md.add(f"{a}.attention.key_length", U32, cfg.head_dim)
     md.add(f"{a}.attention.value_length", U32, cfg.head_dim)
-    md.add(f"{a}.attention.layer_norm_rms_epsilon", F32, cfg.eps)
+    md.add(f"{a}.attention.layer_norm_epsilon" if cfg.layer_norm else f"{a}.attention.layer_norm_rms_epsilon",
+           F32, cfg.eps)
     md.add(f"{a}.rope.freq_base", F32, cfg.rope_base)
     md.add(f"{a}.rope.dimension_count", U32, cfg.head_dim)
     if cfg.sliding_window:

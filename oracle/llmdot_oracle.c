@@ -1548,7 +1548,10 @@ EXPORT int orc_process_token(osess *s, int token, int position)
             rc |= attention_forward(s, l, position, s->norm);
             apply_norm(s, s->h, s->norm2, l, 0);
             rc |= ffn_forward(s, l, s->norm2);
-            orc_add(s->attnres, s->ffnres, s->ffnres, hidden);
+            /* Add(AttnResultBuf, FfnResultBuf) then Add(hs, FfnResultBuf): the two-argument Add
+             * writes its first argument (VectorMath.cs:27-42), so the sum lands in the attention
+             * buffer and only the FFN output reaches the hidden state */
+            orc_add(s->attnres, s->ffnres, s->attnres, hidden);
             orc_add(s->h, s->ffnres, s->h, hidden);
         } else if (c->template_id == TPL_LFM2 && !m->layer_attn[l]) {   /* ProcessConvLayer :222-277 */
             apply_norm(s, s->h, s->norm, l, 1);

@@ -14,7 +14,7 @@
                     the same models: seeded (one draw, new Random(42).NextSingle())
                     and with per-token draws listed in the file.
   template_tokens.json  greedy token ids and logit checksums of the oracle on the
-                    LFM2 short-conv and MoE synthetic models.
+                    LFM2 short-conv, MoE and GPT-NeoX-like synthetic models.
 
 Run:  python tests/golden/make_golden.py              (every fixture)
       python tests/golden/make_golden.py sampled      (sampled_tokens.json only)
@@ -295,7 +295,7 @@ def make_templates() -> dict:
     from oracle import oracle as O
     O.set_threads(max(1, O.max_threads()))
     res = {}
-    for name in ("micro-lfm2", "micro-moe", "micro-lfm2moe"):
+    for name in ("micro-lfm2", "micro-moe", "micro-lfm2moe", "micro-neox"):
         cfg = synth.get(name)
         m = O.Model(synth.build_model(cfg))
         s = O.Session(m)

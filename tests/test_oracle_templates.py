@@ -307,3 +307,44 @@ def test_golden_template_tokens():
         m.close()
         assert list(toks) == g["tokens"], name
         assert np.allclose(lg.astype(np.float64).sum(axis=1), g["logit_sum"], rtol=1e-5, atol=1e-3), name
+
+
+def _with_new_attention(src: str, dst: str, seed: int) -> None:
+    """A copy of the GGUF whose attn_q/k/v/output tensors hold other random weights."""
+    from dotllm_b200 import quant
+    f = gguf.GgufFile(src)
+    raw = bytearray(open(src, "rb").read())
+    rng = np.random.default_rng(seed)
+    for name, t in f.tensors.items():
+        if any(k in name for k in ("attn_q.", "attn_k.", "attn_v.", "attn_output.")):
+            x = rng.standard_normal((t.dims[1], t.dims[0]), dtype=np.float32) * np.float32(0.05)
+            b = quant.quantize(x, t.ggml_type).tobytes()
+            assert len(b) == t.n_bytes
+            raw[t.data_offset:t.data_offset + t.n_bytes] = b
+    open(dst, "wb").write(bytes(raw))
+
+
+@pytest.mark.parametrize("name,dropped", [("micro-neox", True), ("micro", False)])
+def test_neox_layer_adds_only_the_ffn_output(tmp_path, name, dropped):
+    """ProcessGptNeoXLikeLayer (InferenceEngine.cs:198-207) adds the FFN result into the attention
+    buffer and then only the FFN result into the hidden state (the two-argument Add writes its
+    first argument, VectorMath.cs:27-42), so a NeoX model's logits do not depend on its attention
+    weights at all; a LlamaLike model's do (the control case)."""
+    cfg = synth.get(name)
+    a = synth.build_model(cfg)
+    b = str(tmp_path / "other_attention.gguf")
+    _with_new_attention(a, b, 99)
+    prompt = synth.prompt_tokens(cfg)[:6]
+    outs = []
+    for p in (a, b):
+        m = O.Model(p)
+        s = O.Session(m)
+        outs.append(np.stack([s.process_token(int(t), i) for i, t in enumerate(prompt)]))
+        s.close()
+        m.close()
+    assert np.array_equal(outs[0], outs[1]) == dropped
+
+
+def test_neox_config_resolves_layer_norm_standard_ffn_parallel_residual():
+    c = O.Model(synth.build_model(synth.get("micro-neox"))).config
+    assert (c["template_id"], c["norm_is_rms"], c["ffn_type"], c["parallel_residual"]) == (1, 0, 0, 1)
