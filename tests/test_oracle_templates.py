@@ -1,11 +1,15 @@
-"""The oracle's LFM2 short-conv layers and MoE FFN (InferenceEngine.cs:222-301, 489-542;
-ConvStateCache.cs; MoeRouter.cs; TensorOps.Conv1D), templates the device does not run yet.
-CPU only.
+"""The oracle's layer templates against a second restatement.  CPU only.
 
-Pinned two ways: the assertions of the reference's own tests
-(tests/Llmdot.Core.Tests/Inference/ConvLayerTests.cs, ConvStateCacheTests.cs, MoeRouterTests.cs,
-line of each test cited), and a second, independent numpy restatement of the layer wiring (below)
-that must reproduce the oracle's logits on the synthetic LFM2 / MoE models.
+LFM2 short-conv layers and the MoE FFN (InferenceEngine.cs:222-301, 489-542; ConvStateCache.cs;
+MoeRouter.cs; TensorOps.Conv1D), which the device does not run yet, are pinned by the assertions
+of the reference's own tests (tests/Llmdot.Core.Tests/Inference/ConvLayerTests.cs,
+ConvStateCacheTests.cs, MoeRouterTests.cs, line of each test cited).  Every template the
+synthetic models use -- LlamaLike (Llama, Qwen2 with Q5_K/Q8_0, Phi-3 with fused QKV), GemmaLike
+(embedding scale, attention softcap, sliding window, post-norms, GeGLU) and Lfm2Like with dense or
+MoE FFNs -- is also restated a second time in numpy below, from the reference's source, with the
+oracle's pinned primitives (dequantisation, softmax with ExpApprox, SiLU / GELU lanes) as its only
+shared parts; it must reproduce the oracle's logits.  The GPT-NeoX-like layer is pinned by a
+property of the reference's residual (its logits do not depend on the attention weights).
 """
 import math
 
@@ -186,7 +190,11 @@ class _Model:
     def attention(self, l, x, pos):
         c, p = self.cfg, f"blk.{l}."
         hd, H, Hk = c.head_dim, c.heads, c.heads_kv
-        q, k, v = self.mv(p + "attn_q.weight", x), self.mv(p + "attn_k.weight", x), self.mv(p + "attn_v.weight", x)
+        if c.qkv_fused:  # one projection, split q | k | v (InferenceEngine.cs:321-331)
+            f = self.mv(p + "attn_qkv.weight", x)
+            q, k, v = f[:H * hd], f[H * hd:(H + Hk) * hd], f[(H + Hk) * hd:]
+        else:
+            q, k, v = self.mv(p + "attn_q.weight", x), self.mv(p + "attn_k.weight", x), self.mv(p + "attn_v.weight", x)
         qn = self.W(p + "attn_q_norm.weight")[0] if self.W.has(p + "attn_q_norm.weight") else None
         kn = self.W(p + "attn_k_norm.weight")[0] if self.W.has(p + "attn_k_norm.weight") else None
         q, k = q.reshape(H, hd), k.reshape(Hk, hd)
@@ -199,12 +207,14 @@ class _Model:
         self.k[l].append(k)
         self.v[l].append(v.reshape(Hk, hd))
         K, V = np.stack(self.k[l]), np.stack(self.v[l])  # [t, Hk, hd]
+        if c.sliding_window:  # every layer, window start max(0, p + 1 - SW) (:381-383)
+            K, V = K[max(0, pos + 1 - c.sliding_window):], V[max(0, pos + 1 - c.sliding_window):]
         out = np.zeros((H, hd), np.float32)
         g = H // Hk
         for h in range(H):
             sc = (K[:, h // g].astype(np.float64) @ q[h].astype(np.float64)).astype(np.float32)
             sc = (sc * (np.float32(1) / np.float32(math.sqrt(hd)))).astype(np.float32)
-            pr = O.softmax(sc)
+            pr = O.softmax(sc, softcap=c.attn_softcap)
             out[h] = (pr.astype(np.float64) @ V[:, h // g].astype(np.float64)).astype(np.float32)
         return self.mv(p + "attn_output.weight", out.reshape(-1))
 
@@ -230,7 +240,8 @@ class _Model:
     def ffn(self, l, x):
         c, p = self.cfg, f"blk.{l}."
         if not c.experts:
-            gt = O.silu(self.mv(p + "ffn_gate.weight", x))
+            gate = self.mv(p + "ffn_gate.weight", x)
+            gt = O.gelu(gate) if c.arch.startswith("gemma") else O.silu(gate)  # GeGLU / SwiGLU
             return self.mv(p + "ffn_down.weight", (gt * self.mv(p + "ffn_up.weight", x)).astype(np.float32))
         logits = self.mv(p + "ffn_gate_inp.weight", x)
         sel = []
@@ -250,19 +261,26 @@ class _Model:
     def token(self, tok, pos):
         c, W = self.cfg, self.W
         h = W("token_embd.weight")[tok].astype(np.float32).copy()
+        if c.arch.startswith("gemma"):  # EmbeddingScale = MathF.Sqrt(hidden) (ArchitectureResolver.cs:164-166)
+            h = (h * np.float32(math.sqrt(np.float32(c.hidden)))).astype(np.float32)
         for l in range(c.layers):
             p = f"blk.{l}."
             x = _rms(h, W(p + "attn_norm.weight")[0], c.eps)
             op = self.conv_op(l, x, pos) if l in c.conv_layers else self.attention(l, x, pos)
             h = (h + op).astype(np.float32)
+            if c.post_norm:  # GemmaLike post-norms of h after each residual add (:209-220)
+                h = _rms(h, W(p + "post_attention_norm.weight")[0], c.eps)
             x = _rms(h, W(p + "ffn_norm.weight")[0], c.eps)
             h = (h + self.ffn(l, x)).astype(np.float32)
+            if c.post_norm:
+                h = _rms(h, W(p + "post_ffw_norm.weight")[0], c.eps)
         h = _rms(h, W("output_norm.weight")[0], c.eps)
         head = "output.weight" if W.has("output.weight") else "token_embd.weight"
         return self.mv(head, h)
 
 
-@pytest.mark.parametrize("name", ["micro-lfm2", "micro-moe", "micro-lfm2moe"])
+@pytest.mark.parametrize("name", ["micro-lfm2", "micro-moe", "micro-lfm2moe",
+                                  "micro", "micro-gemma", "micro-phi3", "micro-q5q8"])
 def test_oracle_templates_match_independent_restatement(name):
     cfg = synth.get(name)
     path = synth.build_model(cfg)
@@ -271,7 +289,8 @@ def test_oracle_templates_match_independent_restatement(name):
     s = O.Session(m)
     s.reset()
     try:
-        toks = list(synth.prompt_tokens(cfg)[:6])
+        # past the micro-gemma sliding window (24) so the window start moves
+        toks = list(synth.prompt_tokens(cfg, 28 if cfg.sliding_window else 6))
         for pos, t in enumerate(toks):
             want = ref.token(int(t), pos)
             got = s.process_token(int(t), pos)
