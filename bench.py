@@ -23,6 +23,7 @@ import subprocess
 import sys
 import threading
 import time
+from typing import Optional
 
 import numpy as np
 
@@ -59,8 +60,9 @@ class ClockSampler:
     REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
     PERIOD_S = 0.01
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, uuid: Optional[str] = None):
         self.idx = gpu_index
+        self.uuid = uuid  # the CUDA device's UUID: NVML's order need not be CUDA's
         self.proc = None
         self.samples = []  # (sm_mhz, sm_max_mhz, [reason names]) from NVML
         self._stop = threading.Event()
@@ -72,7 +74,18 @@ class ClockSampler:
         except Exception:
             return
         try:
-            h = nv.nvmlDeviceGetHandleByIndex(self.idx)
+            h = None
+            if self.uuid:
+                want = self.uuid.lower().replace("gpu-", "")
+                for i in range(int(nv.nvmlDeviceGetCount())):
+                    hi = nv.nvmlDeviceGetHandleByIndex(i)
+                    u = nv.nvmlDeviceGetUUID(hi)
+                    u = u.decode() if isinstance(u, bytes) else str(u)
+                    if u.lower().replace("gpu-", "") == want:
+                        h = hi
+                        break
+            if h is None:
+                h = nv.nvmlDeviceGetHandleByIndex(self.idx)
             mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
             get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
                 nv.nvmlDeviceGetCurrentClocksThrottleReasons
@@ -230,7 +243,12 @@ def measure(m, cfg, args, B, n_prompt, ctx, rank, steps, dist, local, clocks=Fal
             gpu_index = int(vis.split(",")[local])
         except ValueError:
             pass
-    clk = ClockSampler(gpu_index if clocks else -1)
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        pass
+    clk = ClockSampler(gpu_index if clocks else -1, uuid)
     if clocks:
         with clk:
             out, dev_ms, kps = decode_steps(sessions, cur, steps)

@@ -75,3 +75,25 @@ def test_unsampled_when_nothing_answers(monkeypatch):
         pass
     assert c.summary()["reasons"] == ["unsampled"]
     assert nv.calls == ["init", "shutdown"]
+
+
+def test_nvml_device_found_by_uuid(monkeypatch):
+    """The CUDA device's UUID picks the NVML handle; the index is only the fallback."""
+    nv = _fake_nvml([1700], [0])
+    nv.nvmlDeviceGetCount = lambda: 4
+    nv.nvmlDeviceGetUUID = lambda h: f"GPU-0000000{h[1]}-aaaa".encode()
+    seen = []
+
+    def clock(h, c):
+        seen.append(h)
+        return 1700
+    nv.nvmlDeviceGetClockInfo = clock
+    monkeypatch.setitem(sys.modules, "pynvml", nv)
+    monkeypatch.setattr(bench.subprocess, "Popen", lambda *a, **k: (_ for _ in ()).throw(OSError("no smi")))
+    with bench.ClockSampler(0, uuid="00000002-aaaa") as c:
+        time.sleep(0.03)
+    assert c.summary()["samples"] >= 1 and set(seen) == {("dev", 2)}
+    seen.clear()
+    with bench.ClockSampler(1, uuid="not-present") as c:
+        time.sleep(0.03)
+    assert set(seen) == {("dev", 1)}
