@@ -1,7 +1,8 @@
 """ArchitectureResolver.Resolve (src/Llmdot.Core/Loading/ArchitectureResolver.cs:14-112) in the
 library's native GGUF parser (llmdot_cuda_gguf_config, host only) and in the oracle, on the
-metadata-only files of the reference's tests/Llmdot.Core.Tests/Loading/ArchitectureResolverTests.cs
-(line of each test cited) and against each other.  CPU only.
+files of the reference's tests/Llmdot.Core.Tests/Loading/ArchitectureResolverTests.cs,
+SmolLm2ResolverTests.cs and GgufReaderTests.cs (line of each test cited), and against each other.
+CPU only.
 
 The files are written byte for byte as that test's WriteGguf helper (:179-245) writes them:
 GGUF v3, no tensors, UInt32 / Float32 / String values, and Bool written as a 4-byte UInt32
@@ -24,8 +25,10 @@ def _s(v: str) -> bytes:
     return struct.pack("<Q", len(b)) + b
 
 
-def write_meta_gguf(path, entries):
-    out = b"GGUF" + struct.pack("<IQQ", 3, 0, len(entries))
+def write_meta_gguf(path, entries, tensor_names=()):
+    """Metadata, then (SmolLm2ResolverTests.cs:188-215) one tensor info per name -- 1 dim of 1,
+    F32, offset 0 -- padding to 32 bytes and a 0f per tensor."""
+    out = b"GGUF" + struct.pack("<IQQ", 3, len(tensor_names), len(entries))
     for key, t, v in entries:
         out += _s(key) + struct.pack("<I", t)
         if t == U32:
@@ -36,6 +39,10 @@ def write_meta_gguf(path, entries):
             out += _s(v)
         elif t == BOOL:
             out += struct.pack("<I", 1 if v else 0)
+    for name in tensor_names:
+        out += _s(name) + struct.pack("<IQIQ", 1, 1, 0, 0)
+    if tensor_names:
+        out += b"\0" * ((32 - len(out) % 32) % 32) + struct.pack("<f", 0.0) * len(tensor_names)
     with open(path, "wb") as f:
         f.write(out)
     return str(path)
@@ -177,3 +184,50 @@ def test_gguf_reader_cases(tmp_path):
     old.write_bytes(b"GGUF" + struct.pack("<IQQ", 1, 0, 0))
     with pytest.raises(CudaBackendError, match="Unsupported GGUF version"):
         gguf_config(str(old))
+
+
+# ---- tests/Llmdot.Core.Tests/Loading/SmolLm2ResolverTests.cs --------------------------------
+
+def _smol(hidden, layers, ffn, heads, heads_kv, key_length=True, rope=False):
+    e = [("general.architecture", STR, "llama"), ("llama.embedding_length", U32, hidden),
+         ("llama.block_count", U32, layers), ("llama.context_length", U32, 2048),
+         ("llama.feed_forward_length", U32, ffn), ("llama.attention.head_count", U32, heads),
+         ("llama.attention.head_count_kv", U32, heads_kv)]
+    if key_length:
+        e.append(("llama.attention.key_length", U32, 64))
+    e.append(("llama.attention.layer_norm_rms_epsilon", F32, 1e-5))
+    if rope:
+        e.append(("llama.rope.freq_base", F32, 10000.0))
+    return e
+
+
+@pytest.mark.parametrize("entries,want", [
+    (_smol(576, 30, 1536, 9, 3, rope=True),                                            # :11-44
+     dict(template_id=0, hidden=576, layers=30, context=2048, ffn=1536, heads=9, heads_kv=3, head_dim=64,
+          ffn_type=1, norm_is_rms=1, rope_base=10000.0, tied=1)),
+    (_smol(960, 32, 2560, 15, 5), dict(hidden=960, layers=32, ffn=2560, heads=15, heads_kv=5)),     # :46-71
+    (_smol(2048, 24, 8192, 32, 32), dict(hidden=2048, layers=24, ffn=8192, heads=32, heads_kv=32)),  # :73-98
+])
+def test_smollm2_configs(tmp_path, entries, want):
+    c = both(write_meta_gguf(tmp_path / "a.gguf", entries, ["blk.0.ffn_gate.weight"]))
+    for k, v in want.items():
+        assert c[k] == v, k
+    assert attention_type(c) == ("MHA" if c["heads"] == c["heads_kv"] else "GQA")
+
+
+def test_smollm2_tied_and_separate_output(tmp_path):  # :100-140
+    e = _smol(576, 30, 1536, 9, 3, key_length=False)
+    assert both(write_meta_gguf(tmp_path / "t.gguf", e, ["token_embd.weight"]))["tied"] == 1
+    assert both(write_meta_gguf(tmp_path / "s.gguf", e, ["token_embd.weight", "output.weight"]))["tied"] == 0
+
+
+def test_smollm2_swiglu_from_gate_tensor(tmp_path):  # :142-161
+    e = _smol(576, 30, 1536, 9, 3, key_length=False)
+    assert both(write_meta_gguf(tmp_path / "a.gguf", e, ["blk.0.ffn_gate.weight"]))["ffn_type"] == 1
+    assert both(write_meta_gguf(tmp_path / "b.gguf", e, ["blk.0.ffn_up.weight"]))["ffn_type"] == 0
+
+
+def test_smollm2_rope_parameters(tmp_path):  # :163-186
+    e = _smol(576, 30, 1536, 9, 3, rope=True) + [("llama.rope.dimension_count", U32, 64)]
+    c = both(write_meta_gguf(tmp_path / "a.gguf", e))
+    assert c["rope_base"] == 10000.0 and c["rope_dim"] == 64
