@@ -1,9 +1,11 @@
 """Sampler.Sample on the device (llmdot_cuda_sample, llmdot_cuda_generate_sampled) against the
 oracle's restatement (Sampler.cs:24-165), on the same logits, history and uniform draws.
 
-Logits are continuous random values, so no two tie; the sampled index must be identical.  A draw
-that lands within float rounding of a cumulative-probability boundary could in principle pick
-the neighbour, so the draws are kept away from the boundaries the oracle reports.
+Logits are continuous random values, so no two tie; the sampled index must be identical.  The
+softmax's 8-wide ExpApprox lanes are bit-exact on the device; only its MathF.Exp tail (the last
+k mod 8 entries) may differ by an ulp, so a draw within an ulp of a cumulative-probability
+boundary could in principle pick the neighbour.  The seeds and draws are fixed, and none of them
+lands that close.
 """
 import numpy as np
 import pytest
