@@ -1691,6 +1691,66 @@ static int find_nucleus(const float *p, int n, float topP, int *idx, float *val)
     return count;
 }
 
+/* FindNucleus's result without its quadratic sort, for rows of any size (same idx prefix, same
+ * aliased writes into p, same count).  The selection sort takes, at each pass, the first
+ * maximum in the CURRENT order and swaps it with the pass position; values are distinct across
+ * tie groups, so groups come out in descending value, and inside a group the members leave in the
+ * order of their positions at the moment the group becomes the maximum: the only element a pass
+ * displaces is the occupant of the pass position, the smallest remaining position, and an
+ * occupant that belongs to the current group is itself that group's first member.  So: sort by
+ * value, and per group order the members by their current positions while replaying the swaps. */
+typedef struct { float v; int i; } vkey;
+static int vkey_desc(const void *a, const void *b)
+{
+    const vkey *x = (const vkey *)a, *y = (const vkey *)b;
+    if (x->v > y->v) return -1;
+    if (x->v < y->v) return 1;
+    return x->i - y->i;
+}
+static int *g_pos_for_cmp;
+static int pos_asc(const void *a, const void *b)
+{
+    return g_pos_for_cmp[*(const int *)a] - g_pos_for_cmp[*(const int *)b];
+}
+static int find_nucleus_fast(float *p, int n, float topP, int *idx)
+{
+    vkey *ord = (vkey *)malloc(sizeof(vkey) * (size_t)n);
+    int *pos = (int *)malloc(sizeof(int) * (size_t)n), *at = (int *)malloc(sizeof(int) * (size_t)n);
+    int *grp = (int *)malloc(sizeof(int) * (size_t)n);
+    for (int e = 0; e < n; e++) { ord[e].v = p[e]; ord[e].i = e; pos[e] = e; at[e] = e; }
+    qsort(ord, (size_t)n, sizeof(vkey), vkey_desc);
+    float cum = 0.0f;
+    int i = 0, count = n;
+    for (int g = 0; g < n && count == n;) {
+        int ge = g + 1;
+        while (ge < n && !(ord[ge].v < ord[g].v)) ge++;
+        int m = ge - g;
+        for (int k = 0; k < m; k++) grp[k] = ord[g + k].i;
+        g_pos_for_cmp = pos;
+        qsort(grp, (size_t)m, sizeof(int), pos_asc);
+        for (int k = 0; k < m; k++) {
+            int sel = grp[k], o = at[i];
+            if (o != sel) { at[pos[sel]] = o; pos[o] = pos[sel]; at[i] = sel; pos[sel] = i; }
+            idx[i] = sel;
+            float v = p[sel];  /* slot sel already holds a written value when sel < i */
+            p[i] = v;
+            cum += v;
+            i++;
+            if (cum >= topP) { count = i; break; }
+        }
+        g = ge;
+    }
+    free(ord); free(pos); free(at); free(grp);
+    return count;
+}
+
+/* Both forms on a copy of p (test hook): count; idx[0..count) and the written buffer out */
+EXPORT int orc_nucleus(const float *p, int n, float topP, int fast, int *idx, float *buf)
+{
+    memcpy(buf, p, sizeof(float) * (size_t)n);
+    return fast ? find_nucleus_fast(buf, n, topP, idx) : find_nucleus(buf, n, topP, idx, buf);
+}
+
 /* SampleFromProbabilities :153-165 */
 static int pick(const float *p, int n, float r)
 {
@@ -1723,9 +1783,10 @@ EXPORT int orc_sample(const float *logits, int n, int topK, float topP, float te
         out = -1;
         if (topP < 1.0f) {
             /* values alias the softmax row (Sample :48-50); when the nucleus is the whole row the
-             * fall-through pick below reads the overwritten row and returns a position */
+             * fall-through pick below reads the overwritten row and returns a position.  The
+             * sort-and-replay form gives the selection sort's result (tests hold the two equal) */
             float *val = x;
-            int ns = find_nucleus(x, n, topP, idx, val);
+            int ns = find_nucleus_fast(x, n, topP, idx);
             if (ns < n) {
                 float sum = 0.0f;
                 for (int i = 0; i < ns; i++) sum += val[i];

@@ -110,6 +110,7 @@ def lib():
         L.orc_conv_state_reset.argtypes = [C.c_void_p]
         L.orc_conv1d.argtypes = [F32P, F32P, F32P, C.c_int, C.c_int]
         L.orc_moe_route.argtypes = [F32P, U8P, C.c_uint32, C.c_int, C.c_int, C.c_int, F32P, I32P, F32P]
+        L.orc_nucleus.argtypes = [F32P, C.c_int, C.c_float, C.c_int, I32P, F32P]
         _lib = L
     return _lib
 
@@ -359,6 +360,16 @@ def moe_route(hidden_state, gate: np.ndarray, gate_type: int, experts: int, top_
                            _f(w)) != 0:
         raise ValueError("unsupported gate type")
     return logits, sel[:top_k], w[:top_k]
+
+
+def nucleus(p, top_p: float, fast: bool):
+    """FindNucleus (Sampler.cs:129-151) on a copy of p, literally (quadratic selection sort) or
+    by the sort-and-replay form: (count, idx[:count], the buffer after its aliased writes)."""
+    p = np.ascontiguousarray(p, dtype=np.float32)
+    idx = np.zeros(max(p.size, 1), dtype=np.int32)
+    buf = np.zeros(max(p.size, 1), dtype=np.float32)
+    n = lib().orc_nucleus(_f(p), p.size, top_p, 1 if fast else 0, idx.ctypes.data_as(I32P), _f(buf))
+    return n, idx[:n], buf[:p.size]
 
 
 def net_random_single(seed: int) -> float:

@@ -210,3 +210,25 @@ def test_top_p_only_random_rows_with_ties():
         p = O.softmax(x)
         for r in rng.uniform(0, 1, size=8):
             assert O.sample(logits, o, recent, r=float(r)) == _nucleus_literal(p, top_p, r), trial
+
+
+def test_fast_nucleus_equals_the_selection_sort():
+    """The sort-and-replay nucleus (the form a device port follows) against the literal quadratic
+    selection sort with its aliased writes, on rows full of exact ties (values from a few levels,
+    zeros included) and on continuous rows, for nuclei that stop early and that take the whole row."""
+    rng = np.random.default_rng(21)
+    for trial in range(300):
+        n = int(rng.integers(1, 1200))
+        if trial % 3 == 0:
+            p = rng.standard_normal(n).astype(np.float32) ** 2
+        else:
+            levels = rng.uniform(0, 1, size=int(rng.integers(1, 6))).astype(np.float32)
+            levels[0] = 0.0
+            p = rng.choice(levels, size=n).astype(np.float32)
+        s = float(p.astype(np.float64).sum())
+        top_p = float(rng.uniform(0.0, 1.3)) * max(s, 1e-6)
+        a = O.nucleus(p, top_p, fast=False)
+        b = O.nucleus(p, top_p, fast=True)
+        assert a[0] == b[0], trial
+        assert np.array_equal(a[1], b[1]), trial
+        assert np.array_equal(a[2], b[2]), trial
