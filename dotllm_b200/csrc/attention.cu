@@ -643,12 +643,8 @@ static int launch_cluster_t(const float *q, int ldq, const float *k, const float
                             int batch, float *out, int ldo, int appended, int C, int maxp, int slots, size_t smem,
                             bool pdl, cudaStream_t st)
 {
-    static bool attr_set = false;
-    if (!attr_set) {
-        LLMDOT_CUDA_TRY(
-            cudaFuncSetAttribute(attn_cluster_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_set = true;
-    }
+    static std::atomic<unsigned long long> attr_done{0};
+    LLMDOT_CUDA_TRY(smem_attr_once(attr_done, attn_cluster_kernel<T>, 200 * 1024));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(C, sh.heads_kv, batch);
     cfg.blockDim = dim3(AC_THREADS);
@@ -691,12 +687,9 @@ static int launch_attn_t(const float *q, int ldq, const float *k, const float *v
         LLMDOT_CUDA_TRY(launch_kernel(pdl, append_kv_kernel<T>, dim3(sh.heads_kv, batch), dim3(128), 0, st, k, v, ldkv,
                                       pos, cos_t, sin_t, views, layer, sh));
     const int appended = append_first ? 1 : 0;
-    static bool attr_set = false;
-    if (!attr_set) {
-        LLMDOT_CUDA_TRY(cudaFuncSetAttribute(attn_scores_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        LLMDOT_CUDA_TRY(cudaFuncSetAttribute(attn_pv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_set = true;
-    }
+    static std::atomic<unsigned long long> attr_s{0}, attr_p{0};
+    LLMDOT_CUDA_TRY(smem_attr_once(attr_s, attn_scores_kernel<T>, 200 * 1024));
+    LLMDOT_CUDA_TRY(smem_attr_once(attr_p, attn_pv_kernel<T>, 200 * 1024));
     LLMDOT_CUDA_TRY(launch_kernel(pdl, attn_scores_kernel<T>, grid, dim3(256), scores_smem(sh, sizeof(T)), st, q, ldq, k,
                                   v, ldkv, pos, cos_t, sin_t, views, layer, sh, scores, part_m, appended));
     LLMDOT_CUDA_TRY(launch_kernel(pdl, attn_pv_kernel<T>, grid, dim3(256), pv_smem(sh, sizeof(T)), st, pos, views, layer,

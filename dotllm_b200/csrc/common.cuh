@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "../../include/llmdot_cuda.h"
@@ -21,6 +22,21 @@ int cuda_fail(cudaError_t e, const char *what);
         cudaError_t _e = (expr);                                    \
         if (_e != cudaSuccess) return ::llmdot::cuda_fail(_e, #expr); \
     } while (0)
+
+// cudaFuncSetAttribute applies to the current device only: raise a kernel's dynamic shared-memory
+// limit once per device it is launched on (done: one bit per device, one variable per kernel).
+template <typename K>
+inline cudaError_t smem_attr_once(std::atomic<unsigned long long> &done, K kern, int bytes)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+    return e;
+}
 
 #define LLMDOT_TRY(expr)              \
     do {                              \

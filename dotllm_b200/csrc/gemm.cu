@@ -508,12 +508,8 @@ int gemm_prepare(const float *x, int ldx, int nv, int cols, const float *norm_w,
 
 template <int NB> static int launch_nb(const GemmArgs &a, int grid, cudaStream_t st)
 {
-    static bool attr = false;
-    if (!attr) {
-        LLMDOT_CUDA_TRY(cudaFuncSetAttribute(gemm_q_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)gemm_smem(NB)));
-        attr = true;
-    }
+    static std::atomic<unsigned long long> attr_done{0};
+    LLMDOT_CUDA_TRY(smem_attr_once(attr_done, gemm_q_kernel<NB>, (int)gemm_smem(NB)));
     gemm_q_kernel<NB><<<grid, GW * 32, gemm_smem(NB), st>>>(a);
     LLMDOT_CUDA_TRY(cudaGetLastError());
     return LLMDOT_OK;

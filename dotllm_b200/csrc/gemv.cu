@@ -772,11 +772,8 @@ template <int NV, int MODE, int RING, int TM, bool I8>
 static int launch_r(const GemvArgs &a, int grid, int max_rt, size_t sm, bool pdl, cudaStream_t st)
 {
     auto kern = gemv_mma_kernel<NV, MODE, RING, TM, I8>;
-    static bool attr_set = false;  // once per instantiation
-    if (!attr_set) {
-        LLMDOT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_MAX));
-        attr_set = true;
-    }
+    static std::atomic<unsigned long long> attr_done{0};  // per instantiation, per device
+    LLMDOT_CUDA_TRY(smem_attr_once(attr_done, kern, GEMV_SMEM_MAX));
     LLMDOT_CUDA_TRY(launch_kernel(pdl, kern, dim3(grid), dim3(GEMV_WARPS * 32), sm, st, a, max_rt));
     return LLMDOT_OK;
 }

@@ -368,11 +368,8 @@ int launch_sample(const SampleArgs &a, int rows, cudaStream_t st)
     const int k2 = k2_for(a.top_k > 0 ? a.top_k : 1);
     const size_t sm = sample_smem(a.n, a.window, a.top_k);
     if (sm > 200 * 1024) return fail(LLMDOT_E_UNSUPPORTED, "sample: vocabulary too large for the token bitmap");
-    static bool attr_set = false;
-    if (!attr_set) {
-        LLMDOT_CUDA_TRY(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_set = true;
-    }
+    static std::atomic<unsigned long long> attr_done{0};
+    LLMDOT_CUDA_TRY(smem_attr_once(attr_done, sample_kernel, 200 * 1024));
     sample_kernel<<<rows, SMP_THREADS, sm, st>>>(a, k2);
     LLMDOT_CUDA_TRY(cudaGetLastError());
     return LLMDOT_OK;
