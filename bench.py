@@ -373,6 +373,32 @@ def main():
         b32 = {"global_batch": 32, "sessions_per_gpu": per, "steps": k32, "value": per * world * k32 / (ms32 * 1e-3),
                "unit": "tok/s", "ms_per_step": ms32 / k32, "prefill_tok_s": per * world * n_prompt / pre32}
 
+    # Generate with Sampler.Sample on the device against greedy Generate, same prompt and length:
+    # the difference is the sampler and its per-token history upload (one GPU only)
+    sampled = None
+    if world == 1 and not args.tp:
+        try:
+            from dotllm_b200.native import LlmdotSampling
+            ss = m.session(max_ctx=ctx, kv=args.kv)
+            sp = synth.prompt_tokens(cfg, n_prompt, session=20_000)
+            ntok = min(args.steps, 256)
+            opts = LlmdotSampling(seed=42)  # the reference's defaults: top-k 40, T 0.8, penalty 1.1 over 64
+            ss.generate(sp, 4)
+            ss.generate_sampled(sp, 4, opts)
+            t0 = time.perf_counter()
+            ng = len(ss.generate(sp, ntok))
+            tg = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            ns = len(ss.generate_sampled(sp, ntok, opts))
+            ts = time.perf_counter() - t0
+            ss.close()
+            sampled = {"prompt": n_prompt, "tokens": ntok, "greedy_generate_s": tg, "sampled_generate_s": ts,
+                       "sampler_us_per_token": (ts - tg) / max(ntok, 1) * 1e6, "tokens_out": [ng, ns],
+                       "options": "top_k 40, top_p 0.95 (unused with top_k), temperature 0.8, repeat penalty 1.1 "
+                                  "over 64 tokens, seed 42; wall clock of the public calls, prefill included in both"}
+        except Exception as e:  # recorded, never allowed to drop the measurement line
+            sampled = {"error": str(e)[:300]}
+
     K = args.steps
     step_ms = dev_ms / K
     layer_b, head_b = m.weight_bytes()
@@ -415,6 +441,7 @@ def main():
         "prefill_tok_s": B * ranks_tokens * n_prompt / prefill_s,
         "load_s": load_s,
         "sharded_batch32": b32,
+        "sampled": sampled,
     }
     m.close()
     if dist:
