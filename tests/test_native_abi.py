@@ -123,3 +123,14 @@ def test_engine_rejects_token_and_draw_counts_the_library_would_overrun():
     s._h = None
     with pytest.raises(ValueError):
         s.generate_sampled([1, 2], 8, native.LlmdotSampling(), draws=np.full(7, 0.5, np.float32))
+
+
+def test_integration_bindings_name_declared_entry_points():
+    """Every [LibraryImport] EntryPoint written out in INTEGRATION.md is a function the header
+    declares (the C# binding a maintainer copies must not name a symbol that does not exist)."""
+    import os
+    import re
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    doc = open(os.path.join(root, "INTEGRATION.md")).read()
+    entry_points = set(re.findall(r'EntryPoint = "(\w+)"', doc))
+    assert entry_points and entry_points <= set(native.header_functions())
