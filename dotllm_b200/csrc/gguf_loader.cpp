@@ -55,6 +55,19 @@ struct Reader {
         p += len;
         return s;
     }
+    // a nested array's contents (ReadGgufArray reads them recursively; nothing on this path uses
+    // them), depth-limited so that a crafted file cannot exhaust the stack
+    void skip_array(int depth)
+    {
+        if (depth > 64) { err = true; return; }
+        const uint32_t t = (uint32_t)n(4);
+        const uint64_t cnt = n(8);
+        for (uint64_t j = 0; j < cnt && !err; j++) {
+            if (t == V_STR) str();
+            else if (t == V_ARR) skip_array(depth + 1);
+            else scalar(t);
+        }
+    }
     double scalar(uint32_t t)
     {
         switch (t) {
@@ -134,6 +147,7 @@ int gguf_open(const char *path, GgufModelFile *out)
             v.arr_n = r.n(8);
             for (uint64_t j = 0; j < v.arr_n && !r.err; j++) {
                 if (v.arr_type == V_STR) r.str();
+                else if (v.arr_type == V_ARR) r.skip_array(1);
                 else v.arr_num.push_back(r.scalar(v.arr_type));
             }
         } else v.num = r.scalar(v.type);

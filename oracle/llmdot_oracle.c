@@ -812,6 +812,20 @@ static char *rd_str(rd_t *r)
     r->p += len;
     return s;
 }
+static double rd_scalar(rd_t *r, uint32_t t);
+/* a nested array's contents: GgufReader.ReadGgufArray reads them recursively (GgufReader.cs:84-96);
+ * nothing on the path uses them.  Depth-limited. */
+static void rd_skip_array(rd_t *r, int depth)
+{
+    if (depth > 64) { r->err = 1; return; }
+    uint32_t t = (uint32_t)rd_n(r, 4);
+    uint64_t cnt = rd_n(r, 8);
+    for (uint64_t j = 0; j < cnt && !r->err; j++) {
+        if (t == V_STR) { uint64_t len = rd_n(r, 8); if (r->p + len > r->end) r->err = 1; else r->p += len; }
+        else if (t == V_ARR) rd_skip_array(r, depth + 1);
+        else rd_scalar(r, t);
+    }
+}
 static double rd_scalar(rd_t *r, uint32_t t)
 {
     switch (t) {
@@ -968,6 +982,8 @@ EXPORT omodel *orc_model_load(const char *path)
             v->arr_n = rd_n(&r, 8);
             if (v->arr_type == V_STR) {
                 for (uint64_t j = 0; j < v->arr_n && !r.err; j++) { uint64_t len = rd_n(&r, 8); if (r.p + len > r.end) r.err = 1; else r.p += len; }
+            } else if (v->arr_type == V_ARR) {
+                for (uint64_t j = 0; j < v->arr_n && !r.err; j++) rd_skip_array(&r, 1);
             } else {
                 v->arr_num = (double *)malloc(sizeof(double) * (v->arr_n ? v->arr_n : 1));
                 for (uint64_t j = 0; j < v->arr_n && !r.err; j++) v->arr_num[j] = rd_scalar(&r, v->arr_type);

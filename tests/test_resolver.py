@@ -30,6 +30,9 @@ def write_meta_gguf(path, entries, tensor_names=()):
     F32, offset 0 -- padding to 32 bytes and a 0f per tensor."""
     out = b"GGUF" + struct.pack("<IQQ", 3, len(tensor_names), len(entries))
     for key, t, v in entries:
+        if t == "raw":  # type tag and payload already encoded
+            out += _s(key) + v
+            continue
         out += _s(key) + struct.pack("<I", t)
         if t == U32:
             out += struct.pack("<I", v)
@@ -231,3 +234,22 @@ def test_smollm2_rope_parameters(tmp_path):  # :163-186
     e = _smol(576, 30, 1536, 9, 3, rope=True) + [("llama.rope.dimension_count", U32, 64)]
     c = both(write_meta_gguf(tmp_path / "a.gguf", e))
     assert c["rope_base"] == 10000.0 and c["rope_dim"] == 64
+
+
+ARR = 9
+
+
+def _nested(depth_payloads):
+    """ARR of ARR of U32, and ARR of ARR of STR (GgufReader.ReadGgufArray recurses)."""
+    inner_u32 = struct.pack("<IQ", U32, 2) + struct.pack("<II", 7, 8)
+    inner_str = struct.pack("<IQ", STR, 1) + _s("x")
+    return [("x.nested_u32", "raw", struct.pack("<IIQ", ARR, ARR, 2) + inner_u32 + inner_u32),
+            ("x.nested_str", "raw", struct.pack("<IIQ", ARR, ARR, 1) + inner_str)]
+
+
+def test_nested_metadata_arrays_are_read_past(tmp_path):
+    """A file whose metadata holds arrays of arrays resolves like one without them: both parsers
+    read past the nested values, as GgufReader does (GgufReader.cs:84-96)."""
+    plain = both(write_meta_gguf(tmp_path / "a.gguf", LLAMA))
+    nested = both(write_meta_gguf(tmp_path / "b.gguf", _nested(2) + LLAMA))
+    assert plain == nested
