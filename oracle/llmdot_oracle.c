@@ -888,9 +888,10 @@ typedef struct {
     uint8_t *layer_attn;  /* LayerTypes: 1 Attention, 0 Conv */
 } omodel;
 
+/* the last entry of a key wins, as GgufReader's `values[key] = ...` (GgufReader.cs:44-53) */
 static okv *find_kv(omodel *m, const char *key)
 {
-    for (int i = 0; i < m->nkv; i++) if (strcmp(m->kv[i].key, key) == 0) return &m->kv[i];
+    for (int i = m->nkv - 1; i >= 0; i--) if (m->kv[i].key && strcmp(m->kv[i].key, key) == 0) return &m->kv[i];
     return NULL;
 }
 static okv *find_arch_kv(omodel *m, const char *key)

@@ -253,3 +253,9 @@ def test_nested_metadata_arrays_are_read_past(tmp_path):
     plain = both(write_meta_gguf(tmp_path / "a.gguf", LLAMA))
     nested = both(write_meta_gguf(tmp_path / "b.gguf", _nested(2) + LLAMA))
     assert plain == nested
+
+
+def test_duplicate_metadata_key_last_wins(tmp_path):
+    """GgufReader stores `values[key] = ...`, so a repeated key keeps its last value."""
+    e = LLAMA + [("llama.block_count", U32, 7)]
+    assert both(write_meta_gguf(tmp_path / "a.gguf", e))["layers"] == 7
