@@ -32,10 +32,12 @@ template <typename T> static int dalloc(std::vector<void *> &a, T **p, size_t n)
     return dmalloc(a, (void **)p, n * sizeof(T));
 }
 
+// LoadedModel.LoadTensors keys tensors OrdinalIgnoreCase and a later tensor of the same name
+// replaces an earlier one (LoadedModel.cs:77-107): the last match wins
 static const llmdot_tensor_desc *find_desc(const llmdot_tensor_desc *t, int n, const std::string &name)
 {
-    for (int i = 0; i < n; i++)
-        if (t[i].name && strcasecmp(t[i].name, name.c_str()) == 0) return &t[i];  // OrdinalIgnoreCase
+    for (int i = n - 1; i >= 0; i--)
+        if (t[i].name && strcasecmp(t[i].name, name.c_str()) == 0) return &t[i];
     return nullptr;
 }
 

@@ -916,9 +916,11 @@ static float get_float(omodel *m, const char *key, float def, int *present)
 }
 
 /* case-insensitive tensor lookup (TensorNameResolver uses OrdinalIgnoreCase) */
+/* LoadedModel.LoadTensors (LoadedModel.cs:77-107): tensors with data, keyed OrdinalIgnoreCase, a
+ * later one replacing an earlier one of the same name -- the last loaded match wins */
 static otensor *find_t(omodel *m, const char *name)
 {
-    for (int i = 0; i < m->nt; i++) if (strcasecmp(m->t[i].name, name) == 0) return m->t[i].data ? &m->t[i] : NULL;
+    for (int i = m->nt - 1; i >= 0; i--) if (m->t[i].data && strcasecmp(m->t[i].name, name) == 0) return &m->t[i];
     return NULL;
 }
 static otensor *find_tf(omodel *m, const char *fmt, int layer)
@@ -1012,7 +1014,8 @@ EXPORT omodel *orc_model_load(const char *path)
     for (int i = 0; i < m->nt; i++) {
         otensor *t = &m->t[i];
         t->nbytes = orc_byte_count(t->type, t->nelem);
-        if (t->nbytes == 0 && t->nelem != 0 && t->type != T_F32) { snprintf(g_err, sizeof g_err, "Unsupported GGML type: %u", t->type); orc_model_free(m); return NULL; }
+        /* TensorSize.ByteCount throws for a type it does not know, whatever the element count */
+        if (orc_byte_count(t->type, 256) == 0) { snprintf(g_err, sizeof g_err, "Unsupported GGML type: %u", t->type); orc_model_free(m); return NULL; }
         if (t->nbytes == 0 || dataOff + t->offset + t->nbytes > (uint64_t)sz) { t->data = NULL; continue; }
         t->data = m->file + dataOff + t->offset;
     }

@@ -259,3 +259,46 @@ def test_duplicate_metadata_key_last_wins(tmp_path):
     """GgufReader stores `values[key] = ...`, so a repeated key keeps its last value."""
     e = LLAMA + [("llama.block_count", U32, 7)]
     assert both(write_meta_gguf(tmp_path / "a.gguf", e))["layers"] == 7
+
+
+def test_unsupported_tensor_type_refused_even_when_empty(tmp_path):
+    """TensorSize.ByteCount throws for a type it does not know (TensorSize.cs:7-24), before any
+    element count matters: a zero-element IQ2_XXS tensor still fails the load."""
+    out = bytearray(open(write_meta_gguf(tmp_path / "a.gguf", LLAMA), "rb").read())
+    struct.pack_into("<Q", out, 8, 1)  # one tensor
+    out += _s("blk.0.odd.weight") + struct.pack("<IIQ", 0, 16, 0)  # 0 dims, type 16, offset 0
+    p = tmp_path / "b.gguf"
+    p.write_bytes(bytes(out))
+    with pytest.raises(CudaBackendError, match="Unsupported GGML type"):
+        gguf_config(str(p))
+    with pytest.raises(ValueError, match="Unsupported GGML type"):
+        O.Model(str(p))
+
+
+def test_duplicate_tensor_name_last_loaded_wins(tmp_path):
+    """LoadedModel.LoadTensors stores `tensors[info.Name] = ...` (case-insensitive keys), so a
+    repeated tensor name resolves to the last one: the oracle's logits with an output_norm repeated
+    (different values, other case) equal those of the model whose only output_norm has the new values."""
+    import numpy as np
+
+    from dotllm_b200 import gguf, synth
+    cfg = synth.get("micro")
+    plan = synth.tensor_plan(cfg)
+    data = {t.name: synth.tensor_bytes(cfg, t, r, i) for i, (t, r) in enumerate(plan)}
+    md = synth.metadata_for(cfg)
+    new_norm = (1.0 + 0.2 * np.random.default_rng(5).standard_normal(cfg.hidden)).astype("<f4").tobytes()
+    single = str(tmp_path / "single.gguf")
+    gguf.write_gguf(single, md, [t for t, _ in plan],
+                    lambda t: new_norm if t.name == "output_norm.weight" else data[t.name])
+    dup_infos = [t for t, _ in plan] + [gguf.TensorInfo("OUTPUT_NORM.weight", [cfg.hidden], gguf.GGML_F32)]
+    dup = str(tmp_path / "dup.gguf")
+    gguf.write_gguf(dup, synth.metadata_for(cfg), dup_infos,
+                    lambda t: new_norm if t.name == "OUTPUT_NORM.weight" else data[t.name])
+    outs = []
+    for p in (single, dup):
+        m = O.Model(p)
+        s = O.Session(m)
+        outs.append(s.process_token(3, 0))
+        s.close()
+        m.close()
+    assert np.array_equal(outs[0], outs[1])
