@@ -206,3 +206,19 @@ class CudaBackend:
         check(lib().llmdot_cuda_sample(self._h, _f(x), x.size, C.byref(o), rec.ctypes.data_as(I32P), rec.size,
                                        float(r), C.byref(out)))
         return out.value
+
+
+class Sampler:
+    """Sampler (src/Llmdot.Core/Sampling/Sampler.cs:11-165) over a CudaBackend: ``sample(logits,
+    options, recent_tokens)`` with the reference's draw -- ``new Random(seed).NextSingle()`` when
+    seed >= 0 (the same draw for every call, as the reference re-seeds per call), a fresh uniform
+    draw otherwise.  Option sets the device refuses (the top-p-only branch) raise CudaBackendError."""
+
+    def __init__(self, backend: "CudaBackend"):
+        import random
+        self._backend = backend
+        self._rng = random.Random()
+
+    def sample(self, logits, options, recent_tokens=()) -> int:
+        r = None if options.seed >= 0 else self._rng.random()
+        return self._backend.sample(logits, options, recent_tokens, r)

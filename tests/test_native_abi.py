@@ -134,3 +134,21 @@ def test_integration_bindings_name_declared_entry_points():
     doc = open(os.path.join(root, "INTEGRATION.md")).read()
     entry_points = set(re.findall(r'EntryPoint = "(\w+)"', doc))
     assert entry_points and entry_points <= set(native.header_functions())
+
+
+def test_sampler_mirror_draws_like_the_reference():
+    """backend.Sampler passes no draw for a seed >= 0 (the backend then uses the seeded draw) and a
+    fresh uniform draw in [0, 1) otherwise."""
+    from dotllm_b200.backend import Sampler
+    calls = []
+
+    class FakeBackend:
+        def sample(self, logits, options, recent, r):
+            calls.append(r)
+            return 7
+    s = Sampler(FakeBackend())
+    assert s.sample([0.0, 1.0], native.LlmdotSampling(seed=42), [1]) == 7
+    s.sample([0.0, 1.0], native.LlmdotSampling(seed=-1), [])
+    s.sample([0.0, 1.0], native.LlmdotSampling(seed=-1), [])
+    assert calls[0] is None
+    assert all(0.0 <= r < 1.0 for r in calls[1:]) and calls[1] != calls[2]
