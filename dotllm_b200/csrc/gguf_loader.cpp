@@ -177,7 +177,11 @@ int gguf_open(const char *path, GgufModelFile *out)
     for (auto &t : out->tensors) {
         if (block_elems(t.type) == 0) return bad("Unsupported GGML type: " + std::to_string(t.type));
         t.n_bytes = row_bytes(t.type, t.n_elems);
-        if (t.n_bytes == 0 || data_off + t.offset + t.n_bytes > out->size) continue;
+        // overflow-safe form of data_off + offset + n_bytes > file size: a crafted offset must not
+        // wrap around and point the tensor outside the mapping
+        const uint64_t size = out->size;
+        if (t.n_bytes == 0 || data_off > size || t.offset > size - data_off || t.n_bytes > size - data_off - t.offset)
+            continue;
         t.data = base + data_off + t.offset;
     }
 

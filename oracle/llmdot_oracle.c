@@ -785,6 +785,7 @@ typedef struct {
 
 typedef struct {
     char *name;
+    uint64_t name_len;  /* bytes read: a name may hold a NUL that C string functions stop at */
     uint32_t type, ndims;
     uint64_t dims[4];
     uint64_t nelem, offset;
@@ -802,16 +803,18 @@ static uint64_t rd_n(rd_t *r, int n)
     r->p += n;
     return v;
 }
-static char *rd_str(rd_t *r)
+static char *rd_str_len(rd_t *r, uint64_t *out_len)
 {
     uint64_t len = rd_n(r, 8);
-    if (r->err || r->p + len > r->end) { r->err = 1; return NULL; }
+    if (out_len) *out_len = len;
+    if (r->err || len > (uint64_t)(r->end - r->p)) { r->err = 1; return NULL; }
     char *s = (char *)malloc(len + 1);
     memcpy(s, r->p, len);
     s[len] = 0;
     r->p += len;
     return s;
 }
+static char *rd_str(rd_t *r) { return rd_str_len(r, NULL); }
 static double rd_scalar(rd_t *r, uint32_t t);
 /* a nested array's contents: GgufReader.ReadGgufArray reads them recursively (GgufReader.cs:84-96);
  * nothing on the path uses them.  Depth-limited. */
@@ -821,7 +824,7 @@ static void rd_skip_array(rd_t *r, int depth)
     uint32_t t = (uint32_t)rd_n(r, 4);
     uint64_t cnt = rd_n(r, 8);
     for (uint64_t j = 0; j < cnt && !r->err; j++) {
-        if (t == V_STR) { uint64_t len = rd_n(r, 8); if (r->p + len > r->end) r->err = 1; else r->p += len; }
+        if (t == V_STR) { uint64_t len = rd_n(r, 8); if (len > (uint64_t)(r->end - r->p)) r->err = 1; else r->p += len; }
         else if (t == V_ARR) rd_skip_array(r, depth + 1);
         else rd_scalar(r, t);
     }
@@ -937,9 +940,11 @@ static int has_name(omodel *m, const char *fmt, int layer)
     for (int i = 0; i < m->nt; i++) if (strcasecmp(m->t[i].name, buf) == 0) return 1;
     return 0;
 }
+/* TensorInfos.Any(t => t.Name.Contains(sub)): over the whole name, NUL bytes included */
 static int any_name_contains(omodel *m, const char *sub)
 {
-    for (int i = 0; i < m->nt; i++) if (strstr(m->t[i].name, sub)) return 1;
+    for (int i = 0; i < m->nt; i++)
+        if (m->t[i].name && memmem(m->t[i].name, (size_t)m->t[i].name_len, sub, strlen(sub))) return 1;
     return 0;
 }
 
@@ -974,6 +979,10 @@ EXPORT omodel *orc_model_load(const char *path)
     uint32_t version = (uint32_t)rd_n(&r, 4);
     if (version < 2) { snprintf(g_err, sizeof g_err, "Unsupported GGUF version: %u", version); orc_model_free(m); return NULL; }
     uint64_t nt = rd_n(&r, 8), nkv = rd_n(&r, 8);
+    /* a count the file cannot hold (a key-value pair takes at least 12 bytes, a tensor info 24)
+     * is a truncated header, not an allocation to attempt */
+    const uint64_t left = (uint64_t)(r.end - r.p);
+    if (r.err || nkv > left / 12 || nt > left / 24) { snprintf(g_err, sizeof g_err, "truncated GGUF header"); orc_model_free(m); return NULL; }
     m->kv = (okv *)calloc(nkv ? nkv : 1, sizeof(okv));
     for (uint64_t i = 0; i < nkv && !r.err; i++) {
         okv *v = &m->kv[m->nkv++];
@@ -984,11 +993,13 @@ EXPORT omodel *orc_model_load(const char *path)
             v->arr_type = (uint32_t)rd_n(&r, 4);
             v->arr_n = rd_n(&r, 8);
             if (v->arr_type == V_STR) {
-                for (uint64_t j = 0; j < v->arr_n && !r.err; j++) { uint64_t len = rd_n(&r, 8); if (r.p + len > r.end) r.err = 1; else r.p += len; }
+                for (uint64_t j = 0; j < v->arr_n && !r.err; j++) { uint64_t len = rd_n(&r, 8); if (len > (uint64_t)(r.end - r.p)) r.err = 1; else r.p += len; }
             } else if (v->arr_type == V_ARR) {
                 for (uint64_t j = 0; j < v->arr_n && !r.err; j++) rd_skip_array(&r, 1);
             } else {
+                if (v->arr_n > (uint64_t)(r.end - r.p)) { r.err = 1; break; }  /* >= 1 byte per element */
                 v->arr_num = (double *)malloc(sizeof(double) * (v->arr_n ? v->arr_n : 1));
+                if (!v->arr_num) { r.err = 1; break; }
                 for (uint64_t j = 0; j < v->arr_n && !r.err; j++) v->arr_num[j] = rd_scalar(&r, v->arr_type);
             }
         } else v->num = rd_scalar(&r, v->type);
@@ -996,7 +1007,7 @@ EXPORT omodel *orc_model_load(const char *path)
     m->t = (otensor *)calloc(nt ? nt : 1, sizeof(otensor));
     for (uint64_t i = 0; i < nt && !r.err; i++) {
         otensor *t = &m->t[m->nt++];
-        t->name = rd_str(&r);
+        t->name = rd_str_len(&r, &t->name_len);
         t->ndims = (uint32_t)rd_n(&r, 4);
         if (t->ndims > 4) { r.err = 1; break; }
         uint32_t ne = 1; /* the reference multiplies the uint dims in 32-bit arithmetic */
@@ -1016,7 +1027,9 @@ EXPORT omodel *orc_model_load(const char *path)
         t->nbytes = orc_byte_count(t->type, t->nelem);
         /* TensorSize.ByteCount throws for a type it does not know, whatever the element count */
         if (orc_byte_count(t->type, 256) == 0) { snprintf(g_err, sizeof g_err, "Unsupported GGML type: %u", t->type); orc_model_free(m); return NULL; }
-        if (t->nbytes == 0 || dataOff + t->offset + t->nbytes > (uint64_t)sz) { t->data = NULL; continue; }
+        /* overflow-safe form of dataOff + offset + nbytes > file size */
+        if (t->nbytes == 0 || dataOff > (uint64_t)sz || t->offset > (uint64_t)sz - dataOff ||
+            t->nbytes > (uint64_t)sz - dataOff - t->offset) { t->data = NULL; continue; }
         t->data = m->file + dataOff + t->offset;
     }
 
@@ -1091,6 +1104,7 @@ EXPORT omodel *orc_model_load(const char *path)
     /* HasConvLayers / ConvKernelSize / LayerTypes (:66-70); ResolveLayerTypes :226-238: a layer
      * is Attention when blk.N.attn_q, attn_k or attn_qkv is among the tensor infos */
     m->layer_attn = (uint8_t *)malloc(c->layers > 0 ? (size_t)c->layers : 1);
+    if (!m->layer_attn) { snprintf(g_err, sizeof g_err, "out of memory (%d layers)", c->layers); orc_model_free(m); return NULL; }
     m->conv_kernel = 0;
     for (int l = 0; l < c->layers; l++) m->layer_attn[l] = 1;
     if (c->template_id == TPL_LFM2) {
@@ -1108,7 +1122,8 @@ EXPORT omodel *orc_model_load(const char *path)
     /* PrecomputeRopeFrequencies -- InferenceEngine.cs:57-72 */
     int rd = c->rope_dim > 0 ? c->rope_dim : c->head_dim;
     m->rope_half = rd / 2;
-    m->rope_freq = (float *)malloc(sizeof(float) * (m->rope_half ? m->rope_half : 1));
+    m->rope_freq = m->rope_half >= 0 ? (float *)malloc(sizeof(float) * (m->rope_half ? (size_t)m->rope_half : 1)) : NULL;
+    if (!m->rope_freq) { snprintf(g_err, sizeof g_err, "bad rope dimension %d", rd); orc_model_free(m); return NULL; }
     for (int i = 0; i < m->rope_half; i++) {
         float freq = 1.0f / powf(c->rope_base, 2.0f * (float)i / (float)rd);
         if (c->rope_scaling == ROPE_LINEAR && c->rope_factor > 1.0f) freq /= c->rope_factor;

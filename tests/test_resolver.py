@@ -302,3 +302,47 @@ def test_duplicate_tensor_name_last_loaded_wins(tmp_path):
         s.close()
         m.close()
     assert np.array_equal(outs[0], outs[1])
+
+
+def test_parsers_agree_on_mutated_files(tmp_path):
+    """Seeded byte flips, truncations and insertions of valid files: the library's GGUF parser
+    (which runs inside the caller's process) and the oracle's must neither crash nor disagree --
+    both refuse the file, or both resolve it to the same configuration."""
+    import random
+    rng = random.Random(1)
+    bases = [open(write_meta_gguf(tmp_path / f"b{i}.gguf", e, names), "rb").read() for i, (e, names) in enumerate(
+        [(LLAMA, ["token_embd.weight", "blk.0.ffn_gate.weight"]), (GEMMA, []), (PHI2, ["output.weight"])])]
+    p = str(tmp_path / "f.gguf")
+    resolved = 0
+    for it in range(1500):
+        b = bytearray(rng.choice(bases))
+        for _ in range(rng.randint(1, 4)):
+            op = rng.random()
+            if op < 0.5:
+                i = rng.randrange(len(b))
+                b[i] = rng.randrange(256)
+            elif op < 0.75:
+                b = b[:rng.randrange(len(b))]
+            else:
+                i = rng.randrange(len(b))
+                b[i:i] = bytes(rng.randrange(256) for _ in range(rng.randint(1, 8)))
+            if not b:
+                b = bytearray(b"G")
+        with open(p, "wb") as f:
+            f.write(bytes(b))
+        try:
+            c = gguf_config(p)
+        except CudaBackendError:
+            c = None
+        try:
+            m = O.Model(p)
+            o = m.config
+            m.close()
+        except ValueError:
+            o = None
+        assert (c is None) == (o is None), it
+        if c is not None:
+            resolved += 1
+            for k, v in o.items():
+                assert c[k] == v or (c[k] != c[k] and v != v), (it, k)
+    assert resolved > 50  # the mutations leave enough files valid to compare configurations
