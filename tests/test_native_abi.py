@@ -51,8 +51,12 @@ def test_no_cpu_fallback_without_device():
 def test_seeded_draw_matches_oracle():
     """llmdot_cuda_sampling_seeded_draw (host only) is the oracle's new Random(seed).NextSingle()."""
     from oracle import oracle as O
-    for seed in (0, 1, 7, 42, 99, 12345, -5, 2147483647):
-        assert native.lib().llmdot_cuda_sampling_seeded_draw(seed) == O.net_random_single(seed)
+    # int.MinValue has its own case in the seeding (its absolute value does not fit an int)
+    seeds = [0, 1, 7, 42, 99, 12345, -5, 2147483647, -2147483648]
+    seeds += [int(x) for x in np.random.default_rng(3).integers(-2**31, 2**31, size=500)]
+    for seed in seeds:
+        d = native.lib().llmdot_cuda_sampling_seeded_draw(seed)
+        assert d == O.net_random_single(seed) and 0.0 <= d < 1.0, seed
 
 
 def test_header_is_plain_c99(tmp_path):
