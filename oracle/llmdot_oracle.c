@@ -887,6 +887,7 @@ typedef struct {
     int rope_half;
     char arch[64];
     int conv_kernel;      /* ConvKernelSize (0 unless HasConvLayers) */
+    int bad_rope;         /* a negative rotary dimension, refused when a session is created */
     int expert_used;      /* ExpertUsedCount */
     uint8_t *layer_attn;  /* LayerTypes: 1 Attention, 0 Conv */
 } omodel;
@@ -1121,9 +1122,12 @@ EXPORT omodel *orc_model_load(const char *path)
     }
     /* PrecomputeRopeFrequencies -- InferenceEngine.cs:57-72 */
     int rd = c->rope_dim > 0 ? c->rope_dim : c->head_dim;
-    m->rope_half = rd / 2;
-    m->rope_freq = m->rope_half >= 0 ? (float *)malloc(sizeof(float) * (m->rope_half ? (size_t)m->rope_half : 1)) : NULL;
-    if (!m->rope_freq) { snprintf(g_err, sizeof g_err, "bad rope dimension %d", rd); orc_model_free(m); return NULL; }
+    /* the reference builds this table in the InferenceEngine constructor, not at load: a rope
+     * dimension it cannot size fails the session (orc_session_new), as `new float[halfDim]` would */
+    m->rope_half = rd / 2 > 0 ? rd / 2 : 0;
+    m->bad_rope = rd / 2 < 0 ? rd : 0;
+    m->rope_freq = (float *)malloc(sizeof(float) * (m->rope_half ? (size_t)m->rope_half : 1));
+    if (!m->rope_freq) { snprintf(g_err, sizeof g_err, "out of memory (rope dimension %d)", rd); orc_model_free(m); return NULL; }
     for (int i = 0; i < m->rope_half; i++) {
         float freq = 1.0f / powf(c->rope_base, 2.0f * (float)i / (float)rd);
         if (c->rope_scaling == ROPE_LINEAR && c->rope_factor > 1.0f) freq /= c->rope_factor;
@@ -1281,6 +1285,7 @@ EXPORT void orc_session_free(osess *s)
 EXPORT osess *orc_session_new(omodel *m)
 {
     orc_config *c = &m->cfg;
+    if (m->bad_rope) { snprintf(g_err, sizeof g_err, "bad rope dimension %d", m->bad_rope); return NULL; }
     osess *s = (osess *)calloc(1, sizeof(osess));
     s->m = m;
     size_t kvDim = (size_t)c->heads_kv * c->head_dim, qDim = (size_t)c->heads * c->head_dim;

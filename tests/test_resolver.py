@@ -305,16 +305,20 @@ def test_duplicate_tensor_name_last_loaded_wins(tmp_path):
 
 
 def test_parsers_agree_on_mutated_files(tmp_path):
-    """Seeded byte flips, truncations and insertions of valid files: the library's GGUF parser
+    """Seeded byte flips, truncations and insertions of valid files (metadata-only and a real model's head): the library's GGUF parser
     (which runs inside the caller's process) and the oracle's must neither crash nor disagree --
     both refuse the file, or both resolve it to the same configuration."""
     import random
     rng = random.Random(1)
+    from dotllm_b200 import synth
     bases = [open(write_meta_gguf(tmp_path / f"b{i}.gguf", e, names), "rb").read() for i, (e, names) in enumerate(
-        [(LLAMA, ["token_embd.weight", "blk.0.ffn_gate.weight"]), (GEMMA, []), (PHI2, ["output.weight"])])]
+        [(LLAMA, ["token_embd.weight", "blk.0.ffn_gate.weight"]), (GEMMA, []), (PHI2, ["output.weight"]),
+         (LFM2, ["blk.1.attn_q.weight", "blk.0.shortconv.conv.weight"])])]
+    # and the head of a real synthetic model: its tensor infos and the start of its data
+    bases.append(open(synth.build_model(synth.get("micro-lfm2")), "rb").read()[:200000])
     p = str(tmp_path / "f.gguf")
     resolved = 0
-    for it in range(1500):
+    for it in range(2500):
         b = bytearray(rng.choice(bases))
         for _ in range(rng.randint(1, 4)):
             op = rng.random()
