@@ -843,10 +843,7 @@ static int check_err_flag(llmdot_model *m)
     if (e) {
         cudaMemset(m->ws.err, 0, sizeof(int));
         if (e == 1) return fail(LLMDOT_E_INVALID, "token id outside the vocabulary");
-        // a bounded wait of the persistent step kernel gave up: re-arm its state
-        step_kernel_reset(m, m->stream);
-        cudaStreamSynchronize(m->stream);
-        return fail(LLMDOT_E_TIMEOUT, e == 2 ? "step kernel: grid barrier timed out" : "step kernel: weight tile wait timed out");
+        return fail(LLMDOT_E_CUDA, "device error flag " + std::to_string(e));
     }
     return LLMDOT_OK;
 }
@@ -889,7 +886,7 @@ static int prefill_rows(llmdot_session *s, const int32_t *tokens, int n, float *
     cudaMemcpyAsync(dtok, hp.data(), sizeof(int32_t) * 2 * n, cudaMemcpyHostToDevice, st);
     int rc = LLMDOT_OK;
     int last_row = 0;  // row of the workspace that holds the last prompt token's logits
-    if (m->use_fast_gemv && !m->step_decode) {
+    if (m->use_fast_gemv) {
         // prompt chunks of up to GEMM_MAX_ROWS consecutive positions, one batched step each
         const int CH = n < GEMM_MAX_ROWS ? n : GEMM_MAX_ROWS;
         rc = ensure_workspace(m, CH);
@@ -905,11 +902,6 @@ static int prefill_rows(llmdot_session *s, const int32_t *tokens, int n, float *
                 last_row = T - 1;
             }
         }
-    } else if (step_kernel_supported(m, 1)) {
-        // all prompt tokens in one persistent launch; logits of the last one only
-        cudaMemcpyAsync(w.views, &s->view, sizeof(KvView), cudaMemcpyHostToDevice, st);
-        cudaMemcpyAsync(w.pos, dpos, sizeof(int32_t), cudaMemcpyDeviceToDevice, st);
-        rc = launch_step_kernel(m, 1, s->kv_type, n, dtok, st);
     } else {
         cudaMemcpyAsync(w.views, &s->view, sizeof(KvView), cudaMemcpyHostToDevice, st);
         for (int i = 0; i < n && rc == LLMDOT_OK; i++)
@@ -958,14 +950,12 @@ extern "C" int llmdot_cuda_decode(llmdot_session **sessions, int batch, const in
         x.h_pinned[x.cap + i] = sessions[i]->pos;
         x.h_views[i] = sessions[i]->view;
     }
-    const bool persistent = m->step_decode && step_kernel_supported(m, batch);
     cudaGraphExec_t g = nullptr;
-    if (!persistent) LLMDOT_TRY(step_graph(m, batch, kv_type, &g));
+    LLMDOT_TRY(step_graph(m, batch, kv_type, &g));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.next, x.h_pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.views, x.h_views, sizeof(KvView) * batch, cudaMemcpyHostToDevice, st));
-    if (persistent) LLMDOT_TRY(launch_step_kernel(m, batch, kv_type, 1, nullptr, st));
-    else LLMDOT_CUDA_TRY(cudaGraphLaunch(g, st));
+    LLMDOT_CUDA_TRY(cudaGraphLaunch(g, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(x.h_pinned + 2 * x.cap, w.next, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost, st));
     if (logits) LLMDOT_TRY(read_logits(m, batch, -1, logits, st));
     LLMDOT_CUDA_TRY(cudaStreamSynchronize(st));
@@ -999,9 +989,8 @@ extern "C" int llmdot_cuda_generate(llmdot_session *s, const int32_t *prompt, in
     ModelExtra &x = extra(m);
     Workspace &w = m->ws;
     cudaStream_t st = m->stream;
-    const bool persistent = m->step_decode && step_kernel_supported(m, 1);
     cudaGraphExec_t g = nullptr;
-    if (!persistent) LLMDOT_TRY(step_graph(m, 1, s->kv_type, &g));
+    LLMDOT_TRY(step_graph(m, 1, s->kv_type, &g));
     // device state: w.next holds the token to feed, w.pos its position
     x.h_pinned[x.cap] = s->pos;
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t), cudaMemcpyHostToDevice, st));
@@ -1011,8 +1000,7 @@ extern "C" int llmdot_cuda_generate(llmdot_session *s, const int32_t *prompt, in
         out_tokens[produced++] = next;
         if (next == m->cfg.eos || produced == max_tokens) break;
         if (s->pos >= s->max_ctx) return fail(LLMDOT_E_INVALID, "generate: context length exceeded");
-        if (persistent) LLMDOT_TRY(launch_step_kernel(m, 1, s->kv_type, 1, nullptr, st));
-        else LLMDOT_CUDA_TRY(cudaGraphLaunch(g, st));
+        LLMDOT_CUDA_TRY(cudaGraphLaunch(g, st));
         LLMDOT_CUDA_TRY(cudaMemcpyAsync(x.h_pinned + 2 * x.cap, w.next, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
         LLMDOT_CUDA_TRY(cudaStreamSynchronize(st));
         next = x.h_pinned[2 * x.cap];
@@ -1155,13 +1143,8 @@ extern "C" int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
         x.h_pinned[x.cap + i] = sessions[i]->pos;
         x.h_views[i] = sessions[i]->view;
     }
-    const bool persistent = m->step_decode && step_kernel_supported(m, batch);
     cudaGraphExec_t g = nullptr;
-    if (persistent) {
-        if (kernels_per_step) *kernels_per_step = 1;  // at most: one launch runs a whole chunk of steps
-    } else {
-        LLMDOT_TRY(step_graph(m, batch, kv_type, &g, kernels_per_step));
-    }
+    LLMDOT_TRY(step_graph(m, batch, kv_type, &g, kernels_per_step));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.next, x.h_pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
     LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.views, x.h_views, sizeof(KvView) * batch, cudaMemcpyHostToDevice, st));
@@ -1178,15 +1161,11 @@ extern "C" int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
         int chunk = n_steps - done < HIST_STEPS ? n_steps - done : HIST_STEPS;
         cudaMemsetAsync(w.hist_step, 0, sizeof(int32_t), st);
         cudaEventRecord(e0, st);
-        if (persistent) {
-            rc = launch_step_kernel(m, batch, kv_type, chunk, nullptr, st);
-        } else {
-            for (int i = 0; i < chunk; i++)
-                if (cudaGraphLaunch(g, st) != cudaSuccess) {
-                    rc = cuda_fail(cudaGetLastError(), "cudaGraphLaunch");
-                    break;
-                }
-        }
+        for (int i = 0; i < chunk; i++)
+            if (cudaGraphLaunch(g, st) != cudaSuccess) {
+                rc = cuda_fail(cudaGetLastError(), "cudaGraphLaunch");
+                break;
+            }
         cudaEventRecord(e1, st);
         if (rc == LLMDOT_OK &&
             cudaMemcpyAsync(out_tokens + (size_t)done * batch, w.hist, sizeof(int32_t) * (size_t)chunk * batch,
@@ -1207,28 +1186,25 @@ extern "C" int llmdot_cuda_decode_steps(llmdot_session **sessions, int batch, co
     return LLMDOT_OK;
 }
 
-extern "C" int llmdot_cuda_trace_step(llmdot_session **sessions, int batch, const int32_t *tokens, uint64_t *events,
-                                      int *kinds, int *n_phases, int *n_cta)
+extern "C" int llmdot_cuda_profile_step(llmdot_session **sessions, int batch, const int32_t *tokens,
+                                        int32_t *next_tokens, int n_families, float *family_ms, int *family_launches)
 {
-    if (!sessions || batch <= 0 || !tokens || !n_phases || !n_cta) return fail(LLMDOT_E_INVALID, "trace_step: bad arguments");
+    if (!sessions || batch <= 0 || !tokens || n_families < 0 || (n_families > 0 && (!family_ms || !family_launches)))
+        return fail(LLMDOT_E_INVALID, "profile_step: bad arguments");
     llmdot_model *m = sessions[0] ? sessions[0]->m : nullptr;
-    if (!m) return fail(LLMDOT_E_INVALID, "trace_step: null session, or its model was freed");
+    if (!m) return fail(LLMDOT_E_INVALID, "profile_step: null session, or its model was freed");
     const int kv_type = sessions[0]->kv_type;
     for (int i = 0; i < batch; i++) {
         llmdot_session *s = sessions[i];
         if (!s || s->m != m || s->kv_type != kv_type)
-            return fail(LLMDOT_E_INVALID, "trace_step: sessions must share one model and KV type");
-        if (s->pos >= s->max_ctx) return fail(LLMDOT_E_INVALID, "trace_step: context length exceeded");
-        if (tokens[i] < 0 || tokens[i] >= m->cfg.vocab) return fail(LLMDOT_E_INVALID, "trace_step: token id outside the vocabulary");
+            return fail(LLMDOT_E_INVALID, "profile_step: sessions must share one model and KV type");
+        if (s->pos >= s->max_ctx) return fail(LLMDOT_E_INVALID, "profile_step: context length exceeded");
+        if (tokens[i] < 0 || tokens[i] >= m->cfg.vocab) return fail(LLMDOT_E_INVALID, "profile_step: token id outside the vocabulary");
+        for (int j = 0; j < i; j++)
+            if (sessions[j] == s) return fail(LLMDOT_E_INVALID, "profile_step: a session appears twice in the batch");
     }
     LLMDOT_CUDA_TRY(cudaSetDevice(m->device));
     LLMDOT_TRY(ensure_workspace(m, batch));
-    if (!step_kernel_supported(m, batch)) return fail(LLMDOT_E_UNSUPPORTED, "trace_step: no persistent step kernel");
-    std::vector<int> kind_buf(4096);
-    LLMDOT_TRY(step_kernel_shape(m, batch, n_phases, n_cta, kind_buf.data(), (int)kind_buf.size()));
-    if (!events) return LLMDOT_OK;
-    if (kinds)
-        for (int i = 0; i < *n_phases && i < (int)kind_buf.size(); i++) kinds[i] = kind_buf[i];
     LLMDOT_TRY(ensure_pinned(m, batch));
     ModelExtra &x = extra(m);
     Workspace &w = m->ws;
@@ -1238,22 +1214,39 @@ extern "C" int llmdot_cuda_trace_step(llmdot_session **sessions, int batch, cons
         x.h_pinned[x.cap + i] = sessions[i]->pos;
         x.h_views[i] = sessions[i]->view;
     }
-    const size_t n_ev = (size_t)*n_phases * *n_cta * 16;
-    unsigned long long *d_ev = nullptr;
-    LLMDOT_CUDA_TRY(cudaMalloc(&d_ev, sizeof(unsigned long long) * n_ev));
-    cudaMemsetAsync(d_ev, 0, sizeof(unsigned long long) * n_ev, st);
-    cudaMemcpyAsync(w.next, x.h_pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st);
-    cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st);
-    cudaMemcpyAsync(w.views, x.h_views, sizeof(KvView) * batch, cudaMemcpyHostToDevice, st);
-    int rc = launch_step_kernel(m, batch, kv_type, 1, nullptr, st, d_ev);
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.next, x.h_pinned, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.pos, x.h_pinned + x.cap, sizeof(int32_t) * batch, cudaMemcpyHostToDevice, st));
+    LLMDOT_CUDA_TRY(cudaMemcpyAsync(w.views, x.h_views, sizeof(KvView) * batch, cudaMemcpyHostToDevice, st));
+    StepTimer tm;
+    m->timer = &tm;
+    int rc = forward_step(m, batch, kv_type, w.next, w.pos, w.views, w.next, st);
+    m->timer = nullptr;
     if (rc == LLMDOT_OK &&
-        cudaMemcpyAsync(events, d_ev, sizeof(unsigned long long) * n_ev, cudaMemcpyDeviceToHost, st) != cudaSuccess)
-        rc = cuda_fail(cudaGetLastError(), "trace copy");
-    if (cudaStreamSynchronize(st) != cudaSuccess && rc == LLMDOT_OK) rc = cuda_fail(cudaGetLastError(), "trace_step");
-    cudaFree(d_ev);
+        cudaMemcpyAsync(x.h_pinned + 2 * x.cap, w.next, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        rc = cuda_fail(cudaGetLastError(), "profile_step copy");
+    if (cudaStreamSynchronize(st) != cudaSuccess && rc == LLMDOT_OK) rc = cuda_fail(cudaGetLastError(), "profile_step");
+    for (int f = 0; f < n_families; f++) {
+        family_ms[f] = 0.0f;
+        family_launches[f] = 0;
+    }
+    for (int i = 0; rc == LLMDOT_OK && i < tm.n; i++) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, tm.ev[2 * i], tm.ev[2 * i + 1]) != cudaSuccess) {
+            rc = cuda_fail(cudaGetLastError(), "profile_step elapsed");
+            break;
+        }
+        if (tm.fam[i] < n_families) {
+            family_ms[tm.fam[i]] += ms;
+            family_launches[tm.fam[i]] += 1;
+        }
+    }
+    tm.destroy();
     LLMDOT_TRY(rc);
     LLMDOT_TRY(check_err_flag(m));
-    for (int i = 0; i < batch; i++) sessions[i]->pos += 1;
+    for (int i = 0; i < batch; i++) {
+        if (next_tokens) next_tokens[i] = x.h_pinned[2 * x.cap + i];
+        sessions[i]->pos += 1;
+    }
     return LLMDOT_OK;
 }
 

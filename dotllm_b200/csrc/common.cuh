@@ -179,6 +179,30 @@ __device__ __forceinline__ float key_float(uint32_t k)
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
+// VectorMath.ArgMax (src/Llmdot.Core/Tensors/Numeric/VectorMath.cs:412-425) as a max-reduction of
+// packed keys (value key << 32 | (0xFFFFFFFF - index)), so that among equal value keys the lowest
+// index wins.  The reference starts from element 0 and moves only on a strict `>`, hence:
+//   * a NaN never replaces the running maximum: NaN gets the lowest value key (0, below -Inf);
+//   * a NaN at index 0 is never replaced by anything: there it gets the highest key (0xFFFFFFFF,
+//     above +Inf);
+//   * -0 and +0 compare equal: -0 is keyed as +0, so the earlier of the two stays.
+// gidx is the index in the whole row (the vocabulary index under tensor parallelism).
+__device__ __forceinline__ unsigned long long argmax_key(float f, uint32_t gidx)
+{
+    uint32_t b = __float_as_uint(f), vk;
+    if ((b & 0x7FFFFFFFu) > 0x7F800000u) {
+        vk = gidx == 0 ? 0xFFFFFFFFu : 0u;
+    } else {
+        if (b == 0x80000000u) b = 0u;
+        vk = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    }
+    return ((unsigned long long)vk << 32) | (unsigned long long)(0xFFFFFFFFu - gidx);
+}
+__device__ __forceinline__ int32_t argmax_key_index(unsigned long long k)
+{
+    return (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+}
+
 // Programmatic dependent launch.  A kernel launched with the programmatic-serialization
 // attribute may start while its predecessor in the stream is still running; it must call
 // pdl_wait() before it reads anything the predecessor writes and before it writes any

@@ -164,11 +164,6 @@ int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc 
     m->use_fast_gemv = getenv("LLMDOT_REFERENCE_MATVEC") == nullptr;
     // programmatic dependent launch between the step's kernels (LLMDOT_NO_PDL=1 turns it off)
     m->use_pdl = getenv("LLMDOT_NO_PDL") == nullptr;
-    // persistent whole-step kernel: prompt prefill by default (LLMDOT_NO_STEP_KERNEL=1 turns it
-    // off), greedy decode steps only with LLMDOT_STEP_DECODE=1 (the per-operation graph is faster
-    // there today)
-    m->use_step_kernel = getenv("LLMDOT_NO_STEP_KERNEL") == nullptr;
-    m->step_decode = m->use_step_kernel && getenv("LLMDOT_STEP_DECODE") != nullptr;
     int rc = LLMDOT_OK;
     auto bail = [&](int code) { model_destroy(m); return code; };
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -180,9 +175,9 @@ int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc 
     const llmdot_tensor_desc *emb = D("token_embd.weight");
     if (!emb) return bail(fail(LLMDOT_E_FORMAT, "token_embd.weight missing"));
     if ((rc = upload_mat(m, emb, m->emb, H, c.vocab))) return bail(rc);
-    const llmdot_tensor_desc *outw = nullptr;
-    for (int i = 0; i < n; i++)
-        if (t[i].name && strcmp(t[i].name, "output.weight") == 0) outw = &t[i];
+    // ComputeLogits (InferenceEngine.cs:583-602) looks the head up with TryGetTensor, whose keys
+    // compare OrdinalIgnoreCase like every other lookup here
+    const llmdot_tensor_desc *outw = D("output.weight");
     if (tps) {
         // the logits head holds this rank's vocabulary rows (tied models: a shard of the embedding,
         // which itself stays whole for the lookup)
@@ -278,7 +273,6 @@ void model_destroy(llmdot_model *m)
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     tp_comm_destroy(m);
-    step_cache_free(m);
     for (void *p : m->ws.allocs) cudaFree(p);
     for (void *p : m->allocs) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -337,6 +331,39 @@ int gemv(const DevMat &W, const float *x, int ldx, int nv, float *y, int ldy, bo
 {
     if (fast && W.tiled && gemv_fast_supported(W, nv)) return launch_gemv_fast(W, x, ldx, nv, y, ldy, accumulate, st);
     return launch_gemv_ref(W.raw, W.type, W.rows, W.cols, x, ldx, nv, y, ldy, accumulate, st);
+}
+
+int StepTimer::begin(cudaStream_t st, int family)
+{
+    if ((size_t)(2 * n + 2) > ev.size()) {
+        cudaEvent_t a, b;
+        LLMDOT_CUDA_TRY(cudaEventCreate(&a));
+        if (cudaEventCreate(&b) != cudaSuccess) {
+            cudaEventDestroy(a);
+            return cuda_fail(cudaGetLastError(), "cudaEventCreate");
+        }
+        ev.push_back(a);
+        ev.push_back(b);
+    }
+    if ((size_t)n >= fam.size()) fam.resize(n + 1);
+    fam[n] = family;
+    LLMDOT_CUDA_TRY(cudaEventRecord(ev[2 * n], st));
+    return LLMDOT_OK;
+}
+
+int StepTimer::end(cudaStream_t st)
+{
+    LLMDOT_CUDA_TRY(cudaEventRecord(ev[2 * n + 1], st));
+    n++;
+    return LLMDOT_OK;
+}
+
+void StepTimer::destroy()
+{
+    for (cudaEvent_t e : ev) cudaEventDestroy(e);
+    ev.clear();
+    fam.clear();
+    n = 0;
 }
 
 // ProcessToken (InferenceEngine.cs:134-146) for `batch` independent sessions at once.
@@ -410,8 +437,15 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
         return launch_gemv_ref(W.raw, W.type, W.rows, W.cols, xin, ld, batch, y, ldy, mode == GEMV_ADD, st);
     };
 
+    // measurement hook: brackets the launches of one operation with events (no-op unless attached)
+    StepTimer *tm = m->timer;
+    auto tb = [&](int fam) { return tm ? tm->begin(st, fam) : (int)LLMDOT_OK; };
+    auto te = [&]() { return tm ? tm->end(st) : (int)LLMDOT_OK; };
+
     // GetEmbedding + EmbeddingScale
+    LLMDOT_TRY(tb(FAM_OTHER));
     LLMDOT_TRY(launch_embed(m->emb.raw, m->emb.type, H, c.vocab, tokens, batch, c.emb_scale, w.h, H, w.err, st));
+    LLMDOT_TRY(te());
     for (int l = 0; l < c.layers; l++) {
         const LayerW &L = m->layers[l];
         // L2 prefetches: each matvec pulls in the weights of the one after it (the attention
@@ -428,6 +462,7 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
         // ApplyNorm(attn_norm) :544-562 fused into the Q/K/V projections :321-353
         float *q, *k, *v;
         int ldq, ldkv;
+        LLMDOT_TRY(tb(FAM_MATVEC));
         if (L.qkv.valid()) {
             LLMDOT_TRY(mv(L.qkv, nullptr, w.h, H, L.attn_norm, w.qkv, qDim + 2 * kvDim, GEMV_STORE, &pf_o));
             q = w.qkv;
@@ -475,36 +510,71 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
             ldq = qDim;
             ldkv = kvDim;
         }
+        LLMDOT_TRY(te());
         // RoPE of q and k, K/V cache append :362-382, attention :384-442
+        LLMDOT_TRY(tb(FAM_ATTENTION));
         LLMDOT_TRY(launch_attention_step(q, ldq, k, v, ldkv, pos, m->cos_t, m->sin_t, views, l, kv_type, sh, batch,
                                          w.scores, w.part_m, w.part_s, w.part_o, w.counters, w.attn, qDim,
                                          (flags & STEP_CHUNK) != 0, pdl, st));
+        LLMDOT_TRY(te());
         // attn_output matvec + residual add :444-449, :189
         // tensor parallel: rank 0 adds its partial onto the residual, the others store theirs, and
         // the all-reduce leaves h + the sum of the partials on every rank
         const int res_mode = (m->tp > 1 && m->tp_rank != 0) ? GEMV_STORE : GEMV_ADD;
+        LLMDOT_TRY(tb(FAM_MATVEC));
         LLMDOT_TRY(mv(L.o, nullptr, w.attn, qDim, nullptr, w.h, H, res_mode, &pf_ffn));
-        if (m->tp > 1) LLMDOT_TRY(tp_allreduce_sum(m, w.h, (size_t)batch * H, st));
-        if (gemma && L.post_attn) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_attn, w.h, H, H, batch, c.eps, st, pdl));
+        LLMDOT_TRY(te());
+        if (m->tp > 1) {
+            LLMDOT_TRY(tb(FAM_COLLECTIVE));
+            LLMDOT_TRY(tp_allreduce_sum(m, w.h, (size_t)batch * H, st));
+            LLMDOT_TRY(te());
+        }
+        if (gemma && L.post_attn) {
+            LLMDOT_TRY(tb(FAM_OTHER));
+            LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_attn, w.h, H, H, batch, c.eps, st, pdl));
+            LLMDOT_TRY(te());
+        }
         // FfnForward :452-487: ApplyNorm(ffn_norm ?? attn_norm), gate and up, act(gate)*up in one launch
+        LLMDOT_TRY(tb(FAM_MATVEC));
         LLMDOT_TRY(mv(L.gate, &L.up, w.h, H, L.ffn_norm ? L.ffn_norm : L.attn_norm, w.gate, c.ffn,
                       c.ffn_type == 2 ? GEMV_GELU_MUL : GEMV_SILU_MUL, &pf_down));
+        LLMDOT_TRY(te());
         // down projection + residual add
+        LLMDOT_TRY(tb(FAM_MATVEC));
         LLMDOT_TRY(mv(L.down, nullptr, w.gate, c.ffn, nullptr, w.h, H, res_mode, &pf_next));
-        if (m->tp > 1) LLMDOT_TRY(tp_allreduce_sum(m, w.h, (size_t)batch * H, st));
-        if (gemma && L.post_ffw) LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_ffw, w.h, H, H, batch, c.eps, st, pdl));
+        LLMDOT_TRY(te());
+        if (m->tp > 1) {
+            LLMDOT_TRY(tb(FAM_COLLECTIVE));
+            LLMDOT_TRY(tp_allreduce_sum(m, w.h, (size_t)batch * H, st));
+            LLMDOT_TRY(te());
+        }
+        if (gemma && L.post_ffw) {
+            LLMDOT_TRY(tb(FAM_OTHER));
+            LLMDOT_TRY(launch_rmsnorm(w.h, H, L.post_ffw, w.h, H, H, batch, c.eps, st, pdl));
+            LLMDOT_TRY(te());
+        }
     }
     if (flags & STEP_NO_HEAD) return LLMDOT_OK;  // prompt chunk before the last: no logits needed
     // ApplyFinalNorm :575-581 fused into ComputeLogits :583-602
     const DevMat &head = m->out.valid() ? m->out : m->emb;
     // logits rows [head_lo, head_lo + head_rows): the whole vocabulary without tensor parallelism
+    LLMDOT_TRY(tb(FAM_MATVEC));
     LLMDOT_TRY(mv(head, nullptr, w.h, H, m->out_norm, w.logits, m->head_rows, GEMV_STORE));
+    LLMDOT_TRY(te());
     // final softcap + greedy argmax (InferenceEngine.cs:105-108, Sampler.cs:26-27); across ranks the
     // packed (value, index) keys reduce with max
+    LLMDOT_TRY(tb(FAM_OTHER));
     LLMDOT_TRY(launch_argmax_keys(w.logits, m->head_rows, m->head_rows, batch, w.keys, c.has_final_cap != 0,
                                   c.final_cap, nullptr, m->head_lo, c.vocab, st));
-    if (m->tp > 1) LLMDOT_TRY(tp_allreduce_max_u64(m, w.keys, batch, st));
-    return launch_argmax_finish(w.keys, batch, next, st);
+    LLMDOT_TRY(te());
+    if (m->tp > 1) {
+        LLMDOT_TRY(tb(FAM_COLLECTIVE));
+        LLMDOT_TRY(tp_allreduce_max_u64(m, w.keys, batch, st));
+        LLMDOT_TRY(te());
+    }
+    LLMDOT_TRY(tb(FAM_OTHER));
+    LLMDOT_TRY(launch_argmax_finish(w.keys, batch, next, st));
+    return te();
 }
 
 }  // namespace llmdot

@@ -7,7 +7,6 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
-#include "step.cuh"
 
 namespace llmdot {
 
@@ -49,6 +48,19 @@ struct Workspace {
 };
 constexpr int HIST_STEPS = 4096;
 
+// Per-launch device timing of one forward step (the measurement hook llmdot_cuda_profile_step):
+// while a StepTimer is attached to the model, forward_step brackets each launch (or the launches
+// of one operation) with CUDA events on its stream and files the span under a kernel family.
+enum { FAM_MATVEC = 0, FAM_ATTENTION = 1, FAM_OTHER = 2, FAM_COLLECTIVE = 3, FAM_COUNT = 4 };
+struct StepTimer {
+    std::vector<cudaEvent_t> ev;  // pairs (start, end), reused across steps
+    std::vector<int> fam;         // family of each recorded span
+    int n = 0;                    // spans recorded in the current step
+    int begin(cudaStream_t st, int family);
+    int end(cudaStream_t st);
+    void destroy();
+};
+
 }  // namespace llmdot
 
 struct llmdot_session;
@@ -69,14 +81,12 @@ struct llmdot_model {
     llmdot::Workspace ws;
     bool use_fast_gemv = true;
     bool use_pdl = true;
-    bool use_step_kernel = true;            // persistent whole-step kernel for prefill
-    bool step_decode = false;               // ... and for decode steps
     // tensor parallelism: cfg above holds THIS rank's local heads / kv heads / FFN rows; full_cfg
     // the model's; the logits head (m->out) holds vocabulary rows [head_lo, head_lo + head_rows)
     int tp = 1, tp_rank = 0, head_lo = 0, head_rows = 0;
     llmdot_config full_cfg{};
     void *nccl = nullptr;  // ncclComm_t once llmdot_cuda_tp_init ran
-    llmdot::StepCache *step_cache = nullptr;  // per-batch launch plans of that kernel
+    llmdot::StepTimer *timer = nullptr;  // attached only while llmdot_cuda_profile_step runs
 };
 
 struct llmdot_session {

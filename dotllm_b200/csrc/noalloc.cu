@@ -10,7 +10,10 @@
 //
 // The array's name is only a host-side stand-in in host code, so the host looks up its real
 // device address once per device with cudaGetSymbolAddress (with that device current) and
-// passes the address to the kernels.
+// passes the address to the kernels.  That first call also loads the library's device code
+// (CUDA loads modules lazily), which may make the driver take device memory: hosts make one
+// warm-up call per device before they reserve their pools.  The cached address belongs to the
+// device's primary context; a cudaDeviceReset invalidates it.
 #include <mutex>
 
 #include "common.cuh"
@@ -33,7 +36,7 @@ __global__ void argmax_noalloc_kernel(const float *__restrict__ x, int ld, int n
     const float *xr = x + (uint64_t)row * ld;
     unsigned long long best = 0ull;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        unsigned long long k = ((unsigned long long)float_key(xr[i]) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+        const unsigned long long k = argmax_key(xr[i], (uint32_t)i);
         best = k > best ? k : best;
     }
 #pragma unroll

@@ -320,8 +320,9 @@ int launch_softmax(float *x, int n, bool has_cap, float cap, cudaStream_t st)
 
 // ------------------------------------------------------------------ argmax
 // VectorMath.ArgMax (VectorMath.cs:412-425): first index of the maximum.  Packed
-// 64-bit key (orderable float << 32 | ~index) reduced with atomicMax, so the largest
-// value wins and, among equal values, the lowest index.  Optional in-kernel final
+// 64-bit keys (argmax_key: value key << 32 | ~index) reduced with atomicMax, so the largest
+// value wins and, among equal values, the lowest index; NaN and -0 are keyed so that the result
+// is the reference's strict-`>` scan from element 0.  Optional in-kernel final
 // softcap of the logits first (Generate applies it before sampling,
 // InferenceEngine.cs:105-106); the capped logits are written back to `capped` if given.
 // Under tensor parallelism x holds vocabulary entries [off, off + n) of `ntot`: keys carry the
@@ -340,7 +341,7 @@ __global__ void argmax_kernel(const float *__restrict__ x, int ldx, int n, unsig
             f = softcap_ref(f, cap, inv_cap, i < nvec);
             if (capped) capped[(uint64_t)v * ldx + i] = f;
         }
-        unsigned long long k = ((unsigned long long)float_key(f) << 32) | (0xFFFFFFFFu - (uint32_t)(i + off));
+        const unsigned long long k = argmax_key(f, (uint32_t)(i + off));
         best = k > best ? k : best;
     }
 #pragma unroll

@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
             for (int u = 0; u < SMP_UNROLL; u++) {
                 const int i = base + u * SMP_THREADS + tid;
                 if (i >= n) continue;
-                const unsigned long long kk = ((unsigned long long)float_key(vals[u]) << 32) | (uint32_t)~i;
+                const unsigned long long kk = argmax_key(vals[u], (uint32_t)i);
                 best = kk > best ? kk : best;
             }
         }

@@ -198,19 +198,22 @@ def decode_steps(sessions: List[CudaSession], tokens, n_steps: int):
     return out[:n_steps], ms.value, kps.value
 
 
-def trace_step(sessions: List[CudaSession], tokens):
-    """One greedy step of the persistent step kernel with per-phase timestamps.
-    Returns (events [phases, ctas, 16], kinds [phases]); see llmdot_cuda_trace_step."""
+FAMILIES = ("matvec", "attention", "other", "collective")
+
+
+def profile_step(sessions: List[CudaSession], tokens):
+    """One greedy step launched operation by operation with CUDA events around each operation:
+    returns (next ids, {family: (ms, operations)}); see llmdot_cuda_profile_step."""
     B = len(sessions)
     arr = (VP * B)(*[s._h for s in sessions])
-    toks = _batch_tokens("trace_step", tokens, B)
-    nph, ncta = C.c_int(), C.c_int()
-    check(lib().llmdot_cuda_trace_step(arr, B, toks.ctypes.data_as(I32P), None, None, C.byref(nph), C.byref(ncta)))
-    ev = np.zeros((nph.value, ncta.value, 16), dtype=np.uint64)
-    kinds = np.zeros(nph.value, dtype=np.int32)
-    check(lib().llmdot_cuda_trace_step(arr, B, toks.ctypes.data_as(I32P), ev.ctypes.data_as(C.POINTER(C.c_uint64)),
-                                       kinds.ctypes.data_as(C.POINTER(C.c_int)), C.byref(nph), C.byref(ncta)))
-    return ev, kinds
+    toks = _batch_tokens("profile_step", tokens, B)
+    nxt = np.zeros(B, dtype=np.int32)
+    nf = len(FAMILIES)
+    ms = np.zeros(nf, dtype=np.float32)
+    cnt = (C.c_int * nf)()
+    check(lib().llmdot_cuda_profile_step(arr, B, toks.ctypes.data_as(I32P), nxt.ctypes.data_as(I32P), nf,
+                                         ms.ctypes.data_as(F32P), cnt))
+    return nxt, {f: (float(ms[i]), int(cnt[i])) for i, f in enumerate(FAMILIES)}
 
 
 def decode_batch(sessions: List[CudaSession], tokens, want_logits: bool = False):

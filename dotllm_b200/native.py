@@ -112,9 +112,8 @@ _SIGS = {
     "llmdot_cuda_tp_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
     "llmdot_cuda_tp_init": (C.c_int, [VP, C.POINTER(C.c_uint8)]),
     "llmdot_cuda_tp_shard": (C.c_int, [C.POINTER(LlmdotConfig), C.c_int, C.c_int, I32P]),
+    "llmdot_cuda_profile_step": (C.c_int, [C.POINTER(VP), C.c_int, I32P, I32P, C.c_int, F32P, C.POINTER(C.c_int)]),
     "llmdot_cuda_profile_matvec": (C.c_int, [VP, C.c_char_p, C.c_int, C.c_int, F32P, C.POINTER(C.c_uint64)]),
-    "llmdot_cuda_trace_step": (C.c_int, [C.POINTER(VP), C.c_int, I32P, C.POINTER(C.c_uint64), C.POINTER(C.c_int),
-                                         C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "llmdot_cuda_argmax_noalloc": (C.c_int, [VP, C.c_int, C.c_int, C.c_int, VP, VP]),
     "llmdot_cuda_model_matvec": (C.c_int, [VP, C.c_char_p, F32P, C.c_int, C.c_int, F32P, F32P]),
 }

@@ -323,17 +323,17 @@ LLMDOT_API int llmdot_cuda_tp_shard(const llmdot_config *cfg, int tp_size, int t
 LLMDOT_API int llmdot_cuda_profile_matvec(llmdot_model *m, const char *tensor, int batch, int iters,
                                           float *avg_ms, uint64_t *bytes);
 
-/* Profiling hook (no counterpart in the reference): runs ONE greedy decode step of the
- * persistent step kernel for `batch` sessions fed `tokens` and records %globaltimer stamps (ns)
- * events[(phase * n_cta + cta) * 16 + k], k = 0 phase start, 1 input built, 2 weight tiles done,
- * 3 phase end; for warp 0 of the CTA 4 ns waiting for weight tiles, 5 ns computing them, 6 tile
- * count; inside the input build 8 first thread's loads done, 9 statistics reduced, 10 first
- * thread's fragments written (other k unused, 0); kinds[phase] = 1 attention scores, 2 attention P.V, 10 + epilogue (0 store, 1 residual
- * add, 2 silu*up, 3 gelu*up, 4 logits + argmax) for matvec phases.  With events == NULL only
- * *n_phases and *n_cta are filled in (size the arrays from them).  The sessions advance by one
- * token otherwise.  LLMDOT_E_UNSUPPORTED when the model / batch runs without that kernel. */
-LLMDOT_API int llmdot_cuda_trace_step(llmdot_session **sessions, int batch, const int32_t *tokens,
-                                      uint64_t *events, int *kinds, int *n_phases, int *n_cta);
+/* Measurement hook (no counterpart in the reference): ONE greedy decode step for `batch` sessions
+ * fed `tokens`, launched operation by operation (not from the captured step graph) with CUDA events
+ * around each operation's launches on the model's stream.  family_ms[f] and family_launches[f]
+ * receive the summed device time (ms) and the number of timed operations of kernel family f, for
+ * f < n_families: 0 quantised matvec / matmul (with its fused norm, activation and residual
+ * epilogues), 1 attention (RoPE, KV append, attention), 2 other element-wise kernels (embedding,
+ * Gemma post-norms, argmax), 3 collectives (tensor parallelism).  next_tokens (nullable) receives
+ * the greedy ids; the sessions advance by one token, as with llmdot_cuda_decode.  Under tensor
+ * parallelism every rank makes the same call. */
+LLMDOT_API int llmdot_cuda_profile_step(llmdot_session **sessions, int batch, const int32_t *tokens,
+                                        int32_t *next_tokens, int n_families, float *family_ms, int *family_launches);
 
 /* Greedy argmax over logits that are already in device memory, without allocating any device
  * memory.  No counterpart in the reference: it exists for hosts that own all device memory
@@ -347,8 +347,13 @@ LLMDOT_API int llmdot_cuda_trace_step(llmdot_session **sessions, int batch, cons
  * are rejected with LLMDOT_E_INVALID.  The call is asynchronous on `stream`.  All calls on a
  * device share that array and it keeps the last call's contents (each call clears the rows it
  * uses): calls that overlap on the GPU race and return wrong indices.  The first call on each
- * device looks the array's address up (cudaGetSymbolAddress) with that device current; make that
- * first call before any stream capture. */
+ * device looks the array's address up (cudaGetSymbolAddress) with that device current and is
+ * the first launch of its two kernels; with CUDA's lazy module loading both load the library's
+ * device code, for which the driver itself may take device memory.  So make one warm-up call on
+ * each device before the host reserves its memory pools, and before any stream capture; later
+ * calls allocate nothing.  The address is kept per device for the life of the process: after a
+ * cudaDeviceReset (or anything else that destroys the device's primary context) the cached
+ * address is stale, so do not reset a device that this entry point has been used on. */
 #define LLMDOT_ARGMAX_NOALLOC_MAX_ROWS 4096
 LLMDOT_API int llmdot_cuda_argmax_noalloc(const float *d_logits, int n, int rows, int ld, int32_t *d_index,
                                           void *stream);

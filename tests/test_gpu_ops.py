@@ -145,6 +145,39 @@ def test_argmax(backend, oracle, n):
         assert backend.arg_max(x) == 3 == oracle.argmax(x)
 
 
+def _special_rows(rng, n):
+    """Rows of n floats with NaN, signed zeros and infinities placed where VectorMath.ArgMax's strict
+    `>` scan from element 0 decides differently from a plain order on the float values."""
+    from test_oracle_kats import ARGMAX_SPECIAL
+    rows = [np.array(r, dtype=np.float32) for r, _ in ARGMAX_SPECIAL]
+    nan, inf = np.float32("nan"), np.float32("inf")
+    base = -np.abs(rng.standard_normal(n).astype(np.float32)) - 1.0
+    x = base.copy(); x[0] = nan; x[n // 2] = inf; rows.append(x)            # NaN first: index 0
+    x = base.copy(); x[n // 3] = nan; x[n - 1] = nan; rows.append(x)        # NaN never wins
+    x = base.copy(); x[5] = -0.0; x[n - 7] = 0.0; rows.append(x)             # -0 then +0: the first
+    x = base.copy(); x[9] = 0.0; x[11] = -0.0; x[3] = nan; rows.append(x)
+    x = np.full(n, -inf, dtype=np.float32); x[n - 3] = nan; rows.append(x)  # all -Inf: index 0
+    x = np.full(n, nan, dtype=np.float32); rows.append(x)                    # all NaN: index 0
+    x = base.copy(); x[n - 1] = inf; x[n - 2] = inf; x[n - 4] = nan; rows.append(x)
+    return rows
+
+
+@pytest.mark.parametrize("n", [64, 32000, 128256])
+def test_argmax_special_values(backend, oracle, n):
+    """Index-exact against the reference's ArgMax on NaN, +-0 and +-Inf rows (argmax_kernel)."""
+    for x in _special_rows(np.random.default_rng(n), n):
+        assert backend.arg_max(x) == oracle.argmax(x), x[:16]
+
+
+@pytest.mark.parametrize("n", [64, 32000])
+def test_sampler_greedy_special_values(backend, oracle, n):
+    """Sampler.Sample with Temperature <= 0 is ArgMax (Sampler.cs:26-27): same special rows."""
+    from dotllm_b200.native import LlmdotSampling
+    opt = LlmdotSampling(temperature=0.0, seed=1)
+    for x in _special_rows(np.random.default_rng(n + 1), n):
+        assert backend.sample(x, opt, r=0.5) == oracle.argmax(x), x[:16]
+
+
 def test_conv1d(backend):
     rng = np.random.default_rng(9)
     x = rng.standard_normal(64 * 3).astype(np.float32)

@@ -112,15 +112,14 @@ def test_backend_rejects_short_host_arrays_before_the_call():
 
 
 def test_engine_rejects_token_and_draw_counts_the_library_would_overrun():
-    """decode / decode_steps / trace_step read one token per session and generate_sampled one
+    """decode / decode_steps read one token per session and generate_sampled one
     draw per token: other counts are refused before the call (no device needed)."""
     from types import SimpleNamespace
 
     from dotllm_b200 import engine
     fake = [SimpleNamespace(_h=None), SimpleNamespace(_h=None)]
     for call in (lambda: engine.decode_batch(fake, [1]),
-                 lambda: engine.decode_steps(fake, [1, 2, 3], 4),
-                 lambda: engine.trace_step(fake, [])):
+                 lambda: engine.decode_steps(fake, [1, 2, 3], 4)):
         with pytest.raises(ValueError):
             call()
     s = engine.CudaSession.__new__(engine.CudaSession)
@@ -129,14 +128,14 @@ def test_engine_rejects_token_and_draw_counts_the_library_would_overrun():
         s.generate_sampled([1, 2], 8, native.LlmdotSampling(), draws=np.full(7, 0.5, np.float32))
 
 
-def test_integration_bindings_name_declared_entry_points():
-    """Every [LibraryImport] EntryPoint written out in INTEGRATION.md is a function the header
-    declares (the C# binding a maintainer copies must not name a symbol that does not exist)."""
+def test_csharp_bindings_name_declared_entry_points():
+    """Every entry point the C# [LibraryImport] bindings bind (the list in
+    tests/golden/csharp_bindings.json) is a function the header declares: a binding must not name
+    a symbol that does not exist."""
+    import json
     import os
-    import re
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    doc = open(os.path.join(root, "INTEGRATION.md")).read()
-    entry_points = set(re.findall(r'EntryPoint = "(\w+)"', doc))
+    here = os.path.dirname(os.path.abspath(__file__))
+    entry_points = set(json.load(open(os.path.join(here, "golden", "csharp_bindings.json")))["entry_points"])
     assert entry_points and entry_points <= set(native.header_functions())
 
 

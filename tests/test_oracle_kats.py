@@ -110,6 +110,26 @@ def test_argmax_ties_lowest_index(oracle):  # VectorMath.cs:412-425 (strict >)
     assert oracle.argmax([1, 7, 7, 2]) == 1
 
 
+# VectorMath.ArgMax (VectorMath.cs:412-425) starts from element 0 and moves only on `>`: a NaN never
+# becomes the maximum, a NaN at element 0 is never replaced, and -0 / +0 compare equal.
+ARGMAX_SPECIAL = [
+    ([1.0, float("nan"), 3.0, 2.0], 2),
+    ([float("nan"), 1.0, 5.0, float("inf")], 0),
+    ([1.0, float("nan"), float("nan")], 0),
+    ([-0.0, 0.0, -1.0], 0),
+    ([-1.0, 0.0, -0.0], 1),
+    ([-1.0, -0.0, 0.0], 1),
+    ([float("-inf"), float("-inf"), -3.0], 2),
+    ([float("-inf"), float("nan"), float("-inf")], 0),
+    ([2.0, float("inf"), float("nan"), float("inf")], 1),
+]
+
+
+@pytest.mark.parametrize("row,want", ARGMAX_SPECIAL)
+def test_argmax_special_values(oracle, row, want):
+    assert oracle.argmax(np.array(row, dtype=np.float32)) == want
+
+
 def test_add_scale_mul(oracle):  # VectorMathTests.cs:88-108, VectorMathExtendedTests.cs:50-80
     assert list(oracle.add([1, 2, 3], [4, 5, 6])) == [5, 7, 9]
     assert list(oracle.scale([1, 2, 3], 2.0)) == [2, 4, 6]
