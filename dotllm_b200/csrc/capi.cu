@@ -843,6 +843,7 @@ static int check_err_flag(llmdot_model *m)
     if (e) {
         cudaMemset(m->ws.err, 0, sizeof(int));
         if (e == 1) return fail(LLMDOT_E_INVALID, "token id outside the vocabulary");
+        if (e == 5) return fail(LLMDOT_E_TIMEOUT, "tensor-core matmul: a bounded wait gave up");
         return fail(LLMDOT_E_CUDA, "device error flag " + std::to_string(e));
     }
     return LLMDOT_OK;
@@ -887,8 +888,8 @@ static int prefill_rows(llmdot_session *s, const int32_t *tokens, int n, float *
     int rc = LLMDOT_OK;
     int last_row = 0;  // row of the workspace that holds the last prompt token's logits
     if (m->use_fast_gemv) {
-        // prompt chunks of up to GEMM_MAX_ROWS consecutive positions, one batched step each
-        const int CH = n < GEMM_MAX_ROWS ? n : GEMM_MAX_ROWS;
+        // prompt chunks of up to TC_MAX_ROWS consecutive positions, one batched step each
+        const int CH = n < TC_MAX_ROWS ? n : TC_MAX_ROWS;
         rc = ensure_workspace(m, CH);
         if (rc == LLMDOT_OK) {
             std::vector<KvView> vs(CH, s->view);
@@ -1280,10 +1281,10 @@ extern "C" int llmdot_cuda_profile_matvec(llmdot_model *m, const char *tensor, i
     LLMDOT_CUDA_TRY(cudaSetDevice(m->device));
     // as in the decode step: 5..32 rows run the batched kernel (input fragments + matmul per
     // launch), and so do 2..4 rows whose input does not fit the matvec kernel's shared memory
-    bool batched = m->use_fast_gemv && batch >= 2 && batch <= GEMM_MAX_ROWS;
-    bool any_wide = batch >= GEMM_MIN_ROWS;
+    bool batched = m->use_fast_gemv && batch >= 2 && batch <= TC_MAX_ROWS;
+    bool any_wide = batch >= TC_MIN_ROWS;
     for (const DevMat *W : mats) {
-        batched = batched && gemm_supported(*W, batch);
+        batched = batched && tc_supported(*W);
         any_wide = any_wide || !gemv_fast_supported(*W, batch);
     }
     batched = batched && any_wide;
@@ -1297,9 +1298,10 @@ extern "C" int llmdot_cuda_profile_matvec(llmdot_model *m, const char *tensor, i
         for (const DevMat *W : mats) {
             int rc;
             if (batched) {
-                GemmInput in;
-                rc = gemm_prepare(x, W->cols, batch, W->cols, nullptr, m->cfg.eps, W->type, 0, m->ws.gemm, &in, st);
-                if (rc == LLMDOT_OK) rc = launch_gemm(*W, in, y, W->rows, GEMV_STORE, m->ws.gemm, m->ws.err, st);
+                rc = tc_prepare(x, W->cols, batch, W->cols, nullptr, m->cfg.eps, W->type == T_Q4_K, W->type == T_Q6_K,
+                                m->ws.tc, st);
+                const TcSeg sg = {W, y, W->rows};
+                if (rc == LLMDOT_OK) rc = tc_gemm(&sg, 1, batch, GEMV_STORE, m->ws.tc, m->ws.err, st);
             } else {
                 rc = gemv(*W, x, W->cols, batch, y, W->rows, false, m->use_fast_gemv, st);
             }
@@ -1365,15 +1367,15 @@ extern "C" int llmdot_cuda_model_matvec(llmdot_model *m, const char *tensor, con
     if (cudaMemcpyAsync(dx, x, sizeof(float) * nx, cudaMemcpyHostToDevice, st) != cudaSuccess ||
         (norm_w && cudaMemcpyAsync(dn, norm_w, sizeof(float) * W.cols, cudaMemcpyHostToDevice, st) != cudaSuccess))
         rc = cuda_fail(cudaGetLastError(), "model_matvec upload");
-    const bool batched = mode != 1 && m->use_fast_gemv && batch >= 2 && gemm_supported(W, batch) &&
-                         (batch >= GEMM_MIN_ROWS || !gemv_fast_supported(W, batch));
+    const bool batched = mode != 1 && m->use_fast_gemv && batch >= 2 && batch <= TC_MAX_ROWS && tc_supported(W) &&
+                         (batch >= TC_MIN_ROWS || !gemv_fast_supported(W, batch));
     if (rc == LLMDOT_OK && batched) rc = ensure_workspace(m, batch);
     if (rc == LLMDOT_OK) {
         if (batched) {
-            GemmInput in;
-            rc = gemm_prepare(dx, W.cols, batch, W.cols, mode == 2 ? dn : nullptr, m->cfg.eps, W.type, 0, m->ws.gemm,
-                              &in, st);
-            if (rc == LLMDOT_OK) rc = launch_gemm(W, in, dy, W.rows, GEMV_STORE, m->ws.gemm, m->ws.err, st);
+            rc = tc_prepare(dx, W.cols, batch, W.cols, mode == 2 ? dn : nullptr, m->cfg.eps, W.type == T_Q4_K,
+                            W.type == T_Q6_K, m->ws.tc, st);
+            const TcSeg sg = {&W, dy, W.rows};
+            if (rc == LLMDOT_OK) rc = tc_gemm(&sg, 1, batch, GEMV_STORE, m->ws.tc, m->ws.err, st);
         } else if (mode == 1 || !m->use_fast_gemv || !gemv_fast_supported(W, batch)) {
             if (mode == 2) rc = fail(LLMDOT_E_UNSUPPORTED, "model_matvec: fused norm needs the tensor-core path");
             else rc = launch_gemv_ref(W.raw, W.type, W.rows, W.cols, dx, W.cols, batch, dy, W.rows, false, st);

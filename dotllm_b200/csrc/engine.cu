@@ -8,6 +8,7 @@
 #include <algorithm>
 
 #include "engine.cuh"
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "gemv_tile.cuh"
 #include "ops.cuh"
@@ -320,8 +321,9 @@ int ensure_workspace(llmdot_model *m, int batch)
     LLMDOT_CUDA_TRY(cudaMemset(w.hist_step, 0, sizeof(int32_t)));
     if (batch >= 2) {  // the batched kernel also takes 2..4 rows whose input does not fit the matvec's smem
         const int cols_max = std::max(std::max(c.hidden, (int)qDim), c.ffn);
-        const int rows_max = std::max(std::max(c.hidden, (int)(qDim + 2 * kvDim)), c.ffn);
-        LLMDOT_TRY(gemm_scratch_alloc(w.gemm, cols_max, rows_max, a));
+        // 128-row tiles of the largest launch: Q+K+V, gate+up, the logits head
+        const int rows_max = std::max(std::max(c.hidden, (int)(qDim + 2 * kvDim)), std::max(2 * c.ffn, c.vocab));
+        LLMDOT_TRY(tc_scratch_alloc(w.tc, cols_max, (rows_max + 127) / 128 + 8, a));
     }
     w.batch = batch;
     return LLMDOT_OK;
@@ -389,7 +391,7 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
 
     // y = epilogue(W . [rmsnorm](x)); the tensor-core kernel fuses the norm and the epilogue,
     // the generic kernel runs them as separate launches.
-    const bool batched = fast && batch <= GEMM_MAX_ROWS && w.gemm.xf[0] != nullptr;
+    const bool batched = fast && batch <= TC_MAX_ROWS && w.tc.ready();
     // the weights of the next matvec, handed to the current one for an L2 prefetch
     auto tiled_bytes = [](const DevMat *W) -> unsigned long long {
         if (!W || !W->tiled) return 0;
@@ -410,17 +412,18 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
                   int mode, const GemvPrefetch *pf = nullptr) -> int {
         if (fast && gemv_fast_supported(W, batch) && (!W1 || gemv_fast_supported(*W1, batch)))
             return launch_gemv_fast_ex(W, W1, norm_w, c.eps, x, ldx, batch, y, ldy, mode, st, pdl, pf);
-        if (batched && gemm_supported(W, batch) && (!W1 || gemm_supported(*W1, batch))) {
-            GemmInput in, in1;
-            LLMDOT_TRY(gemm_prepare(x, ldx, batch, W.cols, norm_w, c.eps, W.type, 0, w.gemm, &in, st));
+        if (batched && tc_supported(W) && (!W1 || (tc_supported(*W1) && W1->cols == W.cols))) {
+            // tensor-core matmul: the input's B operands are built once for the layouts in use
+            const bool q4 = W.type == T_Q4_K || (W1 && W1->type == T_Q4_K);
+            const bool q6 = W.type == T_Q6_K || (W1 && W1->type == T_Q6_K);
+            LLMDOT_TRY(tc_prepare(x, ldx, batch, W.cols, norm_w, c.eps, q4, q6, w.tc, st));
             if (mode == GEMV_SILU_MUL || mode == GEMV_GELU_MUL) {
-                LLMDOT_TRY(launch_gemm(W, in, w.gate, c.ffn, GEMV_STORE, w.gemm, w.err, st));
-                if (W1->type != W.type)
-                    LLMDOT_TRY(gemm_prepare(x, ldx, batch, W1->cols, norm_w, c.eps, W1->type, 1, w.gemm, &in1, st));
-                LLMDOT_TRY(launch_gemm(*W1, W1->type != W.type ? in1 : in, w.up, c.ffn, GEMV_STORE, w.gemm, w.err, st));
+                const TcSeg sg[2] = {{&W, w.gate, c.ffn}, {W1, w.up, c.ffn}};
+                LLMDOT_TRY(tc_gemm(sg, 2, batch, GEMV_STORE, w.tc, w.err, st));
                 return launch_act_mul(mode == GEMV_GELU_MUL, w.gate, w.up, y, c.ffn, batch, st);
             }
-            return launch_gemm(W, in, y, ldy, mode == GEMV_ADD ? GEMV_ADD : GEMV_STORE, w.gemm, w.err, st);
+            const TcSeg sg = {&W, y, ldy};
+            return tc_gemm(&sg, 1, batch, mode == GEMV_ADD ? GEMV_ADD : GEMV_STORE, w.tc, w.err, st);
         }
         const float *xin = x;
         int ld = ldx;
@@ -479,23 +482,17 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
                 qkv_rc = launch_gemv_multi(tg, 3, L.attn_norm, c.eps, w.h, H, batch, GEMV_STORE, pdl, st, &pf_o);
                 if (qkv_rc != LLMDOT_OK && qkv_rc != LLMDOT_E_UNSUPPORTED) return qkv_rc;
             }
-            if (qkv_rc != LLMDOT_OK && batched && gemm_supported(L.q, batch) && gemm_supported(L.k, batch) &&
-                gemm_supported(L.v, batch)) {
-                // batched: the fragments of the normed input are built once per tile layout
-                GemmInput in[2];
-                bool have[2] = {false, false};
+            if (qkv_rc != LLMDOT_OK && batched && tc_supported(L.q) && tc_supported(L.k) && tc_supported(L.v)) {
+                // batched: Q, K and V in one tensor-core launch over the normed input
                 const DevMat *mats[3] = {&L.q, &L.k, &L.v};
-                float *ys[3] = {w.q, w.k, w.v};
-                const int lds[3] = {qDim, kvDim, kvDim};
-                for (int i = 0; i < 3; i++) {
-                    const int lay = mats[i]->type == T_Q4_K ? 0 : 1;
-                    if (!have[lay]) {
-                        LLMDOT_TRY(gemm_prepare(w.h, H, batch, H, L.attn_norm, c.eps, mats[i]->type, lay, w.gemm,
-                                                &in[lay], st));
-                        have[lay] = true;
-                    }
-                    LLMDOT_TRY(launch_gemm(*mats[i], in[lay], ys[i], lds[i], GEMV_STORE, w.gemm, w.err, st));
+                bool q4 = false, q6 = false;
+                for (const DevMat *M : mats) {
+                    q4 = q4 || M->type == T_Q4_K;
+                    q6 = q6 || M->type == T_Q6_K;
                 }
+                LLMDOT_TRY(tc_prepare(w.h, H, batch, H, L.attn_norm, c.eps, q4, q6, w.tc, st));
+                const TcSeg sg[3] = {{&L.q, w.q, qDim}, {&L.k, w.k, kvDim}, {&L.v, w.v, kvDim}};
+                LLMDOT_TRY(tc_gemm(sg, 3, batch, GEMV_STORE, w.tc, w.err, st));
                 qkv_rc = LLMDOT_OK;
             }
             if (qkv_rc != LLMDOT_OK) {

@@ -6,7 +6,7 @@
 
 #include "attention.cuh"
 #include "common.cuh"
-#include "gemm.cuh"
+#include "gemm_tc.cuh"
 
 namespace llmdot {
 
@@ -43,7 +43,7 @@ struct Workspace {
     int *counters = nullptr;   // [batch][heads_kv] attention page-combine arrival counters
     int32_t *hist = nullptr;   // [HIST_STEPS][batch] greedy ids recorded by captured steps
     int32_t *hist_step = nullptr;
-    GemmScratch gemm;  // batched (5..32 rows) matmul fragments and K-split partials
+    TcScratch tc;  // tensor-core matmul (2..32 rows): prepared operands and K-split partials
     std::vector<void *> allocs;
 };
 constexpr int HIST_STEPS = 4096;

@@ -1,0 +1,732 @@
+// gemm_tc.cu -- quantised matmul for 2..32 input rows on the 5th-generation tensor cores:
+// batched decode steps (several sessions) and prompt chunks (consecutive tokens of one session).
+//
+// Same contract as the matvec (TensorOps.MatMulFusedQ4_K / Q6_K, src/Llmdot.Core/Tensors/TensorOps.cs:230-395,
+// several input rows as in TensorOps.MatMul's aRows > 1 branch, TensorOps.cs:92-111):
+// y[v][row] = sum_k x[v][k] * W[row][k], fp32 result.
+//
+// Arithmetic (exact products, fp32 sums, as in the matvec):
+// * x is scaled per input row by a power of two and split into fp16 hi + lo: MMA column v holds
+//   x_hi, column 32 + v holds x_lo (N = 64).
+// * Q4_K: the A operand is q * sc (integers <= 945, exact in fp16), one accumulator per super-block,
+//   read back from TMEM and scaled by the row's d on the CUDA cores; the offset term
+//   sum_j (8 d sc_j + dmin m_j) * S_j (S_j = sub-block sums of x) is one more MMA per super-block
+//   (coefficients and sums as fp16 hi/lo pairs) into a second accumulator that spans the whole K.
+// * Q6_K: the A operand sc * (q - 32) (|.| <= 4096) is split into an fp16 hi (rounded) and its exact
+//   residual lo (0 or +-1), two MMAs per K step; d applied per super-block as for Q4_K.
+//
+// Kernel structure (one CTA of 16 warps per SM, persistent over a contiguous range of work units;
+// a unit is one 128-row tile x one 256-weight super-block):
+//   warp 0        producer: cp.async.bulk of the raw 16-row weight tiles (already tiled at model
+//                 load) into a 2-slot ring, and of the prepared B operand per half super-block;
+//   warp 1        TMEM allocator and MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::f16,
+//                 M = 128, N = 64, K = 16, from shared-memory descriptors (no-swizzle K-major core
+//                 matrices), commits to mbarriers;
+//   warps 4-7     epilogue: tcgen05.ld of the accumulators (one TMEM lane = one weight row per
+//                 thread), d scaling, output or K-split partial;
+//   warps 8-15    dequantisation: raw tile bytes (shared memory) -> fp16 A operand in the core-
+//                 matrix layout the MMA reads.
+// Half super-blocks (K = 128) are double-buffered; accumulators are double-buffered in TMEM.  A
+// 128-row tile whose super-blocks are split between CTAs is finished by the last CTA to arrive,
+// which adds the partials in CTA order (deterministic).  Every wait is bounded (%globaltimer).
+#include "engine.cuh"
+#include "gemm_tc.cuh"
+#include "gemv.cuh"
+#include "gemv_tile.cuh"
+
+namespace llmdot {
+
+namespace {
+
+constexpr int TC_THREADS = 512;
+constexpr int TM = 128, TN = 64, HK = 128;
+constexpr uint32_t A_BYTES = TM * HK * 2;          // 32768: one fp16 A operand of a half super-block
+constexpr uint32_t B_BYTES = TN * HK * 2;          // 16384
+constexpr uint32_t STAGE = 2 * A_BYTES + B_BYTES;  // A (hi), A lo (Q6_K), B
+constexpr uint32_t RAW_SLOT = 8 * Q6K_TILE;        // eight 16-row tiles of one super-block
+constexpr uint32_t AM_BYTES = TM * 16 * 2;         // Q4_K offset-term A operand (K = 16)
+constexpr uint32_t BM_BYTES = TN * 16 * 2;
+constexpr uint32_t B4_SB = 2 * B_BYTES + BM_BYTES;  // prepared B per super-block, Q4_K layout
+constexpr uint32_t B6_SB = 2 * B_BYTES;             // Q6_K layout
+constexpr uint32_t OFF_RAW = 2 * STAGE;
+constexpr uint32_t OFF_AM = OFF_RAW + 2 * RAW_SLOT;
+constexpr uint32_t OFF_BM = OFF_AM + 2 * AM_BYTES;
+constexpr uint32_t OFF_DSM = OFF_BM + 2 * BM_BYTES;
+constexpr uint32_t OFF_BAR = OFF_DSM + 2 * TM * 4;
+constexpr int NBAR = 16;
+constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 64;
+static_assert(SMEM_BYTES <= 227 * 1024, "tensor-core matmul: shared memory");
+constexpr int TMEM_COLS = 256;  // two main accumulators (64 columns each) + the Q4_K offset term
+constexpr float S_FAC = 1.0f / 64.0f;  // sub-block sums (< 2^20) scaled into fp16 range
+constexpr float C_FAC = 256.0f;        // offset coefficients scaled up (their lo half stays normal)
+constexpr unsigned long long TC_WAIT_NS = 2000000000ull;
+
+enum {
+    B_RAW_FULL = 0, B_RAW_EMPTY = 2, B_A_FULL = 4, B_B_FULL = 6, B_ST_EMPTY = 8, B_ACC_FULL = 10, B_ACC_EMPTY = 12,
+    B_ACCM_EMPTY = 14, B_DRAIN = 15
+};
+
+struct TcArgs {
+    const uint8_t *w[3];
+    float *y[3];
+    int ldy[3], rows[3], qt[3], nrt16[3], cum[4];  // cum: first 128-row tile of each segment
+    int nseg, nsb, U, nv, mode;
+    const uint8_t *b4, *b6;
+    const float *isc;
+    float *part;
+    int *cnt;
+    int *err;
+};
+
+__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ uint64_t gtime()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void bar_init(uint64_t *b, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint64_t *b)
+{
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint64_t *b, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint64_t *b, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity), "r"(200000u)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *b)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     su32(dst)),
+                 "l"(src), "r"(bytes), "r"(su32(b))
+                 : "memory");
+}
+// shared-memory matrix descriptor: no swizzle, K-major core matrices of 8 rows x 16 bytes; lbo =
+// byte distance of K-adjacent core matrices, sbo = of 8-row groups; bit 46 = descriptor version 1
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo)
+{
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// kind::f16 instruction descriptor: fp32 accumulator, fp16 A and B, both K-major, N = 64, M = 128
+constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t da, uint64_t db, uint32_t acc)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(da), "l"(db), "r"(IDESC), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t *b)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 64 consecutive fp32 TMEM columns of this thread's lane
+__device__ __forceinline__ void tmem_ld64(uint32_t ta, float (&f)[64])
+{
+    uint32_t v[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,"
+        "%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]), "=r"(v[32]),
+          "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]), "=r"(v[40]),
+          "=r"(v[41]), "=r"(v[42]), "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]), "=r"(v[48]),
+          "=r"(v[49]), "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]), "=r"(v[56]),
+          "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
+        : "r"(ta));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 64; i++) f[i] = __uint_as_float(v[i]);
+}
+
+__device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// The CTA whose unit range holds unit u (ranges [c U / G, (c + 1) U / G)).
+__device__ __forceinline__ int cta_of(long long u, int U, int G) { return (int)(((u + 1) * G + U - 1) / U) - 1; }
+
+struct Unit {
+    int seg, rt, gt, sb, qt;
+    bool first, last;
+};
+
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcArgs a)
+{
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int u0 = (int)((long long)c * a.U / G), u1 = (int)((long long)(c + 1) * a.U / G), n = u1 - u0;
+    uint64_t *bars = (uint64_t *)(smem + OFF_BAR);
+    uint32_t *tmem_slot = (uint32_t *)(smem + OFF_MISC);
+    volatile int *abort_f = (volatile int *)(smem + OFF_MISC + 4);
+    volatile int *last_f = (volatile int *)(smem + OFF_MISC + 8);
+    float *dsm = (float *)(smem + OFF_DSM);
+    const int nsb = a.nsb;
+
+    auto unit = [&](int i) {
+        Unit U;
+        const int u = u0 + i;
+        U.gt = u / nsb;
+        U.sb = u % nsb;
+        int s = 0;
+        while (s + 1 < a.nseg && U.gt >= a.cum[s + 1]) s++;
+        U.seg = s;
+        U.rt = U.gt - a.cum[s];
+        U.qt = a.qt[s];
+        U.first = i == 0 || U.sb == 0;
+        U.last = i == n - 1 || U.sb == nsb - 1;
+        return U;
+    };
+    // bounded wait; gives up on another role's abort as well
+    auto wait = [&](int bi, uint32_t parity) -> bool {
+        uint64_t *b = bars + bi;
+        if (bar_try(b, parity)) return true;
+        const uint64_t t0 = gtime();
+        while (!bar_try(b, parity)) {
+            if (*abort_f || gtime() - t0 > TC_WAIT_NS) {
+                if (!*abort_f) {
+                    *abort_f = 1;
+                    atomicExch(a.err, 5);
+                }
+                return false;
+            }
+        }
+        return true;
+    };
+
+    if (tid == 0) {
+        for (int i = 0; i < NBAR; i++) {
+            const uint32_t cnt = (i == B_RAW_EMPTY || i == B_RAW_EMPTY + 1 || i == B_A_FULL || i == B_A_FULL + 1) ? 8u
+                                 : (i == B_ACC_EMPTY || i == B_ACC_EMPTY + 1 || i == B_ACCM_EMPTY)          ? 4u
+                                                                                                           : 1u;
+            bar_init(bars + i, cnt);
+        }
+        *abort_f = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- producer
+        if (lane == 0 && n > 0) {
+            int raw_issued = 0, b_issued[2] = {0, 0};
+            auto issue_raw = [&](int i) {
+                const Unit U = unit(i);
+                const uint32_t tb = U.qt == QT_Q4K ? Q4K_TILE : Q6K_TILE;
+                const int ntile = min(8, a.nrt16[U.seg] - 8 * U.rt);
+                uint8_t *dst = smem + OFF_RAW + (i & 1) * RAW_SLOT;
+                bar_expect_tx(bars + B_RAW_FULL + (i & 1), ntile * tb);
+                for (int k = 0; k < ntile; k++)
+                    bulk_g2s(dst + k * tb, a.w[U.seg] + ((size_t)(8 * U.rt + k) * nsb + U.sb) * tb, tb,
+                             bars + B_RAW_FULL + (i & 1));
+                raw_issued = i + 1;
+            };
+            issue_raw(0);
+            if (n > 1) issue_raw(1);
+            bool ok = true;
+            for (int i = 0; i < n && ok; i++) {
+                const Unit U = unit(i);
+                const bool q4 = U.qt == QT_Q4K;
+                for (int hf = 0; hf < 2 && ok; hf++) {
+                    if (i >= 1 && !(ok = wait(B_ST_EMPTY + hf, (i - 1) & 1))) break;
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    const uint8_t *src = q4 ? a.b4 + (size_t)U.sb * B4_SB : a.b6 + (size_t)U.sb * B6_SB;
+                    bar_expect_tx(bars + B_B_FULL + hf, B_BYTES + (q4 && hf == 1 ? BM_BYTES : 0));
+                    bulk_g2s(smem + hf * STAGE + 2 * A_BYTES, src + hf * B_BYTES, B_BYTES, bars + B_B_FULL + hf);
+                    if (q4 && hf == 1)
+                        bulk_g2s(smem + OFF_BM + (i & 1) * BM_BYTES, src + 2 * B_BYTES, BM_BYTES, bars + B_B_FULL + 1);
+                    b_issued[hf] = i + 1;
+                }
+                if (ok && i + 2 < n) {
+                    if (!(ok = wait(B_RAW_EMPTY + (i & 1), (i >> 1) & 1))) break;
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue_raw(i + 2);
+                }
+            }
+            if (!ok) {  // bounded drain of the copies this thread issued into shared memory
+                for (int r = 0; r < 2; r++) {
+                    const int last = raw_issued - 1 - ((raw_issued - 1 - r) & 1);  // last unit issued to slot r
+                    if (last >= 0) {
+                        const uint64_t t0 = gtime();
+                        while (!bar_try(bars + B_RAW_FULL + r, (last >> 1) & 1) && gtime() - t0 < TC_WAIT_NS) {}
+                    }
+                    if (b_issued[r] > 0) {
+                        const uint64_t t0 = gtime();
+                        while (!bar_try(bars + B_B_FULL + r, (b_issued[r] - 1) & 1) && gtime() - t0 < TC_WAIT_NS) {}
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0 && n > 0) {
+            int run = 0;
+            bool ok = true;
+            for (int i = 0; i < n && ok; i++) {
+                const Unit U = unit(i);
+                const bool q4 = U.qt == QT_Q4K;
+                const int b = i & 1;
+                if (i >= 2 && !(ok = wait(B_ACC_EMPTY + b, ((i - 2) >> 1) & 1))) break;
+                for (int hf = 0; hf < 2 && ok; hf++) {
+                    if (!(ok = wait(B_A_FULL + hf, i & 1)) || !(ok = wait(B_B_FULL + hf, i & 1))) break;
+                    tc_fence_after();
+                    const uint32_t A = su32(smem + hf * STAGE), B = A + 2 * A_BYTES;
+#pragma unroll 1
+                    for (int kk = 0; kk < HK / 16; kk++) {
+                        const uint64_t db = sdesc(B + kk * 256, 128, 2048);
+                        umma(tmem + b * 64, sdesc(A + kk * 256, 128, 2048), db, (hf | kk) != 0);
+                        if (!q4) umma(tmem + b * 64, sdesc(A + A_BYTES + kk * 256, 128, 2048), db, 1u);
+                    }
+                    if (q4 && hf == 1) {
+                        if (U.first && run >= 1 && !(ok = wait(B_ACCM_EMPTY, (run - 1) & 1))) break;
+                        tc_fence_after();
+                        umma(tmem + 128, sdesc(su32(smem + OFF_AM + b * AM_BYTES), 128, 256),
+                             sdesc(su32(smem + OFF_BM + b * BM_BYTES), 128, 256), U.first ? 0u : 1u);
+                    }
+                    umma_commit(bars + B_ST_EMPTY + hf);
+                }
+                if (!ok) break;
+                umma_commit(bars + B_ACC_FULL + b);
+                if (U.last) run++;
+            }
+            // every MMA issued so far completes before the TMEM is released
+            umma_commit(bars + B_DRAIN);
+            const uint64_t t0 = gtime();
+            while (!bar_try(bars + B_DRAIN, 0) && gtime() - t0 < TC_WAIT_NS) {}
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------------------------------------------------------- epilogue
+        const int e = warp - 4, row = 32 * e + lane, te = tid - 128;
+        float acc[TC_MAX_ROWS];
+#pragma unroll
+        for (int t = 0; t < TC_MAX_ROWS; t++) acc[t] = 0.0f;
+        int run = 0, run_sb0 = 0;
+        for (int i = 0; i < n; i++) {
+            const Unit U = unit(i);
+            const int b = i & 1;
+            if (U.first) run_sb0 = U.sb;
+            if (!wait(B_ACC_FULL + b, (i >> 1) & 1)) break;
+            tc_fence_after();
+            float v[64];
+            tmem_ld64(tmem + ((uint32_t)(32 * e) << 16) + b * 64, v);
+            const float d = dsm[b * TM + row];
+#pragma unroll
+            for (int t = 0; t < TC_MAX_ROWS; t++) acc[t] = fmaf(d, v[t] + v[t + 32], acc[t]);
+            if (U.last && U.qt == QT_Q4K) {
+                tmem_ld64(tmem + ((uint32_t)(32 * e) << 16) + 128, v);
+#pragma unroll
+                for (int t = 0; t < TC_MAX_ROWS; t++) acc[t] -= (v[t] + v[t + 32]) * (1.0f / (C_FAC * S_FAC));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                bar_arrive(bars + B_ACC_EMPTY + b);
+                if (U.last) bar_arrive(bars + B_ACCM_EMPTY);
+            }
+            if (!U.last) continue;
+            // ---- a 128-row tile (or this CTA's share of its super-blocks) is complete
+            const int s = U.seg, rowg = 128 * U.rt + row;
+            const bool whole = run_sb0 == 0 && U.sb == nsb - 1;
+            float *y = a.y[s];
+            if (whole) {
+                if (rowg < a.rows[s])
+#pragma unroll
+                    for (int t = 0; t < TC_MAX_ROWS; t++) {
+                        if (t >= a.nv) break;
+                        const float val = acc[t] * __ldg(a.isc + t);
+                        float *yp = y + (size_t)t * a.ldy[s] + rowg;
+                        *yp = a.mode == GEMV_ADD ? __fadd_rn(*yp, val) : val;
+                    }
+            } else {
+                float *pp = a.part + ((size_t)(c * 2 + (run == 0 ? 0 : 1)) * TC_MAX_ROWS) * TM;
+#pragma unroll
+                for (int t = 0; t < TC_MAX_ROWS; t++) pp[t * TM + row] = acc[t];
+                __threadfence();
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                const long long ub = (long long)U.gt * nsb;
+                const int c_lo = cta_of(ub, a.U, G), c_hi = cta_of(ub + nsb - 1, a.U, G);
+                if (te == 0) {
+                    const int old = atomicAdd(a.cnt + U.gt, 1);
+                    *last_f = old == c_hi - c_lo;
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (*last_f) {
+                    __threadfence();
+                    float tot[TC_MAX_ROWS];
+#pragma unroll
+                    for (int t = 0; t < TC_MAX_ROWS; t++) tot[t] = 0.0f;
+                    for (int cc = c_lo; cc <= c_hi; cc++) {
+                        const int first_gt = (int)((long long)cc * a.U / G) / nsb;
+                        const float *qp = a.part + ((size_t)(cc * 2 + (first_gt == U.gt ? 0 : 1)) * TC_MAX_ROWS) * TM;
+#pragma unroll
+                        for (int t = 0; t < TC_MAX_ROWS; t++) tot[t] += __ldcg(qp + t * TM + row);
+                    }
+                    if (rowg < a.rows[s])
+#pragma unroll
+                        for (int t = 0; t < TC_MAX_ROWS; t++) {
+                            if (t >= a.nv) break;
+                            const float val = tot[t] * __ldg(a.isc + t);
+                            float *yp = y + (size_t)t * a.ldy[s] + rowg;
+                            *yp = a.mode == GEMV_ADD ? __fadd_rn(*yp, val) : val;
+                        }
+                    if (te == 0) a.cnt[U.gt] = 0;
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+            }
+#pragma unroll
+            for (int t = 0; t < TC_MAX_ROWS; t++) acc[t] = 0.0f;
+            run++;
+        }
+    } else if (warp >= 8) {
+        // ---------------------------------------------------------------- dequantisation
+        const int dt = tid - 256, rt8 = dt >> 5, L = dt & 31, g = L >> 2, t = L & 3;
+        for (int i = 0; i < n; i++) {
+            const Unit U = unit(i);
+            const int b = i & 1;
+            if (!wait(B_RAW_FULL + b, (i >> 1) & 1)) break;
+            if (i >= 2 && !wait(B_ACC_EMPTY + b, ((i - 2) >> 1) & 1)) break;
+            const bool q4 = U.qt == QT_Q4K;
+            const uint8_t *raw = smem + OFF_RAW + b * RAW_SLOT + rt8 * (q4 ? Q4K_TILE : Q6K_TILE);
+            bool ok = true;
+            for (int hf = 0; hf < 2; hf++) {
+                if (i >= 1 && !(ok = wait(B_ST_EMPTY + hf, (i - 1) & 1))) break;
+                uint8_t *A = smem + hf * STAGE;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int row = 16 * rt8 + g + 8 * h;
+                    uint8_t *arow = A + (row >> 3) * 2048 + (row & 7) * 16;
+                    if (q4) {
+                        // rows g + 8h, sub-block j = 4 hf + t: 32 nibbles as four 8-weight core rows
+                        const int j = 4 * hf + t;
+                        const uint4 W = *(const uint4 *)(raw + ((j & 1) + 2 * h) * 512 + (4 * g + (j >> 1)) * 16);
+                        const uint4 hd = *(const uint4 *)(raw + 2048 + g * 32 + h * 16);
+                        const int bit = 12 * j, wi = bit >> 5;
+                        const uint32_t lo = wi == 0 ? hd.y : (wi == 1 ? hd.z : hd.w);
+                        const uint32_t hi = wi == 0 ? hd.z : hd.w;
+                        const uint32_t pr = __funnelshift_r(lo, hi, bit & 31);
+                        const uint32_t sc = pr & 63u, mm = (pr >> 6) & 63u;
+                        const uint32_t sc2 = hsub2(0x64006400u | (sc * 0x10001u), 0x64006400u);
+                        const uint32_t nsc2 = hfma2(sc2, 0xE400E400u, 0u);   // * -1024
+                        const uint32_t sc16 = hfma2(sc2, 0x2C002C00u, 0u);   // * 1/16
+                        const uint32_t nsc16 = hfma2(sc2, 0xD400D400u, 0u);  // * -64
+                        const uint32_t Ws[4] = {W.x, W.y, W.z, W.w};
+#pragma unroll
+                        for (int i4 = 0; i4 < 4; i4++) {
+                            const uint32_t w = Ws[i4], w8 = w >> 8;
+                            uint4 o;
+                            o.x = hfma2(and_or(w, 0x000F000Fu, 0x64006400u), sc2, nsc2);
+                            o.y = hfma2(and_or(w, 0x00F000F0u, 0x64006400u), sc16, nsc16);
+                            o.z = hfma2(and_or(w8, 0x000F000Fu, 0x64006400u), sc2, nsc2);
+                            o.w = hfma2(and_or(w8, 0x00F000F0u, 0x64006400u), sc16, nsc16);
+                            *(uint4 *)(arow + (4 * t + i4) * 128) = o;
+                        }
+                        // offset coefficient of sub-block j as an fp16 hi/lo pair (K = 2j, 2j + 1)
+                        const float dd = half_bits(hd.x & 0xFFFF), dm = half_bits(hd.x >> 16);
+                        const float cf = fmaf(8.0f * dd, (float)sc, dm * (float)mm) * C_FAC;
+                        const __half2 ch = __floats2half2_rn(cf, 0.0f);
+                        const float chf = __low2float(ch);
+                        const __half2 pair = __halves2half2(__low2half(ch), __float2half_rn(cf - chf));
+                        *(uint32_t *)(smem + OFF_AM + b * AM_BYTES + (row >> 3) * 256 + (j >> 2) * 128 + (row & 7) * 16 +
+                                      (j & 3) * 4) = half2_bits(pair);
+                        if (hf == 0 && t == 0) dsm[b * TM + row] = dd;
+                    } else {
+                        // rows g + 8h, this lane's 4-element groups of sub-blocks 2w, 2w + 1 (w = 4 hf .. 4 hf + 3)
+                        const uint4 LW = *(const uint4 *)(raw + (3 * h + hf) * 512 + L * 16);
+                        const uint4 HU = *(const uint4 *)(raw + (3 * h + 2) * 512 + L * 16);
+                        const uint4 SC = *(const uint4 *)(raw + 3072 + g * 32 + h * 16);
+                        const uint32_t Lw4[4] = {LW.x, LW.y, LW.z, LW.w}, Hu4[4] = {HU.x, HU.y, HU.z, HU.w};
+                        const uint32_t SC4[4] = {SC.x, SC.y, SC.z, SC.w};
+#pragma unroll
+                        for (int w4 = 0; w4 < 4; w4++) {
+                            const int w = 4 * hf + w4;
+                            const uint32_t Lw = Lw4[w4], Hu = Hu4[w >> 1];
+                            uint32_t ohi[4], olo[4];
+#pragma unroll
+                            for (int k = 0; k < 4; k++) {
+                                uint32_t hb;
+                                if ((w & 1) == 0) hb = Hu >> (2 * k);
+                                else hb = k == 0 ? (Hu << 4) : k == 1 ? (Hu << 2) : k == 2 ? (Hu >> 8) : (Hu >> 10);
+                                const uint32_t qv = and_or(hb, 0x00300030u, and_or(Lw >> (4 * k), 0x000F000Fu, 0x64006400u));
+                                const uint32_t p = hsub2(qv, 0x64206420u);  // q - 32, exact
+                                const int s = 2 * w + (k >> 1);
+                                const int scv = (int)(int8_t)(SC4[s >> 2] >> (8 * (s & 3)));
+                                const __half sh = __int2half_rn(scv);  // |sc| <= 128: exact
+                                const uint32_t sc2 = half2_bits(__halves2half2(sh, sh));
+                                uint32_t hv;
+                                asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(hv) : "r"(p), "r"(sc2));
+                                ohi[k] = hv;
+                                olo[k] = hfma2(p, sc2, hv ^ 0x80008000u);  // exact residual of the product
+                            }
+                            const int kc = 4 * w4 + t;
+                            *(uint4 *)(arow + kc * 128) = make_uint4(ohi[0], ohi[1], ohi[2], ohi[3]);
+                            *(uint4 *)(arow + A_BYTES + kc * 128) = make_uint4(olo[0], olo[1], olo[2], olo[3]);
+                        }
+                        if (hf == 0 && t == 0) dsm[b * TM + row] = half_bits(*(const uint16_t *)(raw + 3328 + g * 4 + h * 2));
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) bar_arrive(bars + B_A_FULL + hf);
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) bar_arrive(bars + B_RAW_EMPTY + b);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+}
+
+// ------------------------------------------------------------------ input operands
+// One CTA per input row v: RMSNorm statistics (optional), an exact power-of-two scale putting
+// max |x| in [2^14, 2^15), then fp16 hi (column v) and lo (column 32 + v) of every element, in the
+// K order of each weight layout; for Q4_K also the sub-block sums as the offset term's B operand.
+__global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ x, int ldx, int nsb,
+                                                      const float *__restrict__ norm_w, float eps, int q4, int q6,
+                                                      uint8_t *__restrict__ b4, uint8_t *__restrict__ b6,
+                                                      float *__restrict__ isc)
+{
+    __shared__ float red[2][8];
+    __shared__ float stat[2];
+    const int v = blockIdx.x, tid = threadIdx.x, cols = nsb * 256;
+    const float *xv = x + (size_t)v * ldx;
+    float ss = 0.0f, mx = 0.0f;
+    for (int i = tid; i < cols; i += 256) {
+        const float h = xv[i];
+        ss = fmaf(h, h, ss);
+        mx = fmaxf(mx, fabsf(norm_w ? __fmul_rn(norm_w[i], h) : h));
+    }
+    ss = warp_sum(ss);
+    mx = warp_max(mx);
+    if ((tid & 31) == 0) {
+        red[0][tid >> 5] = ss;
+        red[1][tid >> 5] = mx;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float s = 0.0f, m = 0.0f;
+        for (int w = 0; w < 8; w++) {
+            s += red[0][w];
+            m = fmaxf(m, red[1][w]);
+        }
+        float iv = 1.0f;
+        if (norm_w) {  // VectorMath.RmsNorm: 1 / sqrt(ss/n + eps); x = (w*h)*inv
+            iv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)cols), eps)));
+            m = __fmul_rn(m, iv);
+        }
+        float sc = 1.0f;
+        if (m > 0.0f && m < INFINITY) {
+            int e;
+            frexpf(m, &e);
+            sc = ldexpf(1.0f, 15 - e);
+        }
+        stat[0] = iv;
+        stat[1] = sc;
+        isc[v] = 1.0f / sc;
+    }
+    __syncthreads();
+    // ((w*h)*inv)*sc == (w*h)*(inv*sc): sc is a power of two
+    const float f = norm_w ? stat[0] * stat[1] : stat[1];
+    auto val = [&](int e) { return norm_w ? __fmul_rn(__fmul_rn(norm_w[e], xv[e]), f) : xv[e] * f; };
+    const int n_hi = v, n_lo = v + 32;
+    const int off_hi = (n_hi >> 3) * 2048 + (n_hi & 7) * 16, off_lo = (n_lo >> 3) * 2048 + (n_lo & 7) * 16;
+    // one core row (8 weights, 16 bytes) per item: (super-block, half, core row kc)
+    for (int it = tid; it < nsb * 32; it += 256) {
+        const int sb = it >> 5, kc32 = it & 31, hf = kc32 >> 4, kc = kc32 & 15;
+        float c[8];
+        if (q4) {  // elements 32 (kc / 4) + 8 (kc % 4) + {0,4,1,5,2,6,3,7} of the half
+            const int e0 = sb * 256 + hf * 128 + 32 * (kc >> 2) + 8 * (kc & 3);
+            float nat[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) nat[k] = val(e0 + k);
+            const int perm[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+#pragma unroll
+            for (int k = 0; k < 8; k++) c[k] = nat[perm[k]];
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const __half2 hh = __floats2half2_rn(c[2 * k], c[2 * k + 1]);
+                const float2 hf2 = __half22float2(hh);
+                hi[k] = half2_bits(hh);
+                lo[k] = pack_half2(c[2 * k] - hf2.x, c[2 * k + 1] - hf2.y);
+            }
+            uint8_t *base = b4 + (size_t)sb * B4_SB + hf * B_BYTES + kc * 128;
+            *(uint4 *)(base + off_hi) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *(uint4 *)(base + off_lo) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+        if (q6) {  // elements 32 w4 + 4 t + {0..3} and 32 w4 + 16 + 4 t + {0..3} of the half (kc = 4 w4 + t)
+            const int e0 = sb * 256 + hf * 128 + 32 * (kc >> 2) + 4 * (kc & 3);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                c[k] = val(e0 + k);
+                c[4 + k] = val(e0 + 16 + k);
+            }
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const __half2 hh = __floats2half2_rn(c[2 * k], c[2 * k + 1]);
+                const float2 hf2 = __half22float2(hh);
+                hi[k] = half2_bits(hh);
+                lo[k] = pack_half2(c[2 * k] - hf2.x, c[2 * k + 1] - hf2.y);
+            }
+            uint8_t *base = b6 + (size_t)sb * B6_SB + hf * B_BYTES + kc * 128;
+            *(uint4 *)(base + off_hi) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *(uint4 *)(base + off_lo) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+    }
+    if (q4) {
+        // sub-block sums S_j (fixed order: four 8-element partials), hi and lo, at K = 2j and 2j + 1
+        for (int it = tid; it < nsb * 8; it += 256) {
+            const int sb = it >> 3, j = it & 7;
+            float p[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                float s = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 8; k++) s += val(sb * 256 + 32 * j + 8 * q + k);
+                p[q] = s;
+            }
+            const float S = (((p[0] + p[1]) + p[2]) + p[3]) * S_FAC;
+            const __half sh = __float2half_rn(S);
+            const __half sl = __float2half_rn(S - __half2float(sh));
+            uint8_t *base = b4 + (size_t)sb * B4_SB + 2 * B_BYTES + (j >> 2) * 128 + (j & 3) * 4;
+            *(uint32_t *)(base + (n_hi >> 3) * 256 + (n_hi & 7) * 16) = half2_bits(__halves2half2(sh, sh));
+            *(uint32_t *)(base + (n_lo >> 3) * 256 + (n_lo & 7) * 16) = half2_bits(__halves2half2(sl, sl));
+        }
+    }
+}
+
+int sm_count()
+{
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+}  // namespace
+
+int tc_scratch_alloc(TcScratch &s, int cols_max, int tiles_max, std::vector<void *> &allocs)
+{
+    const int nsb = (cols_max + 255) / 256;
+    const int grid = sm_count();
+    auto get = [&](void **p, size_t bytes) -> int {
+        if (cudaMalloc(p, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(LLMDOT_E_NOMEM, "tensor-core matmul scratch allocation failed");
+        }
+        allocs.push_back(*p);
+        return LLMDOT_OK;
+    };
+    LLMDOT_TRY(get((void **)&s.b4, (size_t)nsb * B4_SB));
+    LLMDOT_TRY(get((void **)&s.b6, (size_t)nsb * B6_SB));
+    LLMDOT_TRY(get((void **)&s.isc, sizeof(float) * TC_MAX_ROWS));
+    LLMDOT_TRY(get((void **)&s.part, sizeof(float) * (size_t)grid * 2 * TC_MAX_ROWS * TM));
+    LLMDOT_TRY(get((void **)&s.cnt, sizeof(int) * (size_t)tiles_max));
+    LLMDOT_CUDA_TRY(cudaMemset(s.cnt, 0, sizeof(int) * (size_t)tiles_max));
+    // stale columns of unused input rows must not hold NaN bit patterns that the MMA would read as
+    // values of live columns: every column is independent, so zeroing once is only for tidiness
+    LLMDOT_CUDA_TRY(cudaMemset(s.b4, 0, (size_t)nsb * B4_SB));
+    LLMDOT_CUDA_TRY(cudaMemset(s.b6, 0, (size_t)nsb * B6_SB));
+    s.cols_max = nsb * 256;
+    s.grid_max = grid;
+    s.tiles_max = tiles_max;
+    return LLMDOT_OK;
+}
+
+bool tc_supported(const DevMat &W)
+{
+    return W.tiled && (W.type == T_Q4_K || W.type == T_Q6_K) && W.cols % 256 == 0;
+}
+
+int tc_prepare(const float *x, int ldx, int nv, int cols, const float *norm_w, float eps, bool q4, bool q6,
+               TcScratch &s, cudaStream_t st)
+{
+    if (!s.ready() || nv < 1 || nv > TC_MAX_ROWS || cols % 256 || cols > s.cols_max)
+        return fail(LLMDOT_E_INVALID, "tensor-core matmul: bad input shape");
+    tc_prep_kernel<<<nv, 256, 0, st>>>(x, ldx, cols / 256, norm_w, eps, q4 ? 1 : 0, q6 ? 1 : 0, s.b4, s.b6, s.isc);
+    LLMDOT_CUDA_TRY(cudaGetLastError());
+    return LLMDOT_OK;
+}
+
+int tc_gemm(const TcSeg *seg, int nseg, int nv, int mode, TcScratch &s, int *err, cudaStream_t st)
+{
+    if (!s.ready() || nseg < 1 || nseg > 3 || nv < 1 || nv > TC_MAX_ROWS || (mode != GEMV_STORE && mode != GEMV_ADD))
+        return fail(LLMDOT_E_INVALID, "tensor-core matmul: bad arguments");
+    TcArgs a{};
+    a.nseg = nseg;
+    a.nsb = seg[0].W->cols / 256;
+    a.nv = nv;
+    a.mode = mode;
+    int tiles = 0;
+    for (int i = 0; i < nseg; i++) {
+        const DevMat &W = *seg[i].W;
+        if (!tc_supported(W) || W.cols != seg[0].W->cols || W.cols > s.cols_max)
+            return fail(LLMDOT_E_UNSUPPORTED, "tensor-core matmul: unsupported matrix");
+        a.w[i] = W.tiled;
+        a.y[i] = seg[i].y;
+        a.ldy[i] = seg[i].ldy;
+        a.rows[i] = W.rows;
+        a.qt[i] = W.type == T_Q4_K ? QT_Q4K : QT_Q6K;
+        a.nrt16[i] = (W.rows + 15) / 16;
+        a.cum[i] = tiles;
+        tiles += (W.rows + TM - 1) / TM;
+    }
+    a.cum[nseg] = tiles;
+    if (tiles > s.tiles_max) return fail(LLMDOT_E_UNSUPPORTED, "tensor-core matmul: more row tiles than scratch");
+    a.U = tiles * a.nsb;
+    a.b4 = s.b4;
+    a.b6 = s.b6;
+    a.isc = s.isc;
+    a.part = s.part;
+    a.cnt = s.cnt;
+    a.err = err;
+    const int grid = a.U < s.grid_max ? a.U : s.grid_max;
+    static std::atomic<unsigned long long> attr_done{0};
+    LLMDOT_CUDA_TRY(smem_attr_once(attr_done, tc_gemm_kernel, (int)SMEM_BYTES));
+    tc_gemm_kernel<<<grid, TC_THREADS, SMEM_BYTES, st>>>(a);
+    LLMDOT_CUDA_TRY(cudaGetLastError());
+    return LLMDOT_OK;
+}
+
+}  // namespace llmdot

@@ -311,8 +311,17 @@ EXPORT int orc_dequantize(const uint8_t *src, float *dst, uint32_t type, int num
 /* ------------------------------------------------------------------------ */
 /* 8-lane helpers */
 
-/* Vector.Dot(acc, Vector<float>.One): see header for the assumed tree order. */
-static float hsum8(const float *v) { return ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7])); }
+/* Vector.Dot(acc, Vector<float>.One): see header for the assumed tree order.  The order is the
+ * one thing the reference's source leaves to the JIT and the host's vector unit; a diagnostic
+ * switch (orc_set_hsum_order(1)) sums the lanes left to right instead, to measure how far the
+ * reference algorithm's own result moves when only that order changes. */
+static int g_hsum_order = 0;
+EXPORT void orc_set_hsum_order(int order) { g_hsum_order = order; }
+static float hsum8(const float *v)
+{
+    if (g_hsum_order == 1) return ((((((v[0] + v[1]) + v[2]) + v[3]) + v[4]) + v[5]) + v[6]) + v[7];
+    return ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+}
 
 /* TensorOps.DotProduct -- TensorOps.cs:510-531 */
 static float dot_product(const float *a, const float *b, int n)

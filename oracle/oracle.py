@@ -78,6 +78,7 @@ def lib():
         L.orc_rope.argtypes = [F32P, F32P, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_set_kv_fp16.argtypes = [C.c_int]
+        L.orc_set_hsum_order.argtypes = [C.c_int]
         L.orc_last_error.restype = C.c_char_p
         L.orc_model_load.restype = C.c_void_p
         L.orc_model_load.argtypes = [C.c_char_p]
@@ -130,6 +131,12 @@ def set_threads(n: int) -> None:
 def set_kv_fp16(on: bool) -> None:
     """Diagnostic: round cached K/V to fp16 (what a device fp16 KV cache stores)."""
     lib().orc_set_kv_fp16(1 if on else 0)
+
+
+def set_hsum_order(order: int) -> None:
+    """Diagnostic: 0 sums the 8 vector lanes as the pairwise tree the oracle assumes for the
+    reference's Vector.Dot, 1 left to right (the order the reference's source does not fix)."""
+    lib().orc_set_hsum_order(int(order))
 
 
 def max_threads() -> int:

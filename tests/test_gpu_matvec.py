@@ -53,7 +53,7 @@ def test_matvec_every_weight(oracle, name, nv):
 @pytest.mark.parametrize("name", ["micro", "micro-phi3", "tiny"])
 @pytest.mark.parametrize("nv", [5, 8, 13, 32])
 def test_matmul_batched_every_weight(oracle, name, nv):
-    """5..32 input rows: the batched tensor-core kernel (gemm.cu) on every Q4_K / Q6_K matrix."""
+    """5..32 input rows: the batched tensor-core kernel (gemm_tc.cu) on every Q4_K / Q6_K matrix."""
     m, f = loaded(name)
     rng = np.random.default_rng(100 + nv)
     for tname, info in f.tensors.items():
