@@ -310,9 +310,9 @@ __device__ __forceinline__ bool ac_mbar_wait(uint64_t *b, uint32_t parity)
     uint64_t t0 = 0;
     for (int it = 0;; it++) {
         asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(ok)
-            : "r"(smem_u32(b)), "r"(parity), "r"(1000000u)
+            : "r"(smem_u32(b)), "r"(parity)
             : "memory");
         if (ok) return true;
         uint64_t now;

@@ -419,11 +419,11 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
             LLMDOT_TRY(tc_prepare(x, ldx, batch, W.cols, norm_w, c.eps, q4, q6, w.tc, st));
             if (mode == GEMV_SILU_MUL || mode == GEMV_GELU_MUL) {
                 const TcSeg sg[2] = {{&W, w.gate, c.ffn}, {W1, w.up, c.ffn}};
-                LLMDOT_TRY(tc_gemm(sg, 2, batch, GEMV_STORE, w.tc, w.err, st));
+                LLMDOT_TRY(tc_gemm(sg, 2, batch, GEMV_STORE, w.tc, w.err, st, pf));
                 return launch_act_mul(mode == GEMV_GELU_MUL, w.gate, w.up, y, c.ffn, batch, st);
             }
             const TcSeg sg = {&W, y, ldy};
-            return tc_gemm(&sg, 1, batch, mode == GEMV_ADD ? GEMV_ADD : GEMV_STORE, w.tc, w.err, st);
+            return tc_gemm(&sg, 1, batch, mode == GEMV_ADD ? GEMV_ADD : GEMV_STORE, w.tc, w.err, st, pf);
         }
         const float *xin = x;
         int ld = ldx;
@@ -492,7 +492,7 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
                 }
                 LLMDOT_TRY(tc_prepare(w.h, H, batch, H, L.attn_norm, c.eps, q4, q6, w.tc, st));
                 const TcSeg sg[3] = {{&L.q, w.q, qDim}, {&L.k, w.k, kvDim}, {&L.v, w.v, kvDim}};
-                LLMDOT_TRY(tc_gemm(sg, 3, batch, GEMV_STORE, w.tc, w.err, st));
+                LLMDOT_TRY(tc_gemm(sg, 3, batch, GEMV_STORE, w.tc, w.err, st, &pf_o));
                 qkv_rc = LLMDOT_OK;
             }
             if (qkv_rc != LLMDOT_OK) {

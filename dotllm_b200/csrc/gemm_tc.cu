@@ -18,7 +18,7 @@
 // Kernel structure (one CTA of 16 warps per SM, persistent over a contiguous range of work units;
 // a unit is one 128-row tile x one 256-weight super-block):
 //   warp 0        producer: cp.async.bulk of the raw 16-row weight tiles (already tiled at model
-//                 load) into a 2-slot ring, and of the prepared B operand per half super-block;
+//                 load) into a 4-slot ring, and of the prepared B operand per quarter super-block;
 //   warp 1        TMEM allocator and MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::f16,
 //                 M = 128, N = 64, K = 16, from shared-memory descriptors (no-swizzle K-major core
 //                 matrices), commits to mbarriers;
@@ -26,7 +26,8 @@
 //                 thread), d scaling, output or K-split partial;
 //   warps 8-15    dequantisation: raw tile bytes (shared memory) -> fp16 A operand in the core-
 //                 matrix layout the MMA reads.
-// Half super-blocks (K = 128) are double-buffered; accumulators are double-buffered in TMEM.  A
+// Quarter super-blocks (K = 64) are double-buffered, four raw super-blocks are in flight (and the next
+// eight are prefetched into L2); accumulators are double-buffered in TMEM.  A
 // 128-row tile whose super-blocks are split between CTAs is finished by the last CTA to arrive,
 // which adds the partials in CTA order (deterministic).  Every wait is bounded (%globaltimer).
 #include "engine.cuh"
@@ -39,21 +40,23 @@ namespace llmdot {
 namespace {
 
 constexpr int TC_THREADS = 512;
-constexpr int TM = 128, TN = 64, HK = 128;
-constexpr uint32_t A_BYTES = TM * HK * 2;          // 32768: one fp16 A operand of a half super-block
-constexpr uint32_t B_BYTES = TN * HK * 2;          // 16384
-constexpr uint32_t STAGE = 2 * A_BYTES + B_BYTES;  // A (hi), A lo (Q6_K), B
-constexpr uint32_t RAW_SLOT = 8 * Q6K_TILE;        // eight 16-row tiles of one super-block
-constexpr uint32_t AM_BYTES = TM * 16 * 2;         // Q4_K offset-term A operand (K = 16)
+constexpr int TM = 128, TN = 64, QK = 64;           // tile rows, MMA N, K per pipeline stage (quarter super-block)
+constexpr uint32_t A_BYTES = TM * QK * 2;           // 16384: one fp16 A operand of a quarter super-block
+constexpr uint32_t B_BYTES = TN * QK * 2;           // 8192
+constexpr uint32_t STAGE = 2 * A_BYTES + B_BYTES;   // A (hi), A lo (Q6_K), B
+constexpr int NSTAGE = 3;
+constexpr int NRAW = 3;                             // raw super-block slots (units in flight)
+constexpr uint32_t RAW_SLOT = 8 * Q6K_TILE;         // eight 16-row tiles of one super-block
+constexpr uint32_t AM_BYTES = TM * 16 * 2;          // Q4_K offset-term A operand (K = 16)
 constexpr uint32_t BM_BYTES = TN * 16 * 2;
-constexpr uint32_t B4_SB = 2 * B_BYTES + BM_BYTES;  // prepared B per super-block, Q4_K layout
-constexpr uint32_t B6_SB = 2 * B_BYTES;             // Q6_K layout
-constexpr uint32_t OFF_RAW = 2 * STAGE;
-constexpr uint32_t OFF_AM = OFF_RAW + 2 * RAW_SLOT;
+constexpr uint32_t B4_SB = 4 * B_BYTES + BM_BYTES;  // prepared B per super-block, Q4_K layout
+constexpr uint32_t B6_SB = 4 * B_BYTES;             // Q6_K layout
+constexpr uint32_t OFF_RAW = NSTAGE * STAGE;
+constexpr uint32_t OFF_AM = OFF_RAW + NRAW * RAW_SLOT;
 constexpr uint32_t OFF_BM = OFF_AM + 2 * AM_BYTES;
 constexpr uint32_t OFF_DSM = OFF_BM + 2 * BM_BYTES;
 constexpr uint32_t OFF_BAR = OFF_DSM + 2 * TM * 4;
-constexpr int NBAR = 16;
+constexpr int NBAR = 48;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 64;
 static_assert(SMEM_BYTES <= 227 * 1024, "tensor-core matmul: shared memory");
@@ -63,9 +66,11 @@ constexpr float C_FAC = 256.0f;        // offset coefficients scaled up (their l
 constexpr unsigned long long TC_WAIT_NS = 2000000000ull;
 
 enum {
-    B_RAW_FULL = 0, B_RAW_EMPTY = 2, B_A_FULL = 4, B_B_FULL = 6, B_ST_EMPTY = 8, B_ACC_FULL = 10, B_ACC_EMPTY = 12,
-    B_ACCM_EMPTY = 14, B_DRAIN = 15
+    B_RAW_FULL = 0, B_A_FULL = B_RAW_FULL + 8 * NRAW, B_B_FULL = B_A_FULL + NSTAGE,
+    B_ST_EMPTY = B_B_FULL + NSTAGE, B_ACC_FULL = B_ST_EMPTY + NSTAGE, B_ACC_EMPTY = B_ACC_FULL + 2,
+    B_ACCM_EMPTY = B_ACC_EMPTY + 2, B_DRAIN = B_ACCM_EMPTY + 1, B_COUNT = B_DRAIN + 1
 };
+static_assert(B_COUNT <= NBAR, "tensor-core matmul: barrier slots");
 
 struct TcArgs {
     const uint8_t *w[3];
@@ -77,6 +82,7 @@ struct TcArgs {
     float *part;
     int *cnt;
     int *err;
+    GemvPrefetch pf;  // weights of the next operation, pulled into L2 while this one runs
 };
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -102,9 +108,9 @@ __device__ __forceinline__ bool bar_try(uint64_t *b, uint32_t parity)
 {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(su32(b)), "r"(parity), "r"(200000u)
+        : "r"(su32(b)), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -172,6 +178,11 @@ struct Unit {
     bool first, last;
 };
 
+__device__ __forceinline__ void l2_prefetch(const void *src, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcArgs a)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -218,9 +229,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
 
     if (tid == 0) {
         for (int i = 0; i < NBAR; i++) {
-            const uint32_t cnt = (i == B_RAW_EMPTY || i == B_RAW_EMPTY + 1 || i == B_A_FULL || i == B_A_FULL + 1) ? 8u
-                                 : (i == B_ACC_EMPTY || i == B_ACC_EMPTY + 1 || i == B_ACCM_EMPTY)          ? 4u
-                                                                                                           : 1u;
+            uint32_t cnt = 1;
+            if (i >= B_A_FULL && i < B_A_FULL + NSTAGE) cnt = 8;
+            if (i == B_ACC_EMPTY || i == B_ACC_EMPTY + 1 || i == B_ACCM_EMPTY) cnt = 4;
             bar_init(bars + i, cnt);
         }
         *abort_f = 0;
@@ -240,50 +251,47 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     if (warp == 0) {
         // ---------------------------------------------------------------- producer
         if (lane == 0 && n > 0) {
-            int raw_issued = 0, b_issued[2] = {0, 0};
-            auto issue_raw = [&](int i) {
-                const Unit U = unit(i);
-                const uint32_t tb = U.qt == QT_Q4K ? Q4K_TILE : Q6K_TILE;
-                const int ntile = min(8, a.nrt16[U.seg] - 8 * U.rt);
-                uint8_t *dst = smem + OFF_RAW + (i & 1) * RAW_SLOT;
-                bar_expect_tx(bars + B_RAW_FULL + (i & 1), ntile * tb);
-                for (int k = 0; k < ntile; k++)
-                    bulk_g2s(dst + k * tb, a.w[U.seg] + ((size_t)(8 * U.rt + k) * nsb + U.sb) * tb, tb,
-                             bars + B_RAW_FULL + (i & 1));
-                raw_issued = i + 1;
-            };
-            issue_raw(0);
-            if (n > 1) issue_raw(1);
+            int b_issued = 0;
+            // this CTA's share of the next operation's weights into L2
+#pragma unroll
+            for (int r = 0; r < GEMV_PREFETCH_MAX; r++) {
+                const unsigned long long nb = a.pf.n[r];
+                if (!a.pf.p[r] || nb == 0) continue;
+                const unsigned long long share = (nb / G + 15) & ~15ull, lo = (unsigned long long)c * share;
+                if (lo >= nb) continue;
+                unsigned long long len = nb - lo < share ? nb - lo : share;
+                const uint8_t *src = (const uint8_t *)a.pf.p[r] + lo;
+                while (len > 0) {
+                    const uint32_t piece = len > (1u << 20) ? (1u << 20) : (uint32_t)len;
+                    l2_prefetch(src, piece);
+                    src += piece;
+                    len -= piece;
+                }
+            }
             bool ok = true;
             for (int i = 0; i < n && ok; i++) {
                 const Unit U = unit(i);
                 const bool q4 = U.qt == QT_Q4K;
-                for (int hf = 0; hf < 2 && ok; hf++) {
-                    if (i >= 1 && !(ok = wait(B_ST_EMPTY + hf, (i - 1) & 1))) break;
+                const uint8_t *src = q4 ? a.b4 + (size_t)U.sb * B4_SB : a.b6 + (size_t)U.sb * B6_SB;
+                for (int qt = 0; qt < 4 && ok; qt++) {
+                    const int Q = 4 * i + qt, st = Q % NSTAGE;
+                    if (Q >= NSTAGE && !(ok = wait(B_ST_EMPTY + st, (Q / NSTAGE - 1) & 1))) break;
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    const uint8_t *src = q4 ? a.b4 + (size_t)U.sb * B4_SB : a.b6 + (size_t)U.sb * B6_SB;
-                    bar_expect_tx(bars + B_B_FULL + hf, B_BYTES + (q4 && hf == 1 ? BM_BYTES : 0));
-                    bulk_g2s(smem + hf * STAGE + 2 * A_BYTES, src + hf * B_BYTES, B_BYTES, bars + B_B_FULL + hf);
-                    if (q4 && hf == 1)
-                        bulk_g2s(smem + OFF_BM + (i & 1) * BM_BYTES, src + 2 * B_BYTES, BM_BYTES, bars + B_B_FULL + 1);
-                    b_issued[hf] = i + 1;
-                }
-                if (ok && i + 2 < n) {
-                    if (!(ok = wait(B_RAW_EMPTY + (i & 1), (i >> 1) & 1))) break;
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    issue_raw(i + 2);
+                    const bool bm = q4 && qt == 3;
+                    bar_expect_tx(bars + B_B_FULL + st, B_BYTES + (bm ? BM_BYTES : 0));
+                    bulk_g2s(smem + st * STAGE + 2 * A_BYTES, src + qt * B_BYTES, B_BYTES, bars + B_B_FULL + st);
+                    if (bm) bulk_g2s(smem + OFF_BM + (i & 1) * BM_BYTES, src + 4 * B_BYTES, BM_BYTES, bars + B_B_FULL + st);
+                    b_issued = Q + 1;
                 }
             }
             if (!ok) {  // bounded drain of the copies this thread issued into shared memory
-                for (int r = 0; r < 2; r++) {
-                    const int last = raw_issued - 1 - ((raw_issued - 1 - r) & 1);  // last unit issued to slot r
+                for (int st = 0; st < NSTAGE; st++) {
+                    int last = -1;  // last quarter issued to stage st
+                    for (int q = b_issued - 1; q >= 0 && q >= b_issued - NSTAGE; q--)
+                        if (q % NSTAGE == st) last = q;
                     if (last >= 0) {
                         const uint64_t t0 = gtime();
-                        while (!bar_try(bars + B_RAW_FULL + r, (last >> 1) & 1) && gtime() - t0 < TC_WAIT_NS) {}
-                    }
-                    if (b_issued[r] > 0) {
-                        const uint64_t t0 = gtime();
-                        while (!bar_try(bars + B_B_FULL + r, (b_issued[r] - 1) & 1) && gtime() - t0 < TC_WAIT_NS) {}
+                        while (!bar_try(bars + B_B_FULL + st, (last / NSTAGE) & 1) && gtime() - t0 < TC_WAIT_NS) {}
                     }
                 }
             }
@@ -298,23 +306,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 const bool q4 = U.qt == QT_Q4K;
                 const int b = i & 1;
                 if (i >= 2 && !(ok = wait(B_ACC_EMPTY + b, ((i - 2) >> 1) & 1))) break;
-                for (int hf = 0; hf < 2 && ok; hf++) {
-                    if (!(ok = wait(B_A_FULL + hf, i & 1)) || !(ok = wait(B_B_FULL + hf, i & 1))) break;
+                for (int qt = 0; qt < 4 && ok; qt++) {
+                    const int Q = 4 * i + qt, st = Q % NSTAGE;
+                    if (!(ok = wait(B_A_FULL + st, (Q / NSTAGE) & 1)) || !(ok = wait(B_B_FULL + st, (Q / NSTAGE) & 1))) break;
                     tc_fence_after();
-                    const uint32_t A = su32(smem + hf * STAGE), B = A + 2 * A_BYTES;
-#pragma unroll 1
-                    for (int kk = 0; kk < HK / 16; kk++) {
-                        const uint64_t db = sdesc(B + kk * 256, 128, 2048);
-                        umma(tmem + b * 64, sdesc(A + kk * 256, 128, 2048), db, (hf | kk) != 0);
-                        if (!q4) umma(tmem + b * 64, sdesc(A + A_BYTES + kk * 256, 128, 2048), db, 1u);
+                    const uint32_t A = su32(smem + st * STAGE), B = A + 2 * A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < QK / 16; kk++) {
+                        const uint64_t db = sdesc(B + kk * 256, 128, 1024);
+                        umma(tmem + b * 64, sdesc(A + kk * 256, 128, 1024), db, (qt | kk) != 0);
+                        if (!q4) umma(tmem + b * 64, sdesc(A + A_BYTES + kk * 256, 128, 1024), db, 1u);
                     }
-                    if (q4 && hf == 1) {
+                    if (q4 && qt == 3) {
                         if (U.first && run >= 1 && !(ok = wait(B_ACCM_EMPTY, (run - 1) & 1))) break;
                         tc_fence_after();
                         umma(tmem + 128, sdesc(su32(smem + OFF_AM + b * AM_BYTES), 128, 256),
                              sdesc(su32(smem + OFF_BM + b * BM_BYTES), 128, 256), U.first ? 0u : 1u);
                     }
-                    umma_commit(bars + B_ST_EMPTY + hf);
+                    umma_commit(bars + B_ST_EMPTY + st);
                 }
                 if (!ok) break;
                 umma_commit(bars + B_ACC_FULL + b);
@@ -410,67 +419,91 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         }
     } else if (warp >= 8) {
         // ---------------------------------------------------------------- dequantisation
-        const int dt = tid - 256, rt8 = dt >> 5, L = dt & 31, g = L >> 2, t = L & 3;
+        // thread (tile rt8 = warp - 8, lane L); per quarter super-block a warp writes 16-byte core-
+        // matrix rows so that each group of 8 lanes covers 128 contiguous bytes (no bank conflict)
+        const int dt = tid - 256, rt8 = dt >> 5, L = dt & 31;
+        // each warp streams its own 16-row tile of every unit into its part of the raw ring
+        int own_issued = 0;
+        auto issue_own = [&](int k) {
+            if (lane == 0) {
+                const Unit V = unit(k);
+                const uint32_t tb = V.qt == QT_Q4K ? Q4K_TILE : Q6K_TILE;
+                uint64_t *bar = bars + B_RAW_FULL + (k % NRAW) * 8 + rt8;
+                if (8 * V.rt + rt8 < a.nrt16[V.seg]) {
+                    bar_expect_tx(bar, tb);
+                    bulk_g2s(smem + OFF_RAW + (k % NRAW) * RAW_SLOT + rt8 * tb,
+                             a.w[V.seg] + ((size_t)(8 * V.rt + rt8) * nsb + V.sb) * tb, tb, bar);
+                } else {
+                    bar_arrive(bar);  // no such rows: the phase completes without data
+                }
+            }
+            own_issued = k + 1;
+        };
+        for (int k = 0; k < NRAW && k < n; k++) issue_own(k);
         for (int i = 0; i < n; i++) {
             const Unit U = unit(i);
             const int b = i & 1;
-            if (!wait(B_RAW_FULL + b, (i >> 1) & 1)) break;
+            if (!wait(B_RAW_FULL + (i % NRAW) * 8 + rt8, (i / NRAW) & 1)) break;
             if (i >= 2 && !wait(B_ACC_EMPTY + b, ((i - 2) >> 1) & 1)) break;
             const bool q4 = U.qt == QT_Q4K;
-            const uint8_t *raw = smem + OFF_RAW + b * RAW_SLOT + rt8 * (q4 ? Q4K_TILE : Q6K_TILE);
+            const uint8_t *raw = smem + OFF_RAW + (i % NRAW) * RAW_SLOT + rt8 * (q4 ? Q4K_TILE : Q6K_TILE);
             bool ok = true;
-            for (int hf = 0; hf < 2; hf++) {
-                if (i >= 1 && !(ok = wait(B_ST_EMPTY + hf, (i - 1) & 1))) break;
-                uint8_t *A = smem + hf * STAGE;
+            for (int qt = 0; qt < 4; qt++) {
+                const int Q = 4 * i + qt, st = Q % NSTAGE;
+                if (Q >= NSTAGE && !(ok = wait(B_ST_EMPTY + st, (Q / NSTAGE - 1) & 1))) break;
+                uint8_t *A = smem + st * STAGE;
+                if (q4) {
+                    // row r16 = L & 15 of the 16-row tile, sub-block j = 2 qt + (L >> 4): four core rows
+                    const int r16 = L & 15, jj = L >> 4, j = 2 * qt + jj, h = r16 >> 3, g = r16 & 7;
+                    const int row = 16 * rt8 + r16;
+                    uint8_t *arow = A + (row >> 3) * 1024 + (row & 7) * 16;
+                    const uint4 W = *(const uint4 *)(raw + ((j & 1) + 2 * h) * 512 + (4 * g + (j >> 1)) * 16);
+                    const uint4 hd = *(const uint4 *)(raw + 2048 + g * 32 + h * 16);
+                    const int bit = 12 * j, wi = bit >> 5;
+                    const uint32_t lo = wi == 0 ? hd.y : (wi == 1 ? hd.z : hd.w);
+                    const uint32_t hi = wi == 0 ? hd.z : hd.w;
+                    const uint32_t pr = __funnelshift_r(lo, hi, bit & 31);
+                    const uint32_t sc = pr & 63u, mm = (pr >> 6) & 63u;
+                    const uint32_t sc2 = hsub2(0x64006400u | (sc * 0x10001u), 0x64006400u);
+                    const uint32_t nsc2 = hfma2(sc2, 0xE400E400u, 0u);   // * -1024
+                    const uint32_t sc16 = hfma2(sc2, 0x2C002C00u, 0u);   // * 1/16
+                    const uint32_t nsc16 = hfma2(sc2, 0xD400D400u, 0u);  // * -64
+                    const uint32_t Ws[4] = {W.x, W.y, W.z, W.w};
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const int row = 16 * rt8 + g + 8 * h;
-                    uint8_t *arow = A + (row >> 3) * 2048 + (row & 7) * 16;
-                    if (q4) {
-                        // rows g + 8h, sub-block j = 4 hf + t: 32 nibbles as four 8-weight core rows
-                        const int j = 4 * hf + t;
-                        const uint4 W = *(const uint4 *)(raw + ((j & 1) + 2 * h) * 512 + (4 * g + (j >> 1)) * 16);
-                        const uint4 hd = *(const uint4 *)(raw + 2048 + g * 32 + h * 16);
-                        const int bit = 12 * j, wi = bit >> 5;
-                        const uint32_t lo = wi == 0 ? hd.y : (wi == 1 ? hd.z : hd.w);
-                        const uint32_t hi = wi == 0 ? hd.z : hd.w;
-                        const uint32_t pr = __funnelshift_r(lo, hi, bit & 31);
-                        const uint32_t sc = pr & 63u, mm = (pr >> 6) & 63u;
-                        const uint32_t sc2 = hsub2(0x64006400u | (sc * 0x10001u), 0x64006400u);
-                        const uint32_t nsc2 = hfma2(sc2, 0xE400E400u, 0u);   // * -1024
-                        const uint32_t sc16 = hfma2(sc2, 0x2C002C00u, 0u);   // * 1/16
-                        const uint32_t nsc16 = hfma2(sc2, 0xD400D400u, 0u);  // * -64
-                        const uint32_t Ws[4] = {W.x, W.y, W.z, W.w};
+                    for (int i4 = 0; i4 < 4; i4++) {
+                        const uint32_t w = Ws[i4], w8 = w >> 8;
+                        uint4 o;
+                        o.x = hfma2(and_or(w, 0x000F000Fu, 0x64006400u), sc2, nsc2);
+                        o.y = hfma2(and_or(w, 0x00F000F0u, 0x64006400u), sc16, nsc16);
+                        o.z = hfma2(and_or(w8, 0x000F000Fu, 0x64006400u), sc2, nsc2);
+                        o.w = hfma2(and_or(w8, 0x00F000F0u, 0x64006400u), sc16, nsc16);
+                        *(uint4 *)(arow + (4 * jj + i4) * 128) = o;
+                    }
+                    // offset coefficient of sub-block j as an fp16 hi/lo pair (K = 2j, 2j + 1)
+                    const float dd = half_bits(hd.x & 0xFFFF), dm = half_bits(hd.x >> 16);
+                    const float cf = fmaf(8.0f * dd, (float)sc, dm * (float)mm) * C_FAC;
+                    const __half chh = __float2half_rn(cf);
+                    const __half2 pair = __halves2half2(chh, __float2half_rn(cf - __half2float(chh)));
+                    *(uint32_t *)(smem + OFF_AM + b * AM_BYTES + (row >> 3) * 256 + (j >> 2) * 128 + (row & 7) * 16 +
+                                  (j & 3) * 4) = half2_bits(pair);
+                    if (qt == 0 && jj == 0) dsm[b * TM + row] = dd;
+                } else {
+                    // lane (g = L & 7, t = L >> 3) takes tile lane 4g + t: its 4-element groups of
+                    // sub-blocks 2w, 2w + 1 (w = 2 qt, 2 qt + 1) for rows g and g + 8
+                    const int g = L & 7, t = L >> 3, sl = 4 * g + t;
 #pragma unroll
-                        for (int i4 = 0; i4 < 4; i4++) {
-                            const uint32_t w = Ws[i4], w8 = w >> 8;
-                            uint4 o;
-                            o.x = hfma2(and_or(w, 0x000F000Fu, 0x64006400u), sc2, nsc2);
-                            o.y = hfma2(and_or(w, 0x00F000F0u, 0x64006400u), sc16, nsc16);
-                            o.z = hfma2(and_or(w8, 0x000F000Fu, 0x64006400u), sc2, nsc2);
-                            o.w = hfma2(and_or(w8, 0x00F000F0u, 0x64006400u), sc16, nsc16);
-                            *(uint4 *)(arow + (4 * t + i4) * 128) = o;
-                        }
-                        // offset coefficient of sub-block j as an fp16 hi/lo pair (K = 2j, 2j + 1)
-                        const float dd = half_bits(hd.x & 0xFFFF), dm = half_bits(hd.x >> 16);
-                        const float cf = fmaf(8.0f * dd, (float)sc, dm * (float)mm) * C_FAC;
-                        const __half2 ch = __floats2half2_rn(cf, 0.0f);
-                        const float chf = __low2float(ch);
-                        const __half2 pair = __halves2half2(__low2half(ch), __float2half_rn(cf - chf));
-                        *(uint32_t *)(smem + OFF_AM + b * AM_BYTES + (row >> 3) * 256 + (j >> 2) * 128 + (row & 7) * 16 +
-                                      (j & 3) * 4) = half2_bits(pair);
-                        if (hf == 0 && t == 0) dsm[b * TM + row] = dd;
-                    } else {
-                        // rows g + 8h, this lane's 4-element groups of sub-blocks 2w, 2w + 1 (w = 4 hf .. 4 hf + 3)
-                        const uint4 LW = *(const uint4 *)(raw + (3 * h + hf) * 512 + L * 16);
-                        const uint4 HU = *(const uint4 *)(raw + (3 * h + 2) * 512 + L * 16);
+                    for (int h = 0; h < 2; h++) {
+                        const int row = 16 * rt8 + g + 8 * h;
+                        uint8_t *arow = A + (row >> 3) * 1024 + (row & 7) * 16;
+                        const uint4 LW = *(const uint4 *)(raw + (3 * h + (qt >> 1)) * 512 + sl * 16);
+                        const uint4 HU = *(const uint4 *)(raw + (3 * h + 2) * 512 + sl * 16);
                         const uint4 SC = *(const uint4 *)(raw + 3072 + g * 32 + h * 16);
                         const uint32_t Lw4[4] = {LW.x, LW.y, LW.z, LW.w}, Hu4[4] = {HU.x, HU.y, HU.z, HU.w};
                         const uint32_t SC4[4] = {SC.x, SC.y, SC.z, SC.w};
 #pragma unroll
-                        for (int w4 = 0; w4 < 4; w4++) {
-                            const int w = 4 * hf + w4;
-                            const uint32_t Lw = Lw4[w4], Hu = Hu4[w >> 1];
+                        for (int w2 = 0; w2 < 2; w2++) {
+                            const int w = 2 * qt + w2;
+                            const uint32_t Lw = Lw4[w & 3], Hu = Hu4[w >> 1];
                             uint32_t ohi[4], olo[4];
 #pragma unroll
                             for (int k = 0; k < 4; k++) {
@@ -479,29 +512,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                                 else hb = k == 0 ? (Hu << 4) : k == 1 ? (Hu << 2) : k == 2 ? (Hu >> 8) : (Hu >> 10);
                                 const uint32_t qv = and_or(hb, 0x00300030u, and_or(Lw >> (4 * k), 0x000F000Fu, 0x64006400u));
                                 const uint32_t p = hsub2(qv, 0x64206420u);  // q - 32, exact
-                                const int s = 2 * w + (k >> 1);
-                                const int scv = (int)(int8_t)(SC4[s >> 2] >> (8 * (s & 3)));
-                                const __half sh = __int2half_rn(scv);  // |sc| <= 128: exact
-                                const uint32_t sc2 = half2_bits(__halves2half2(sh, sh));
+                                const int sidx = 2 * w + (k >> 1);
+                                const int scv = (int)(int8_t)(SC4[sidx >> 2] >> (8 * (sidx & 3)));
+                                const __half shv = __int2half_rn(scv);  // |sc| <= 128: exact
+                                const uint32_t sc2 = half2_bits(__halves2half2(shv, shv));
                                 uint32_t hv;
                                 asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(hv) : "r"(p), "r"(sc2));
                                 ohi[k] = hv;
                                 olo[k] = hfma2(p, sc2, hv ^ 0x80008000u);  // exact residual of the product
                             }
-                            const int kc = 4 * w4 + t;
+                            const int kc = 4 * w2 + t;
                             *(uint4 *)(arow + kc * 128) = make_uint4(ohi[0], ohi[1], ohi[2], ohi[3]);
                             *(uint4 *)(arow + A_BYTES + kc * 128) = make_uint4(olo[0], olo[1], olo[2], olo[3]);
                         }
-                        if (hf == 0 && t == 0) dsm[b * TM + row] = half_bits(*(const uint16_t *)(raw + 3328 + g * 4 + h * 2));
+                        if (qt == 0 && t == 0) dsm[b * TM + row] = half_bits(*(const uint16_t *)(raw + 3328 + g * 4 + h * 2));
                     }
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) bar_arrive(bars + B_A_FULL + hf);
+                if (lane == 0) bar_arrive(bars + B_A_FULL + st);
             }
             if (!ok) break;
-            __syncwarp();
-            if (lane == 0) bar_arrive(bars + B_RAW_EMPTY + b);
+            __syncwarp();  // every lane is done with this unit's tile: refill the slot
+            if (i + NRAW < n) {
+                if (lane == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue_own(i + NRAW);
+            }
+        }
+        // bounded drain of this warp's copies still in flight (an early exit leaves some)
+        for (int k = own_issued - NRAW < 0 ? 0 : own_issued - NRAW; k < own_issued; k++) {
+            const uint64_t t0 = gtime();
+            while (!bar_try(bars + B_RAW_FULL + (k % NRAW) * 8 + rt8, (k / NRAW) & 1) && gtime() - t0 < TC_WAIT_NS) {}
         }
     }
 
@@ -564,13 +605,13 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
     const float f = norm_w ? stat[0] * stat[1] : stat[1];
     auto val = [&](int e) { return norm_w ? __fmul_rn(__fmul_rn(norm_w[e], xv[e]), f) : xv[e] * f; };
     const int n_hi = v, n_lo = v + 32;
-    const int off_hi = (n_hi >> 3) * 2048 + (n_hi & 7) * 16, off_lo = (n_lo >> 3) * 2048 + (n_lo & 7) * 16;
-    // one core row (8 weights, 16 bytes) per item: (super-block, half, core row kc)
+    const int off_hi = (n_hi >> 3) * 1024 + (n_hi & 7) * 16, off_lo = (n_lo >> 3) * 1024 + (n_lo & 7) * 16;
+    // one core row (8 weights, 16 bytes) per item: (super-block, quarter qt, core row kc of the quarter)
     for (int it = tid; it < nsb * 32; it += 256) {
-        const int sb = it >> 5, kc32 = it & 31, hf = kc32 >> 4, kc = kc32 & 15;
+        const int sb = it >> 5, kc32 = it & 31, qt = kc32 >> 3, kc = kc32 & 7;
         float c[8];
-        if (q4) {  // elements 32 (kc / 4) + 8 (kc % 4) + {0,4,1,5,2,6,3,7} of the half
-            const int e0 = sb * 256 + hf * 128 + 32 * (kc >> 2) + 8 * (kc & 3);
+        if (q4) {  // elements 32 (kc / 4) + 8 (kc % 4) + {0,4,1,5,2,6,3,7} of the quarter
+            const int e0 = sb * 256 + qt * 64 + 32 * (kc >> 2) + 8 * (kc & 3);
             float nat[8];
 #pragma unroll
             for (int k = 0; k < 8; k++) nat[k] = val(e0 + k);
@@ -585,12 +626,12 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
                 hi[k] = half2_bits(hh);
                 lo[k] = pack_half2(c[2 * k] - hf2.x, c[2 * k + 1] - hf2.y);
             }
-            uint8_t *base = b4 + (size_t)sb * B4_SB + hf * B_BYTES + kc * 128;
+            uint8_t *base = b4 + (size_t)sb * B4_SB + qt * B_BYTES + kc * 128;
             *(uint4 *)(base + off_hi) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             *(uint4 *)(base + off_lo) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
-        if (q6) {  // elements 32 w4 + 4 t + {0..3} and 32 w4 + 16 + 4 t + {0..3} of the half (kc = 4 w4 + t)
-            const int e0 = sb * 256 + hf * 128 + 32 * (kc >> 2) + 4 * (kc & 3);
+        if (q6) {  // elements 32 w2 + 4 t + {0..3} and 32 w2 + 16 + 4 t + {0..3} of the quarter (kc = 4 w2 + t)
+            const int e0 = sb * 256 + qt * 64 + 32 * (kc >> 2) + 4 * (kc & 3);
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 c[k] = val(e0 + k);
@@ -604,7 +645,7 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
                 hi[k] = half2_bits(hh);
                 lo[k] = pack_half2(c[2 * k] - hf2.x, c[2 * k + 1] - hf2.y);
             }
-            uint8_t *base = b6 + (size_t)sb * B6_SB + hf * B_BYTES + kc * 128;
+            uint8_t *base = b6 + (size_t)sb * B6_SB + qt * B_BYTES + kc * 128;
             *(uint4 *)(base + off_hi) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             *(uint4 *)(base + off_lo) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
@@ -624,7 +665,7 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
             const float S = (((p[0] + p[1]) + p[2]) + p[3]) * S_FAC;
             const __half sh = __float2half_rn(S);
             const __half sl = __float2half_rn(S - __half2float(sh));
-            uint8_t *base = b4 + (size_t)sb * B4_SB + 2 * B_BYTES + (j >> 2) * 128 + (j & 3) * 4;
+            uint8_t *base = b4 + (size_t)sb * B4_SB + 4 * B_BYTES + (j >> 2) * 128 + (j & 3) * 4;
             *(uint32_t *)(base + (n_hi >> 3) * 256 + (n_hi & 7) * 16) = half2_bits(__halves2half2(sh, sh));
             *(uint32_t *)(base + (n_lo >> 3) * 256 + (n_lo & 7) * 16) = half2_bits(__halves2half2(sl, sl));
         }
@@ -689,7 +730,8 @@ int tc_prepare(const float *x, int ldx, int nv, int cols, const float *norm_w, f
     return LLMDOT_OK;
 }
 
-int tc_gemm(const TcSeg *seg, int nseg, int nv, int mode, TcScratch &s, int *err, cudaStream_t st)
+int tc_gemm(const TcSeg *seg, int nseg, int nv, int mode, TcScratch &s, int *err, cudaStream_t st,
+            const GemvPrefetch *pf)
 {
     if (!s.ready() || nseg < 1 || nseg > 3 || nv < 1 || nv > TC_MAX_ROWS || (mode != GEMV_STORE && mode != GEMV_ADD))
         return fail(LLMDOT_E_INVALID, "tensor-core matmul: bad arguments");
@@ -721,6 +763,11 @@ int tc_gemm(const TcSeg *seg, int nseg, int nv, int mode, TcScratch &s, int *err
     a.part = s.part;
     a.cnt = s.cnt;
     a.err = err;
+    if (pf) {
+        for (int r = 0; r < GEMV_PREFETCH_MAX; r++)  // bulk prefetches want 16-byte aligned, 16-byte multiples
+            if (((uintptr_t)pf->p[r] & 15) || (pf->n[r] & 15)) return fail(LLMDOT_E_INVALID, "tensor-core matmul: prefetch range");
+        a.pf = *pf;
+    }
     const int grid = a.U < s.grid_max ? a.U : s.grid_max;
     static std::atomic<unsigned long long> attr_done{0};
     LLMDOT_CUDA_TRY(smem_attr_once(attr_done, tc_gemm_kernel, (int)SMEM_BYTES));

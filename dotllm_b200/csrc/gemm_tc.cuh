@@ -8,6 +8,7 @@
 namespace llmdot {
 
 struct DevMat;
+struct GemvPrefetch;
 
 constexpr int TC_MIN_ROWS = 5;   // below this the matvec kernel (gemv.cu), where its input fits
 constexpr int TC_MAX_ROWS = 32;  // input rows per launch (MMA N = 2 x 32: the hi and lo fp16 halves)
@@ -42,7 +43,9 @@ int tc_prepare(const float *x, int ldx, int nv, int cols, const float *norm_w, f
                TcScratch &s, cudaStream_t st);
 
 // y = W . x for the prepared input, for 1..3 segments of the same input width; mode GEMV_STORE or
-// GEMV_ADD (residual add).  err: device flag set to 5 when a bounded wait gave up.
-int tc_gemm(const TcSeg *seg, int nseg, int nv, int mode, TcScratch &s, int *err, cudaStream_t st);
+// GEMV_ADD (residual add).  err: device flag set to 5 when a bounded wait gave up.  pf (nullable):
+// weights of the next operation, prefetched into L2 while this one runs.
+int tc_gemm(const TcSeg *seg, int nseg, int nv, int mode, TcScratch &s, int *err, cudaStream_t st,
+            const GemvPrefetch *pf = nullptr);
 
 }  // namespace llmdot

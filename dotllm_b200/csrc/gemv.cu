@@ -254,9 +254,9 @@ __device__ __forceinline__ bool gmbar_test(uint64_t *b, uint32_t parity)
 {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(gsm_u32(b)), "r"(parity), "r"(1000000u)
+        : "r"(gsm_u32(b)), "r"(parity)
         : "memory");
     return ok != 0;
 }
