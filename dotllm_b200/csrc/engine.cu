@@ -132,14 +132,19 @@ int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc 
     *out = nullptr;
     if (!cfg || !t || n <= 0) return fail(LLMDOT_E_INVALID, "model_load: null config or tensors");
     const llmdot_config &c = *cfg;
-    if (c.template_id != 0 && c.template_id != 2)
-        return fail(LLMDOT_E_UNSUPPORTED, "model_load: only the LlamaLike and GemmaLike execution templates run on the device");
+    const bool neox = c.template_id == 1;
+    if (c.template_id != 0 && c.template_id != 1 && c.template_id != 2)
+        return fail(LLMDOT_E_UNSUPPORTED,
+                    "model_load: only the LlamaLike, GptNeoXLike and GemmaLike execution templates run on the device");
     if (c.expert_count > 0) return fail(LLMDOT_E_UNSUPPORTED, "model_load: MoE models are not supported on the device");
-    if (!c.norm_is_rms) return fail(LLMDOT_E_UNSUPPORTED, "model_load: LayerNorm models are not supported on the device");
+    if (!c.norm_is_rms && !neox)
+        return fail(LLMDOT_E_UNSUPPORTED, "model_load: LayerNorm is supported on the device for the GptNeoXLike template only");
+    if (neox && tp > 1) return fail(LLMDOT_E_UNSUPPORTED, "model_load: the GptNeoXLike template runs on one GPU");
     if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.heads_kv <= 0 || c.head_dim <= 0 || c.vocab <= 0 ||
         c.context <= 0 || c.heads % c.heads_kv != 0)
         return fail(LLMDOT_E_FORMAT, "model_load: invalid dimensions in config");
-    if (c.ffn_type == 0) return fail(LLMDOT_E_UNSUPPORTED, "model_load: non-gated FFN is not supported on the device");
+    if (c.ffn_type == 0 && !neox)
+        return fail(LLMDOT_E_UNSUPPORTED, "model_load: the non-gated FFN is supported on the device for the GptNeoXLike template only");
     int rd = c.rope_dim > 0 ? c.rope_dim : c.head_dim;
     if (rd > c.head_dim || rd % 2) return fail(LLMDOT_E_FORMAT, "model_load: bad rope dimension");
     if (c.head_dim % 8 != 0) return fail(LLMDOT_E_UNSUPPORTED, "model_load: head_dim must be a multiple of 8");
@@ -211,6 +216,21 @@ int model_upload(int device, const llmdot_config *cfg, const llmdot_tensor_desc 
         const std::vector<RowRange> qr = tps ? std::vector<RowRange>{{sh.q_lo, sh.q_n}} : all;
         const std::vector<RowRange> kvr = tps ? std::vector<RowRange>{{sh.kv_lo, sh.kv_n}} : all;
         const std::vector<RowRange> fr = tps ? std::vector<RowRange>{{sh.f_lo, sh.f_n}} : all;
+        if (neox) {
+            // ProcessGptNeoXLikeLayer (InferenceEngine.cs:198-207) adds only the FFN result to the hidden
+            // state: the attention result goes into a buffer the hidden state never reads.  So the
+            // layer's output depends on the FFN weights alone; attention tensors are not uploaded.
+            const bool gated = c.ffn_type != 0;
+            if (!D(p + "ffn_up.weight") || !D(p + "ffn_down.weight") || (gated && !D(p + "ffn_gate.weight")))
+                return bail(fail(LLMDOT_E_FORMAT, p + "FFN tensors missing"));
+            if (gated && (rc = upload_mat(m, D(p + "ffn_gate.weight"), L.gate, H, c.ffn))) return bail(rc);
+            if ((rc = upload_mat(m, D(p + "ffn_up.weight"), L.up, H, c.ffn))) return bail(rc);
+            if ((rc = upload_mat(m, D(p + "ffn_down.weight"), L.down, c.ffn, H))) return bail(rc);
+            for (const DevMat *w : {&L.gate, &L.up, &L.down})
+                if (w->valid()) m->layer_bytes += w->bytes();
+            m->layer_bytes += (uint64_t)H * 4;
+            continue;
+        }
         if (c.qkv_fused) {
             if (!D(p + "attn_qkv.weight")) return bail(fail(LLMDOT_E_FORMAT, p + "attn_qkv.weight missing"));
             const std::vector<RowRange> qkvr =
@@ -451,6 +471,34 @@ int forward_step(llmdot_model *m, int batch, int kv_type, const int32_t *tokens,
     LLMDOT_TRY(te());
     for (int l = 0; l < c.layers; l++) {
         const LayerW &L = m->layers[l];
+        if (c.template_id == 1) {
+            // ProcessGptNeoXLikeLayer (InferenceEngine.cs:198-207): h += FFN(ApplyNorm(h, ffn)).  Its
+            // attention result only reaches a buffer the hidden state never reads (the two-argument
+            // Add writes its first argument), and no later step reads that layer's K/V either, so
+            // neither is computed.  ApplyNorm (:544-562): RMSNorm, or LayerNorm without a bias for
+            // the FFN norm; FfnForward (:452-487): gated as in LlamaLike, else up -> Gelu -> down.
+            const float *nw = L.ffn_norm ? L.ffn_norm : L.attn_norm;
+            const float *xin = w.h, *fused = nullptr;
+            LLMDOT_TRY(tb(FAM_OTHER));
+            if (c.norm_is_rms) {
+                fused = nw;
+            } else {
+                for (int v = 0; v < batch; v++)
+                    LLMDOT_TRY(launch_layernorm(w.h + (size_t)v * H, nw, nullptr, w.xn + (size_t)v * H, H, c.eps, st));
+                xin = w.xn;
+            }
+            LLMDOT_TRY(te());
+            LLMDOT_TRY(tb(FAM_MATVEC));
+            if (c.ffn_type != 0) {
+                LLMDOT_TRY(mv(L.gate, &L.up, xin, H, fused, w.gate, c.ffn, c.ffn_type == 2 ? GEMV_GELU_MUL : GEMV_SILU_MUL));
+            } else {
+                LLMDOT_TRY(mv(L.up, nullptr, xin, H, fused, w.gate, c.ffn, GEMV_STORE));
+                LLMDOT_TRY(launch_eltwise(OP_GELU, w.gate, nullptr, w.gate, c.ffn * batch, 0.0f, st, c.ffn));
+            }
+            LLMDOT_TRY(mv(L.down, nullptr, w.gate, c.ffn, nullptr, w.h, H, GEMV_ADD));
+            LLMDOT_TRY(te());
+            continue;
+        }
         // L2 prefetches: each matvec pulls in the weights of the one after it (the attention
         // sits between Q/K/V and the output projection)
         const GemvPrefetch pf_o = prefetch(&L.o), pf_ffn = prefetch(&L.gate, &L.up), pf_down = prefetch(&L.down);

@@ -17,17 +17,18 @@
 //
 // Kernel structure (one CTA of 16 warps per SM, persistent over a contiguous range of work units;
 // a unit is one 128-row tile x one 256-weight super-block):
-//   warp 0        producer: cp.async.bulk of the raw 16-row weight tiles (already tiled at model
-//                 load) into a 4-slot ring, and of the prepared B operand per quarter super-block;
+//   warp 0        producer: one cp.async.bulk of the prepared B operand per super-block into a
+//                 3-slot ring;
 //   warp 1        TMEM allocator and MMA issuer (one thread): tcgen05.mma.cta_group::1.kind::f16,
-//                 M = 128, N = 64, K = 16, from shared-memory descriptors (no-swizzle K-major core
+//                 M = 128, N = 64, K = 16, A from TMEM, B from shared memory (no-swizzle K-major core
 //                 matrices), commits to mbarriers;
 //   warps 4-7     epilogue: tcgen05.ld of the accumulators (one TMEM lane = one weight row per
 //                 thread), d scaling, output or K-split partial;
-//   warps 8-15    dequantisation: raw tile bytes (shared memory) -> fp16 A operand in the core-
-//                 matrix layout the MMA reads.
-// Quarter super-blocks (K = 64) are double-buffered, four raw super-blocks are in flight (and the next
-// eight are prefetched into L2); accumulators are double-buffered in TMEM.  A
+//   warps 8-15    dequantisation: raw tile bytes (shared memory, streamed by these warps with
+//                 bulk copies) -> fp16 A operand written straight into TMEM (tcgen05.st, one thread
+//                 per weight row), which the MMA reads from there.
+// The A operand lives in TMEM in three quarter super-block (K = 64) stages; three raw super-blocks and
+// three B super-blocks are in flight; accumulators are double-buffered in TMEM.  A
 // 128-row tile whose super-blocks are split between CTAs is finished by the last CTA to arrive,
 // which adds the partials in CTA order (deterministic).  Every wait is bounded (%globaltimer).
 #include "engine.cuh"
@@ -41,34 +42,37 @@ namespace {
 
 constexpr int TC_THREADS = 512;
 constexpr int TM = 128, TN = 64, QK = 64;           // tile rows, MMA N, K per pipeline stage (quarter super-block)
-constexpr uint32_t A_BYTES = TM * QK * 2;           // 16384: one fp16 A operand of a quarter super-block
-constexpr uint32_t B_BYTES = TN * QK * 2;           // 8192
-constexpr uint32_t STAGE = 2 * A_BYTES + B_BYTES;   // A (hi), A lo (Q6_K), B
-constexpr int NSTAGE = 3;
+constexpr uint32_t B_BYTES = TN * QK * 2;           // 8192: B operand of a quarter super-block
+constexpr int NSTAGE = 3;                           // A operand stages in TMEM (quarter super-blocks)
+constexpr int NB = 3;                               // B operand slots (whole super-blocks) in shared memory
 constexpr int NRAW = 3;                             // raw super-block slots (units in flight)
 constexpr uint32_t RAW_SLOT = 8 * Q6K_TILE;         // eight 16-row tiles of one super-block
 constexpr uint32_t AM_BYTES = TM * 16 * 2;          // Q4_K offset-term A operand (K = 16)
 constexpr uint32_t BM_BYTES = TN * 16 * 2;
 constexpr uint32_t B4_SB = 4 * B_BYTES + BM_BYTES;  // prepared B per super-block, Q4_K layout
 constexpr uint32_t B6_SB = 4 * B_BYTES;             // Q6_K layout
-constexpr uint32_t OFF_RAW = NSTAGE * STAGE;
+constexpr uint32_t OFF_B = 0;
+constexpr uint32_t OFF_RAW = OFF_B + NB * B4_SB;
 constexpr uint32_t OFF_AM = OFF_RAW + NRAW * RAW_SLOT;
-constexpr uint32_t OFF_BM = OFF_AM + 2 * AM_BYTES;
-constexpr uint32_t OFF_DSM = OFF_BM + 2 * BM_BYTES;
+constexpr uint32_t OFF_DSM = OFF_AM + 2 * AM_BYTES;
 constexpr uint32_t OFF_BAR = OFF_DSM + 2 * TM * 4;
-constexpr int NBAR = 48;
+constexpr int NBAR = 72;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 64;
 static_assert(SMEM_BYTES <= 227 * 1024, "tensor-core matmul: shared memory");
-constexpr int TMEM_COLS = 256;  // two main accumulators (64 columns each) + the Q4_K offset term
+// TMEM columns: accumulators 0..63 and 64..127 (one per super-block in flight), the Q4_K offset
+// term 128..191, then NSTAGE A stages of 64 columns (32 for fp16 A of K = 64, 32 for the Q6_K lo part)
+constexpr int TMEM_COLS = 512;
+constexpr uint32_t A_COL = 192;
 constexpr float S_FAC = 1.0f / 64.0f;  // sub-block sums (< 2^20) scaled into fp16 range
 constexpr float C_FAC = 256.0f;        // offset coefficients scaled up (their lo half stays normal)
 constexpr unsigned long long TC_WAIT_NS = 2000000000ull;
+constexpr int TC_DEFAULT_REPLICAS = 8;
 
 enum {
-    B_RAW_FULL = 0, B_A_FULL = B_RAW_FULL + 8 * NRAW, B_B_FULL = B_A_FULL + NSTAGE,
-    B_ST_EMPTY = B_B_FULL + NSTAGE, B_ACC_FULL = B_ST_EMPTY + NSTAGE, B_ACC_EMPTY = B_ACC_FULL + 2,
-    B_ACCM_EMPTY = B_ACC_EMPTY + 2, B_DRAIN = B_ACCM_EMPTY + 1, B_COUNT = B_DRAIN + 1
+    B_B_FULL = 0, B_B_EMPTY = B_B_FULL + NB, B_RAW_FULL = B_B_EMPTY + NB, B_RAW_EMPTY = B_RAW_FULL + 8 * NRAW,
+    B_A_FULL = B_RAW_EMPTY + 8 * NRAW, B_ST_EMPTY = B_A_FULL + NSTAGE, B_ACC_FULL = B_ST_EMPTY + NSTAGE,
+    B_ACC_EMPTY = B_ACC_FULL + 2, B_ACCM_EMPTY = B_ACC_EMPTY + 2, B_DRAIN = B_ACCM_EMPTY + 1, B_COUNT = B_DRAIN + 1
 };
 static_assert(B_COUNT <= NBAR, "tensor-core matmul: barrier slots");
 
@@ -78,6 +82,8 @@ struct TcArgs {
     int ldy[3], rows[3], qt[3], nrt16[3], cum[4];  // cum: first 128-row tile of each segment
     int nseg, nsb, U, nv, mode;
     const uint8_t *b4, *b6;
+    size_t b4s, b6s;  // bytes between the replicas of the prepared operands
+    int reps;         // replicas: CTA c reads replica c % reps (spreads the hot lines over L2)
     const float *isc;
     float *part;
     int *cnt;
@@ -114,6 +120,15 @@ __device__ __forceinline__ bool bar_try(uint64_t *b, uint32_t parity)
         : "memory");
     return ok != 0;
 }
+__device__ __forceinline__ void cp16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+// arrives on b once every cp.async this thread issued so far has landed (no pending-count change)
+__device__ __forceinline__ void cp_arrive(uint64_t *b)
+{
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(su32(b)) : "memory");
+}
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *b)
 {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -136,6 +151,15 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t da, uint64_t db, 
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
         "l"(da), "l"(db), "r"(IDESC), "r"(acc)
+        : "memory");
+}
+// A operand from TMEM: row m in lane m, K element k in column k/2 (low half for even k)
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t db, uint32_t acc)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(db), "r"(IDESC), "r"(acc)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t *b)
@@ -166,6 +190,16 @@ __device__ __forceinline__ void tmem_ld64(uint32_t ta, float (&f)[64])
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 64; i++) f[i] = __uint_as_float(v[i]);
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane
+__device__ __forceinline__ void tmem_st16(uint32_t ta, const uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(ta),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
 }
 
 __device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
@@ -228,9 +262,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     };
 
     if (tid == 0) {
-        for (int i = 0; i < NBAR; i++) {
+        for (int i = 0; i < B_COUNT; i++) {
             uint32_t cnt = 1;
-            if (i >= B_A_FULL && i < B_A_FULL + NSTAGE) cnt = 8;
+            if (i >= B_B_FULL && i < B_B_FULL + NB) cnt = 64;            // the B loader threads
+            if (i >= B_RAW_FULL && i < B_RAW_FULL + 8 * NRAW) cnt = 32;  // the copying warp's lanes
+            if (i >= B_RAW_EMPTY && i < B_RAW_EMPTY + 8 * NRAW) cnt = 2;  // the two warps reading a tile
+            if (i >= B_A_FULL && i < B_A_FULL + NSTAGE) cnt = 8;         // the dequantisation warps
             if (i == B_ACC_EMPTY || i == B_ACC_EMPTY + 1 || i == B_ACCM_EMPTY) cnt = 4;
             bar_init(bars + i, cnt);
         }
@@ -249,9 +286,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ---------------------------------------------------------------- producer
+        // ---------------------------------------------------------------- producer: B operands
         if (lane == 0 && n > 0) {
-            int b_issued = 0;
             // this CTA's share of the next operation's weights into L2
 #pragma unroll
             for (int r = 0; r < GEMV_PREFETCH_MAX; r++) {
@@ -268,34 +304,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                     len -= piece;
                 }
             }
-            bool ok = true;
-            for (int i = 0; i < n && ok; i++) {
-                const Unit U = unit(i);
-                const bool q4 = U.qt == QT_Q4K;
-                const uint8_t *src = q4 ? a.b4 + (size_t)U.sb * B4_SB : a.b6 + (size_t)U.sb * B6_SB;
-                for (int qt = 0; qt < 4 && ok; qt++) {
-                    const int Q = 4 * i + qt, st = Q % NSTAGE;
-                    if (Q >= NSTAGE && !(ok = wait(B_ST_EMPTY + st, (Q / NSTAGE - 1) & 1))) break;
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    const bool bm = q4 && qt == 3;
-                    bar_expect_tx(bars + B_B_FULL + st, B_BYTES + (bm ? BM_BYTES : 0));
-                    bulk_g2s(smem + st * STAGE + 2 * A_BYTES, src + qt * B_BYTES, B_BYTES, bars + B_B_FULL + st);
-                    if (bm) bulk_g2s(smem + OFF_BM + (i & 1) * BM_BYTES, src + 4 * B_BYTES, BM_BYTES, bars + B_B_FULL + st);
-                    b_issued = Q + 1;
-                }
-            }
-            if (!ok) {  // bounded drain of the copies this thread issued into shared memory
-                for (int st = 0; st < NSTAGE; st++) {
-                    int last = -1;  // last quarter issued to stage st
-                    for (int q = b_issued - 1; q >= 0 && q >= b_issued - NSTAGE; q--)
-                        if (q % NSTAGE == st) last = q;
-                    if (last >= 0) {
-                        const uint64_t t0 = gtime();
-                        while (!bar_try(bars + B_B_FULL + st, (last / NSTAGE) & 1) && gtime() - t0 < TC_WAIT_NS) {}
-                    }
-                }
+        }
+    } else if (warp == 2 || warp == 3) {
+        // ---------------------------------------------------------------- B loader (64 threads)
+        // cp.async 16-byte pieces of the prepared B of each super-block into a 3-slot ring; a unit's
+        // slot is signalled once its copies have landed and are made visible to the tensor core
+        const int lt = tid - 64;
+        auto issue_b = [&](int k) {
+            const Unit U = unit(k);
+            const bool q4 = U.qt == QT_Q4K;
+            const int rr = c % a.reps;
+            const uint32_t bytes = q4 ? B4_SB : B6_SB;
+            const uint8_t *src = q4 ? a.b4 + rr * a.b4s + (size_t)U.sb * B4_SB : a.b6 + rr * a.b6s + (size_t)U.sb * B6_SB;
+            uint8_t *dst = smem + OFF_B + (k % NB) * B4_SB;
+            for (uint32_t o = (uint32_t)lt * 16; o < bytes; o += 64 * 16) cp16(dst + o, src + o);
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+        int issued = 0;
+        for (; issued < NB && issued < n; issued++) issue_b(issued);
+        // unit k is signalled as soon as its copies land; the slot of unit k - 1 is refilled with unit
+        // k - 1 + NB once the tensor core is done with it, so signalling never waits on the MMA
+        for (int k = 0; k < n; k++) {
+            const int pend = issued - k - 1;  // copy groups issued after unit k's
+            if (pend >= 2) asm volatile("cp.async.wait_group 2;" ::: "memory");
+            else if (pend == 1) asm volatile("cp.async.wait_group 1;" ::: "memory");
+            else asm volatile("cp.async.wait_group 0;" ::: "memory");
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic-proxy writes -> tensor core
+            bar_arrive(bars + B_B_FULL + k % NB);
+            if (k >= 1 && issued < n) {
+                if (!wait(B_B_EMPTY + (k - 1) % NB, ((k - 1) / NB) & 1)) break;
+                issue_b(issued++);
             }
         }
+        asm volatile("cp.async.wait_all;" ::: "memory");  // no copy may land after the CTA exits
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0 && n > 0) {
@@ -304,28 +345,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             for (int i = 0; i < n && ok; i++) {
                 const Unit U = unit(i);
                 const bool q4 = U.qt == QT_Q4K;
-                const int b = i & 1;
+                const int b = i & 1, bs = i % NB;
                 if (i >= 2 && !(ok = wait(B_ACC_EMPTY + b, ((i - 2) >> 1) & 1))) break;
+                if (!(ok = wait(B_B_FULL + bs, (i / NB) & 1))) break;
+                const uint32_t Bsm = su32(smem + OFF_B + bs * B4_SB);
                 for (int qt = 0; qt < 4 && ok; qt++) {
                     const int Q = 4 * i + qt, st = Q % NSTAGE;
-                    if (!(ok = wait(B_A_FULL + st, (Q / NSTAGE) & 1)) || !(ok = wait(B_B_FULL + st, (Q / NSTAGE) & 1))) break;
+                    if (!(ok = wait(B_A_FULL + st, (Q / NSTAGE) & 1))) break;
                     tc_fence_after();
-                    const uint32_t A = su32(smem + st * STAGE), B = A + 2 * A_BYTES;
+                    const uint32_t A = tmem + A_COL + st * 64;
 #pragma unroll
                     for (int kk = 0; kk < QK / 16; kk++) {
-                        const uint64_t db = sdesc(B + kk * 256, 128, 1024);
-                        umma(tmem + b * 64, sdesc(A + kk * 256, 128, 1024), db, (qt | kk) != 0);
-                        if (!q4) umma(tmem + b * 64, sdesc(A + A_BYTES + kk * 256, 128, 1024), db, 1u);
+                        const uint64_t db = sdesc(Bsm + qt * B_BYTES + kk * 256, 128, 1024);
+                        umma_ts(tmem + b * 64, A + kk * 8, db, (qt | kk) != 0);
+                        if (!q4) umma_ts(tmem + b * 64, A + 32 + kk * 8, db, 1u);
                     }
                     if (q4 && qt == 3) {
                         if (U.first && run >= 1 && !(ok = wait(B_ACCM_EMPTY, (run - 1) & 1))) break;
                         tc_fence_after();
                         umma(tmem + 128, sdesc(su32(smem + OFF_AM + b * AM_BYTES), 128, 256),
-                             sdesc(su32(smem + OFF_BM + b * BM_BYTES), 128, 256), U.first ? 0u : 1u);
+                             sdesc(Bsm + 4 * B_BYTES, 128, 256), U.first ? 0u : 1u);
                     }
                     umma_commit(bars + B_ST_EMPTY + st);
                 }
                 if (!ok) break;
+                umma_commit(bars + B_B_EMPTY + bs);
                 umma_commit(bars + B_ACC_FULL + b);
                 if (U.last) run++;
             }
@@ -419,46 +463,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         }
     } else if (warp >= 8) {
         // ---------------------------------------------------------------- dequantisation
-        // thread (tile rt8 = warp - 8, lane L); per quarter super-block a warp writes 16-byte core-
-        // matrix rows so that each group of 8 lanes covers 128 contiguous bytes (no bank conflict)
-        const int dt = tid - 256, rt8 = dt >> 5, L = dt & 31;
-        // each warp streams its own 16-row tile of every unit into its part of the raw ring
-        int own_issued = 0;
-        auto issue_own = [&](int k) {
-            if (lane == 0) {
-                const Unit V = unit(k);
-                const uint32_t tb = V.qt == QT_Q4K ? Q4K_TILE : Q6K_TILE;
-                uint64_t *bar = bars + B_RAW_FULL + (k % NRAW) * 8 + rt8;
-                if (8 * V.rt + rt8 < a.nrt16[V.seg]) {
-                    bar_expect_tx(bar, tb);
-                    bulk_g2s(smem + OFF_RAW + (k % NRAW) * RAW_SLOT + rt8 * tb,
-                             a.w[V.seg] + ((size_t)(8 * V.rt + rt8) * nsb + V.sb) * tb, tb, bar);
-                } else {
-                    bar_arrive(bar);  // no such rows: the phase completes without data
-                }
+        // warp 8 + 4 kh + lq: TMEM lanes (weight rows) 32 lq .. 32 lq + 31, K half kh of each quarter
+        // super-block; one thread per row writes its A columns with tcgen05.st.  Warp 8 + r also
+        // streams raw 16-row tile r of every unit into the ring; tile r is read by the two warps of
+        // lane quarter r / 2.
+        const int dw = warp - 8, lq = dw & 3, kh = dw >> 2, row = 32 * lq + lane;
+        const int rt8 = row >> 4, r16 = row & 15, g = r16 & 7, h = r16 >> 3;
+        const int my_tile = dw;  // the tile this warp copies
+        auto issue_tile = [&](int k) {  // cp.async by all 32 lanes; each lane arrives when its pieces land
+            const Unit V = unit(k);
+            const uint32_t tb = V.qt == QT_Q4K ? Q4K_TILE : Q6K_TILE;
+            if (8 * V.rt + my_tile < a.nrt16[V.seg]) {  // else no such rows: the lanes only arrive
+                uint8_t *dst = smem + OFF_RAW + (k % NRAW) * RAW_SLOT + my_tile * tb;
+                const uint8_t *src = a.w[V.seg] + ((size_t)(8 * V.rt + my_tile) * nsb + V.sb) * tb;
+                for (uint32_t o = (uint32_t)lane * 16; o < tb; o += 32 * 16) cp16(dst + o, src + o);
             }
-            own_issued = k + 1;
+            cp_arrive(bars + B_RAW_FULL + (k % NRAW) * 8 + my_tile);
         };
-        for (int k = 0; k < NRAW && k < n; k++) issue_own(k);
-        for (int i = 0; i < n; i++) {
+        int own_issued = 0;
+        for (int k = 0; k < NRAW && k < n; k++) {
+            issue_tile(k);
+            own_issued = k + 1;
+        }
+        bool ok = true;
+        for (int i = 0; i < n && ok; i++) {
             const Unit U = unit(i);
-            const int b = i & 1;
-            if (!wait(B_RAW_FULL + (i % NRAW) * 8 + rt8, (i / NRAW) & 1)) break;
-            if (i >= 2 && !wait(B_ACC_EMPTY + b, ((i - 2) >> 1) & 1)) break;
+            const int b = i & 1, slot = i % NRAW;
             const bool q4 = U.qt == QT_Q4K;
-            const uint8_t *raw = smem + OFF_RAW + (i % NRAW) * RAW_SLOT + rt8 * (q4 ? Q4K_TILE : Q6K_TILE);
-            bool ok = true;
+            if (!(ok = wait(B_RAW_FULL + slot * 8 + rt8, (i / NRAW) & 1))) break;
+            if (i >= 2 && !(ok = wait(B_ACC_EMPTY + b, ((i - 2) >> 1) & 1))) break;
+            const uint8_t *tile = smem + OFF_RAW + slot * RAW_SLOT + rt8 * (q4 ? Q4K_TILE : Q6K_TILE);
+            uint4 hd = make_uint4(0, 0, 0, 0);
+            if (q4) {
+                hd = *(const uint4 *)(tile + 2048 + g * 32 + h * 16);
+                if (kh == 0) dsm[b * TM + row] = half_bits(hd.x & 0xFFFF);
+            } else if (kh == 0) {
+                dsm[b * TM + row] = half_bits(*(const uint16_t *)(tile + 3328 + g * 4 + h * 2));
+            }
             for (int qt = 0; qt < 4; qt++) {
                 const int Q = 4 * i + qt, st = Q % NSTAGE;
                 if (Q >= NSTAGE && !(ok = wait(B_ST_EMPTY + st, (Q / NSTAGE - 1) & 1))) break;
-                uint8_t *A = smem + st * STAGE;
+                tc_fence_after();
+                const uint32_t ta = tmem + ((uint32_t)(32 * lq) << 16) + A_COL + st * 64 + kh * 16;
                 if (q4) {
-                    // row r16 = L & 15 of the 16-row tile, sub-block j = 2 qt + (L >> 4): four core rows
-                    const int r16 = L & 15, jj = L >> 4, j = 2 * qt + jj, h = r16 >> 3, g = r16 & 7;
-                    const int row = 16 * rt8 + r16;
-                    uint8_t *arow = A + (row >> 3) * 1024 + (row & 7) * 16;
-                    const uint4 W = *(const uint4 *)(raw + ((j & 1) + 2 * h) * 512 + (4 * g + (j >> 1)) * 16);
-                    const uint4 hd = *(const uint4 *)(raw + 2048 + g * 32 + h * 16);
+                    // sub-block j = 2 qt + kh of this row: 32 weights q * sc as 16 columns of fp16 pairs
+                    const int j = 2 * qt + kh;
+                    const uint4 W = *(const uint4 *)(tile + ((j & 1) + 2 * h) * 512 + (4 * g + (j >> 1)) * 16);
                     const int bit = 12 * j, wi = bit >> 5;
                     const uint32_t lo = wi == 0 ? hd.y : (wi == 1 ? hd.z : hd.w);
                     const uint32_t hi = wi == 0 ? hd.z : hd.w;
@@ -469,16 +519,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                     const uint32_t sc16 = hfma2(sc2, 0x2C002C00u, 0u);   // * 1/16
                     const uint32_t nsc16 = hfma2(sc2, 0xD400D400u, 0u);  // * -64
                     const uint32_t Ws[4] = {W.x, W.y, W.z, W.w};
+                    uint32_t o[16];
 #pragma unroll
                     for (int i4 = 0; i4 < 4; i4++) {
                         const uint32_t w = Ws[i4], w8 = w >> 8;
-                        uint4 o;
-                        o.x = hfma2(and_or(w, 0x000F000Fu, 0x64006400u), sc2, nsc2);
-                        o.y = hfma2(and_or(w, 0x00F000F0u, 0x64006400u), sc16, nsc16);
-                        o.z = hfma2(and_or(w8, 0x000F000Fu, 0x64006400u), sc2, nsc2);
-                        o.w = hfma2(and_or(w8, 0x00F000F0u, 0x64006400u), sc16, nsc16);
-                        *(uint4 *)(arow + (4 * jj + i4) * 128) = o;
+                        o[4 * i4 + 0] = hfma2(and_or(w, 0x000F000Fu, 0x64006400u), sc2, nsc2);
+                        o[4 * i4 + 1] = hfma2(and_or(w, 0x00F000F0u, 0x64006400u), sc16, nsc16);
+                        o[4 * i4 + 2] = hfma2(and_or(w8, 0x000F000Fu, 0x64006400u), sc2, nsc2);
+                        o[4 * i4 + 3] = hfma2(and_or(w8, 0x00F000F0u, 0x64006400u), sc16, nsc16);
                     }
+                    tmem_st16(ta, o);
                     // offset coefficient of sub-block j as an fp16 hi/lo pair (K = 2j, 2j + 1)
                     const float dd = half_bits(hd.x & 0xFFFF), dm = half_bits(hd.x >> 16);
                     const float cf = fmaf(8.0f * dd, (float)sc, dm * (float)mm) * C_FAC;
@@ -486,64 +536,58 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                     const __half2 pair = __halves2half2(chh, __float2half_rn(cf - __half2float(chh)));
                     *(uint32_t *)(smem + OFF_AM + b * AM_BYTES + (row >> 3) * 256 + (j >> 2) * 128 + (row & 7) * 16 +
                                   (j & 3) * 4) = half2_bits(pair);
-                    if (qt == 0 && jj == 0) dsm[b * TM + row] = dd;
                 } else {
-                    // lane (g = L & 7, t = L >> 3) takes tile lane 4g + t: its 4-element groups of
-                    // sub-blocks 2w, 2w + 1 (w = 2 qt, 2 qt + 1) for rows g and g + 8
-                    const int g = L & 7, t = L >> 3, sl = 4 * g + t;
+                    // group w = 2 qt + kh (sub-blocks 2w, 2w + 1) of this row: the four tile lanes
+                    // t = 0..3 each hold its 4-element pieces; sc * (q - 32) as fp16 hi + exact lo
+                    const int w = 2 * qt + kh;
+                    const uint8_t *lwp = tile + (3 * h + (w >> 2)) * 512 + (4 * g) * 16 + (w & 3) * 4;
+                    const uint8_t *hup = tile + (3 * h + 2) * 512 + (4 * g) * 16 + (w >> 1) * 4;
+                    const uint32_t SCa = *(const uint16_t *)(tile + 3072 + g * 32 + h * 16 + 2 * w);  // int8 sc of 2w, 2w + 1
+                    uint32_t ohi[16], olo[16];
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const int row = 16 * rt8 + g + 8 * h;
-                        uint8_t *arow = A + (row >> 3) * 1024 + (row & 7) * 16;
-                        const uint4 LW = *(const uint4 *)(raw + (3 * h + (qt >> 1)) * 512 + sl * 16);
-                        const uint4 HU = *(const uint4 *)(raw + (3 * h + 2) * 512 + sl * 16);
-                        const uint4 SC = *(const uint4 *)(raw + 3072 + g * 32 + h * 16);
-                        const uint32_t Lw4[4] = {LW.x, LW.y, LW.z, LW.w}, Hu4[4] = {HU.x, HU.y, HU.z, HU.w};
-                        const uint32_t SC4[4] = {SC.x, SC.y, SC.z, SC.w};
+                    for (int t = 0; t < 4; t++) {
+                        const uint32_t Lw = *(const uint32_t *)(lwp + t * 16), Hu = *(const uint32_t *)(hup + t * 16);
 #pragma unroll
-                        for (int w2 = 0; w2 < 2; w2++) {
-                            const int w = 2 * qt + w2;
-                            const uint32_t Lw = Lw4[w & 3], Hu = Hu4[w >> 1];
-                            uint32_t ohi[4], olo[4];
-#pragma unroll
-                            for (int k = 0; k < 4; k++) {
-                                uint32_t hb;
-                                if ((w & 1) == 0) hb = Hu >> (2 * k);
-                                else hb = k == 0 ? (Hu << 4) : k == 1 ? (Hu << 2) : k == 2 ? (Hu >> 8) : (Hu >> 10);
-                                const uint32_t qv = and_or(hb, 0x00300030u, and_or(Lw >> (4 * k), 0x000F000Fu, 0x64006400u));
-                                const uint32_t p = hsub2(qv, 0x64206420u);  // q - 32, exact
-                                const int sidx = 2 * w + (k >> 1);
-                                const int scv = (int)(int8_t)(SC4[sidx >> 2] >> (8 * (sidx & 3)));
-                                const __half shv = __int2half_rn(scv);  // |sc| <= 128: exact
-                                const uint32_t sc2 = half2_bits(__halves2half2(shv, shv));
-                                uint32_t hv;
-                                asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(hv) : "r"(p), "r"(sc2));
-                                ohi[k] = hv;
-                                olo[k] = hfma2(p, sc2, hv ^ 0x80008000u);  // exact residual of the product
-                            }
-                            const int kc = 4 * w2 + t;
-                            *(uint4 *)(arow + kc * 128) = make_uint4(ohi[0], ohi[1], ohi[2], ohi[3]);
-                            *(uint4 *)(arow + A_BYTES + kc * 128) = make_uint4(olo[0], olo[1], olo[2], olo[3]);
+                        for (int k = 0; k < 4; k++) {
+                            uint32_t hb;
+                            if ((w & 1) == 0) hb = Hu >> (2 * k);
+                            else hb = k == 0 ? (Hu << 4) : k == 1 ? (Hu << 2) : k == 2 ? (Hu >> 8) : (Hu >> 10);
+                            const uint32_t qv = and_or(hb, 0x00300030u, and_or(Lw >> (4 * k), 0x000F000Fu, 0x64006400u));
+                            const uint32_t pq = hsub2(qv, 0x64206420u);  // q - 32, exact
+                            const int scv = (int)(int8_t)(SCa >> (8 * (k >> 1)));
+                            const __half shv = __int2half_rn(scv);  // |sc| <= 128: exact
+                            const uint32_t sc2 = half2_bits(__halves2half2(shv, shv));
+                            uint32_t hv;
+                            asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(hv) : "r"(pq), "r"(sc2));
+                            ohi[4 * t + k] = hv;
+                            olo[4 * t + k] = hfma2(pq, sc2, hv ^ 0x80008000u);  // exact residual of the product
                         }
-                        if (qt == 0 && t == 0) dsm[b * TM + row] = half_bits(*(const uint16_t *)(raw + 3328 + g * 4 + h * 2));
                     }
+                    tmem_st16(ta, ohi);
+                    tmem_st16(ta + 32, olo);
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the offset-term operand in smem
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) bar_arrive(bars + B_A_FULL + st);
             }
             if (!ok) break;
-            __syncwarp();  // every lane is done with this unit's tile: refill the slot
+            // this warp is done with its lane quarter's two tiles of unit i
+            __syncwarp();
+            if (lane == 0) {
+                bar_arrive(bars + B_RAW_EMPTY + slot * 8 + 2 * lq);
+                bar_arrive(bars + B_RAW_EMPTY + slot * 8 + 2 * lq + 1);
+            }
             if (i + NRAW < n) {
-                if (lane == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                issue_own(i + NRAW);
+                // refill this warp's tile of the slot once both readers of it are done with unit i
+                if (!(ok = wait(B_RAW_EMPTY + slot * 8 + my_tile, (i / NRAW) & 1))) break;
+                issue_tile(i + NRAW);
+                own_issued = i + NRAW + 1;
             }
         }
-        // bounded drain of this warp's copies still in flight (an early exit leaves some)
-        for (int k = own_issued - NRAW < 0 ? 0 : own_issued - NRAW; k < own_issued; k++) {
-            const uint64_t t0 = gtime();
-            while (!bar_try(bars + B_RAW_FULL + (k % NRAW) * 8 + rt8, (k / NRAW) & 1) && gtime() - t0 < TC_WAIT_NS) {}
-        }
+        asm volatile("cp.async.wait_all;" ::: "memory");  // no copy may land after the CTA exits
+        (void)own_issued;
     }
 
     tc_fence_before();
@@ -560,7 +604,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
 __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ x, int ldx, int nsb,
                                                       const float *__restrict__ norm_w, float eps, int q4, int q6,
                                                       uint8_t *__restrict__ b4, uint8_t *__restrict__ b6,
-                                                      float *__restrict__ isc)
+                                                      float *__restrict__ isc, int reps, size_t b4s, size_t b6s)
 {
     __shared__ float red[2][8];
     __shared__ float stat[2];
@@ -627,8 +671,10 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
                 lo[k] = pack_half2(c[2 * k] - hf2.x, c[2 * k + 1] - hf2.y);
             }
             uint8_t *base = b4 + (size_t)sb * B4_SB + qt * B_BYTES + kc * 128;
-            *(uint4 *)(base + off_hi) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *(uint4 *)(base + off_lo) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            for (int r = 0; r < reps; r++) {
+                *(uint4 *)(base + r * b4s + off_hi) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *(uint4 *)(base + r * b4s + off_lo) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
         }
         if (q6) {  // elements 32 w2 + 4 t + {0..3} and 32 w2 + 16 + 4 t + {0..3} of the quarter (kc = 4 w2 + t)
             const int e0 = sb * 256 + qt * 64 + 32 * (kc >> 2) + 4 * (kc & 3);
@@ -646,8 +692,10 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
                 lo[k] = pack_half2(c[2 * k] - hf2.x, c[2 * k + 1] - hf2.y);
             }
             uint8_t *base = b6 + (size_t)sb * B6_SB + qt * B_BYTES + kc * 128;
-            *(uint4 *)(base + off_hi) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *(uint4 *)(base + off_lo) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            for (int r = 0; r < reps; r++) {
+                *(uint4 *)(base + r * b6s + off_hi) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *(uint4 *)(base + r * b6s + off_lo) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
         }
     }
     if (q4) {
@@ -666,8 +714,10 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
             const __half sh = __float2half_rn(S);
             const __half sl = __float2half_rn(S - __half2float(sh));
             uint8_t *base = b4 + (size_t)sb * B4_SB + 4 * B_BYTES + (j >> 2) * 128 + (j & 3) * 4;
-            *(uint32_t *)(base + (n_hi >> 3) * 256 + (n_hi & 7) * 16) = half2_bits(__halves2half2(sh, sh));
-            *(uint32_t *)(base + (n_lo >> 3) * 256 + (n_lo & 7) * 16) = half2_bits(__halves2half2(sl, sl));
+            for (int r = 0; r < reps; r++) {
+                *(uint32_t *)(base + r * b4s + (n_hi >> 3) * 256 + (n_hi & 7) * 16) = half2_bits(__halves2half2(sh, sh));
+                *(uint32_t *)(base + r * b4s + (n_lo >> 3) * 256 + (n_lo & 7) * 16) = half2_bits(__halves2half2(sl, sl));
+            }
         }
     }
 }
@@ -699,16 +749,25 @@ int tc_scratch_alloc(TcScratch &s, int cols_max, int tiles_max, std::vector<void
         allocs.push_back(*p);
         return LLMDOT_OK;
     };
-    LLMDOT_TRY(get((void **)&s.b4, (size_t)nsb * B4_SB));
-    LLMDOT_TRY(get((void **)&s.b6, (size_t)nsb * B6_SB));
+    // replicas of the prepared operands: every CTA reads all of one input's B, so a single copy
+    // concentrates 148 readers on the same L2 lines; CTA c reads replica c % reps
+    static const int reps_env = [] {
+        const char *e = getenv("LLMDOT_TC_REPLICAS");
+        return e ? std::max(1, std::min(16, atoi(e))) : TC_DEFAULT_REPLICAS;
+    }();
+    s.reps = reps_env;
+    s.b4s = (size_t)nsb * B4_SB;
+    s.b6s = (size_t)nsb * B6_SB;
+    LLMDOT_TRY(get((void **)&s.b4, s.b4s * s.reps));
+    LLMDOT_TRY(get((void **)&s.b6, s.b6s * s.reps));
     LLMDOT_TRY(get((void **)&s.isc, sizeof(float) * TC_MAX_ROWS));
     LLMDOT_TRY(get((void **)&s.part, sizeof(float) * (size_t)grid * 2 * TC_MAX_ROWS * TM));
     LLMDOT_TRY(get((void **)&s.cnt, sizeof(int) * (size_t)tiles_max));
     LLMDOT_CUDA_TRY(cudaMemset(s.cnt, 0, sizeof(int) * (size_t)tiles_max));
     // stale columns of unused input rows must not hold NaN bit patterns that the MMA would read as
     // values of live columns: every column is independent, so zeroing once is only for tidiness
-    LLMDOT_CUDA_TRY(cudaMemset(s.b4, 0, (size_t)nsb * B4_SB));
-    LLMDOT_CUDA_TRY(cudaMemset(s.b6, 0, (size_t)nsb * B6_SB));
+    LLMDOT_CUDA_TRY(cudaMemset(s.b4, 0, s.b4s * s.reps));
+    LLMDOT_CUDA_TRY(cudaMemset(s.b6, 0, s.b6s * s.reps));
     s.cols_max = nsb * 256;
     s.grid_max = grid;
     s.tiles_max = tiles_max;
@@ -725,7 +784,8 @@ int tc_prepare(const float *x, int ldx, int nv, int cols, const float *norm_w, f
 {
     if (!s.ready() || nv < 1 || nv > TC_MAX_ROWS || cols % 256 || cols > s.cols_max)
         return fail(LLMDOT_E_INVALID, "tensor-core matmul: bad input shape");
-    tc_prep_kernel<<<nv, 256, 0, st>>>(x, ldx, cols / 256, norm_w, eps, q4 ? 1 : 0, q6 ? 1 : 0, s.b4, s.b6, s.isc);
+    tc_prep_kernel<<<nv, 256, 0, st>>>(x, ldx, cols / 256, norm_w, eps, q4 ? 1 : 0, q6 ? 1 : 0, s.b4, s.b6, s.isc,
+                                       s.reps, s.b4s, s.b6s);
     LLMDOT_CUDA_TRY(cudaGetLastError());
     return LLMDOT_OK;
 }
@@ -759,6 +819,9 @@ int tc_gemm(const TcSeg *seg, int nseg, int nv, int mode, TcScratch &s, int *err
     a.U = tiles * a.nsb;
     a.b4 = s.b4;
     a.b6 = s.b6;
+    a.b4s = s.b4s;
+    a.b6s = s.b6s;
+    a.reps = s.reps;
     a.isc = s.isc;
     a.part = s.part;
     a.cnt = s.cnt;

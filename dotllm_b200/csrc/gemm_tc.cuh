@@ -21,6 +21,8 @@ struct TcScratch {
     float *isc = nullptr;   // [TC_MAX_ROWS] 1 / (power-of-two scale of the row)
     float *part = nullptr;  // [grid][2][TC_MAX_ROWS][128] partial row tiles
     int *cnt = nullptr;     // [tiles_max] arrivals per 128-row tile (left at zero)
+    size_t b4s = 0, b6s = 0;  // bytes of one replica of each layout
+    int reps = 1;             // replicas of the prepared operands (CTA c reads replica c % reps)
     int cols_max = 0, grid_max = 0, tiles_max = 0;
     bool ready() const { return b4 != nullptr; }
 };
