@@ -294,13 +294,18 @@ def measure(m, cfg, args, B, n_prompt, ctx, rank, steps, dist, local, windows=1,
     clk = ClockSampler(gpu_index if clocks else -1, uuid)
     per_window = []
     kps = 0
+    region = getattr(args, "profile_region", False)
     with clk:
         for _ in range(windows):
             if dist:
                 dist.barrier()
             torch.cuda.synchronize()
+            if region:
+                torch.cuda.cudart().cudaProfilerStart()
             out, dev_ms, kps = decode_steps(sessions, cur, steps)
             torch.cuda.synchronize()
+            if region:
+                torch.cuda.cudart().cudaProfilerStop()
             cur = out[-1]
             per_window.append(dev_ms)
     if dist:
@@ -428,6 +433,8 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the Phi-3 sharded-sessions and Llama-3-8B tensor-parallel workloads")
     ap.add_argument("--matvec", default=None, help="time one matvec over this tensor only (profiling)")
+    ap.add_argument("--profile-region", action="store_true",
+                    help="bracket the timed decode windows with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

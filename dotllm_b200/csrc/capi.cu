@@ -61,8 +61,8 @@ struct llmdot_backend {
         size_t bytes = 0;
     };
     std::map<std::string, Cached> weights;
-    void *scratch[4] = {nullptr, nullptr, nullptr, nullptr};
-    size_t scratch_bytes[4] = {0, 0, 0, 0};
+    void *scratch[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // 4: the sampler's full-row work
+    size_t scratch_bytes[5] = {0, 0, 0, 0, 0};
     unsigned long long *keys = nullptr;
     int32_t *idx = nullptr;
 };
@@ -172,7 +172,7 @@ extern "C" int llmdot_cuda_destroy(llmdot_backend *h)
     cudaSetDevice(h->device);
     if (h->st) cudaStreamSynchronize(h->st);
     for (auto &kv : h->weights) cudaFree(kv.second.ptr);
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < 5; i++)
         if (h->scratch[i]) cudaFree(h->scratch[i]);
     if (h->keys) cudaFree(h->keys);
     if (h->idx) cudaFree(h->idx);
@@ -467,6 +467,7 @@ static SampleArgs sample_args(const llmdot_sampling &o, int n)
     a.temperature = o.temperature;
     a.inv_temp = o.temperature > 0.0f ? 1.0f / o.temperature : 0.0f;  // 1f / options.Temperature
     a.top_k = o.top_k;
+    a.top_p = o.top_p;
     a.penalty = o.repeat_penalty;
     a.window = o.repeat_window > 0 ? o.repeat_window : 0;
     return a;
@@ -494,9 +495,11 @@ extern "C" int llmdot_cuda_sample(llmdot_backend *h, const float *logits, int n,
     a.recent_ld = n_recent;
     a.out = (int32_t *)dp + 1;
     a.r = (const float *)((int32_t *)dp + 3);
+    if (sample_full_row(a.temperature, a.top_k, n)) LLMDOT_TRY(scratch(h, 4, sample_work_bytes(n), &a.work));
     LLMDOT_TRY(launch_sample(a, 1, h->st));
     int32_t out = 0;
     LLMDOT_TRY(down(h, &out, (int32_t *)dp + 1, sizeof(int32_t)));
+    if (out < 0) return fail(LLMDOT_E_UNSUPPORTED, "sample: a tie group of the nucleus above 8192 tokens");
     *index = out;
     return LLMDOT_OK;
 }
@@ -1022,8 +1025,9 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
     if (m->tp > 1) return fail(LLMDOT_E_UNSUPPORTED, "generate_sampled: not under tensor parallelism");
     const llmdot_config &c = m->cfg;
     SampleArgs a = sample_args(*opt, c.vocab);
-    if (a.temperature > 0.0f && (a.top_k <= 0 || a.top_k >= c.vocab || a.top_k > SAMPLE_MAX_TOP_K))
-        return fail(LLMDOT_E_UNSUPPORTED, "generate_sampled: temperature > 0 needs 0 < top_k < vocabulary, <= 1024");
+    const bool full_row = sample_full_row(a.temperature, a.top_k, c.vocab);
+    if (a.temperature > 0.0f && !full_row && a.top_k > SAMPLE_MAX_TOP_K)
+        return fail(LLMDOT_E_UNSUPPORTED, "generate_sampled: top_k above 1024 (and below the vocabulary)");
     if (a.window > SAMPLE_MAX_WINDOW) return fail(LLMDOT_E_UNSUPPORTED, "generate_sampled: repeat window above 1024");
     *n_out = 0;
     LLMDOT_TRY(llmdot_cuda_session_reset(s));  // InferenceEngine.cs:79
@@ -1054,11 +1058,17 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
     // device: [history (keep)] [length] [out] [r]
     int32_t *dbuf = nullptr;
     LLMDOT_CUDA_TRY(cudaMallocAsync(&dbuf, sizeof(int32_t) * (keep + 3), st));
+    if (full_row && cudaMallocAsync(&a.work, sample_work_bytes(c.vocab), st) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFreeAsync(dbuf, st);
+        return fail(LLMDOT_E_NOMEM, "generate_sampled: sampler work allocation failed");
+    }
     // pinned: the per-token upload is then a plain DMA instead of the driver's pageable staging
     int32_t *hbuf = nullptr;
     if (cudaMallocHost(&hbuf, sizeof(int32_t) * (keep + 3)) != cudaSuccess) {
         cudaGetLastError();
         cudaFreeAsync(dbuf, st);
+        if (a.work) cudaFreeAsync(a.work, st);
         return fail(LLMDOT_E_NOMEM, "generate_sampled: pinned staging allocation failed");
     }
     std::mt19937 rng(std::random_device{}());
@@ -1094,6 +1104,10 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
             break;
         }
         tok = x.h_pinned[2 * x.cap];
+        if (tok < 0) {
+            rc = fail(LLMDOT_E_UNSUPPORTED, "generate_sampled: a tie group of the nucleus above 8192 tokens");
+            break;
+        }
         out_tokens[produced++] = tok;
         recent.push_back(tok);
         if (recent.size() > (size_t)keep) recent.erase(recent.begin(), recent.end() - keep);
@@ -1109,6 +1123,7 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
         s->pos += 1;
     }
     cudaFreeAsync(dbuf, st);
+    if (a.work) cudaFreeAsync(a.work, st);
     cudaStreamSynchronize(st);
     cudaFreeHost(hbuf);
     if (rc == LLMDOT_OK) rc = check_err_flag(m);

@@ -433,22 +433,55 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
     pdl_launch();
     pdl_wait();
 
-    // ---- prologue pass A: sum of squares (norm) and max |x| per vector, all threads
-    {
+    // ---- prologue.  Short form (no int8 layout, 1/2/4 vectors, at most two fragment items per
+    // thread): each thread loads the x (and norm weight) elements of its fragment items once, the
+    // statistics need one barrier (every thread then derives the scales itself), and the offset
+    // term's sub-block sums come from the four partials' lanes by shuffles, in the same order as
+    // the general form below.
+    const int nlay = (a.need_q4 ? 1 : 0) + (a.need_q6 ? 1 : 0), per_lay = nsb * 32 * NV;
+    const bool short_pro = !I8 && (NV == 1 || NV == 2 || NV == 4) && nlay * per_lay <= 2 * NT;
+    if (short_pro) {
+        constexpr int IPT = 2;
+        const int ss_lay = a.need_q4 ? 0 : 1;  // the layout whose items cover x once
+        float c[IPT][8], nw[IPT][8];
+        int lay_of[IPT], it_of[IPT];
+#pragma unroll
+        for (int k = 0; k < IPT; k++) {
+            const int gi = tid + k * NT;
+            lay_of[k] = -1;
+            it_of[k] = 0;
+            if (gi < nlay * per_lay) {
+                const int lay = nlay == 2 ? (gi >= per_lay ? 1 : 0) : ss_lay, it = gi >= per_lay ? gi - per_lay : gi;
+                lay_of[k] = lay;
+                it_of[k] = it;
+                const int v = it % NV, r = it / NV, w = r & 7, tt = (r >> 3) & 3, sb = r >> 5;
+                const int e0 = lay == 0 ? sb * 256 + 64 * tt + 8 * w : sb * 256 + 32 * w + 4 * tt;
+                const int e1 = lay == 0 ? e0 + 4 : e0 + 16;
+                const float *h = a.x + (size_t)v * a.ldx;
+                const float4 p0 = *(const float4 *)(h + e0), p1 = *(const float4 *)(h + e1);
+                c[k][0] = p0.x, c[k][1] = p0.y, c[k][2] = p0.z, c[k][3] = p0.w;
+                c[k][4] = p1.x, c[k][5] = p1.y, c[k][6] = p1.z, c[k][7] = p1.w;
+                if (a.norm_w) {
+                    const float4 n0 = *(const float4 *)(a.norm_w + e0), n1 = *(const float4 *)(a.norm_w + e1);
+                    nw[k][0] = n0.x, nw[k][1] = n0.y, nw[k][2] = n0.z, nw[k][3] = n0.w;
+                    nw[k][4] = n1.x, nw[k][5] = n1.y, nw[k][6] = n1.z, nw[k][7] = n1.w;
+                }
+            }
+        }
         float ss[NV], mx[NV];
 #pragma unroll
         for (int v = 0; v < NV; v++) ss[v] = mx[v] = 0.0f;
-        for (int i = tid; i < cols; i += NT) {
-            const float wn = a.norm_w ? a.norm_w[i] : 1.0f;
 #pragma unroll
-            for (int v = 0; v < NV; v++) {
-                const float h = a.x[(size_t)v * a.ldx + i];
-                ss[v] = fmaf(h, h, ss[v]);
-                const float ax = fabsf(a.norm_w ? __fmul_rn(wn, h) : h);
-                mx[v] = fmaxf(mx[v], ax);
-                if (I8 && a.need_q4) {  // the warp's 32 consecutive elements share a super-block
-                    const float wm = warp_max(ax);
-                    if (lane == 0) atomicMax((unsigned *)xsc + v * nsb + (i >> 8), __float_as_uint(wm));
+        for (int k = 0; k < IPT; k++) {
+            if (lay_of[k] != ss_lay) continue;
+            const int v = it_of[k] % NV;
+#pragma unroll
+            for (int vv = 0; vv < NV; vv++) {
+                if (vv != v) continue;
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    ss[vv] = fmaf(c[k][q], c[k][q], ss[vv]);
+                    mx[vv] = fmaxf(mx[vv], fabsf(a.norm_w ? __fmul_rn(nw[k][q], c[k][q]) : c[k][q]));
                 }
             }
         }
@@ -464,16 +497,18 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
                 wred[warp * 2 * NV + NV + v] = mx[v];
             }
         __syncthreads();
-        if (tid < NV) {
-            float s = 0.0f, m = 0.0f;
+        float f_of[NV], sc_of[NV];
+#pragma unroll
+        for (int v = 0; v < NV; v++) {
+            float s2 = 0.0f, m = 0.0f;
             for (int w = 0; w < GEMV_WARPS; w++) {
-                s += wred[w * 2 * NV + tid];
-                m = fmaxf(m, wred[w * 2 * NV + NV + tid]);
+                s2 += wred[w * 2 * NV + v];
+                m = fmaxf(m, wred[w * 2 * NV + NV + v]);
             }
             float inv = 1.0f;
             if (a.norm_w) {  // VectorMath.RmsNorm: 1 / sqrt(ss/n + eps); x = (w*h)*inv
-                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)cols), a.eps)));
-                m = __fmul_rn(m, inv);  // rounding is monotone: max of the products
+                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s2, (float)cols), a.eps)));
+                m = __fmul_rn(m, inv);
             }
             float sc = 1.0f;  // exact power of two putting max|x|*sc in [2^14, 2^15)
             if (m > 0.0f && m < INFINITY) {
@@ -481,113 +516,209 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) gemv_mma_kernel(GemvArgs a, i
                 frexpf(m, &e);
                 sc = ldexpf(1.0f, 15 - e);
             }
-            stat[tid] = inv;
-            stat[NV + tid] = sc;
+            sc_of[v] = sc;
+            f_of[v] = a.norm_w ? inv * sc : sc;  // ((w*h)*inv)*sc == (w*h)*(inv*sc): sc is a power of two
+            if (tid == 0) {
+                stat[v] = inv;
+                stat[NV + v] = sc;
+            }
         }
-        __syncthreads();
-        if (I8 && a.need_q4)  // X = x * 2^k with the super-block's max |x| * 2^k in [2^29, 2^30)
-            for (int i = tid; i < NV * nsb; i += NT) {
-                float m = __uint_as_float(((const unsigned *)xsc)[i]);
-                if (a.norm_w) m = __fmul_rn(m, stat[i / nsb]);
-                int e = 0;
-                if (m > 0.0f && m < INFINITY) frexpf(m, &e);
-                e = max(e, -90);
-                xsc[i] = ldexpf(1.0f, 30 - e);
-                xinv[i] = ldexpf(1.0f, e - 30);
-            }
-    }
-    // ---- pass B: fp16 hi/lo fragments of the scaled x for the layouts in use
-    if (I8 && a.need_q4) {
-        __syncthreads();
-        // int8 form: item (v, sb, j, t) = elements 32j + 4t + b and 32j + 16 + 4t + b (b = 0..3) of
-        // super-block sb, as four signed digits of X (one 8-byte unit per digit); P gets the sum
-        // of the 8 normed values for the sub-block sums S
-        uint2 *xs8 = (uint2 *)xs4;
-        for (int it = tid; it < NV * nsb * 32; it += NT) {
-            const int tt = it & 3, j = (it >> 2) & 7, sb = (it >> 5) % nsb, v = it / (nsb * 32);
-            const int e0 = sb * 256 + 32 * j + 4 * tt;
-            const float *h = a.x + (size_t)v * a.ldx;
-            const float4 p0 = *(const float4 *)(h + e0), p1 = *(const float4 *)(h + e0 + 16);
-            float c[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-            if (a.norm_w) {
-                const float inv = stat[v];
-                const float4 n0 = *(const float4 *)(a.norm_w + e0), n1 = *(const float4 *)(a.norm_w + e0 + 16);
-                const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
 #pragma unroll
-                for (int k = 0; k < 8; k++) c[k] = __fmul_rn(__fmul_rn(nw[k], c[k]), inv);
-            }
-            float psum = 0.0f;
-#pragma unroll
-            for (int k = 0; k < 8; k++) psum += c[k];
-            P[((v * nsb + sb) * 4 + (j >> 1)) * 8 + 4 * (j & 1) + tt] = psum;
-            const float scale = xsc[v * nsb + sb];
-            uint32_t dg[4][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}};
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                int X = __float2int_rn(c[k] * scale);
-#pragma unroll
-                for (int dd = 0; dd < 4; dd++) {  // balanced base-256 digits
-                    const int dgt = dd < 3 ? (int)(int8_t)(X & 0xFF) : X;
-                    X = (X - dgt) >> 8;
-                    dg[dd][k >> 2] |= ((uint32_t)dgt & 0xFFu) << (8 * (k & 3));
-                }
-            }
-#pragma unroll
-            for (int dd = 0; dd < 4; dd++) xs8[x8unit<NV>(sb, j, tt, 4 * v + dd)] = make_uint2(dg[dd][0], dg[dd][1]);
-        }
-    }
-    for (int lay = 0; lay < 2; lay++) {
-        if ((lay == 0 && (I8 || !a.need_q4)) || (lay == 1 && !a.need_q6)) continue;
-        uint4 *xs = lay == 0 ? xs4 : xs6;
-        for (int it = tid; it < nsb * 32 * NV; it += NT) {
+        for (int k = 0; k < IPT; k++) {
+            if (lay_of[k] < 0) continue;  // warp-uniform: a layout's items fill whole warps
+            const int lay = lay_of[k], it = it_of[k];
             const int v = it % NV, r = it / NV, w = r & 7, tt = (r >> 3) & 3, sb = r >> 5;
-            // Q4_K: 8 consecutive weights 64t+8w.. in slot order {0,4,1,5,2,6,3,7};
-            // Q6_K: 4 at 32w+4t.. and 4 at 32w+16+4t.. in order
-            const int e0 = lay == 0 ? sb * 256 + 64 * tt + 8 * w : sb * 256 + 32 * w + 4 * tt;
-            const int e1 = lay == 0 ? e0 + 4 : e0 + 16;
-            const float *h = a.x + (size_t)v * a.ldx;
-            float4 p0 = *(const float4 *)(h + e0), p1 = *(const float4 *)(h + e1);
-            float c[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-            const float sc = stat[NV + v];
-            if (a.norm_w) {
-                // ((w*h)*inv)*sc == (w*h)*(inv*sc): sc is a power of two
-                const float f = stat[v] * sc;
-                const float4 n0 = *(const float4 *)(a.norm_w + e0), n1 = *(const float4 *)(a.norm_w + e1);
-                const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+            float f = 1.0f, scv = 1.0f;
 #pragma unroll
-                for (int k = 0; k < 8; k++) c[k] = __fmul_rn(__fmul_rn(nw[k], c[k]), f);
-            } else {
+            for (int vv = 0; vv < NV; vv++)
+                if (vv == v) {
+                    f = f_of[vv];
+                    scv = sc_of[vv];
+                }
+            float cc[8];
 #pragma unroll
-                for (int k = 0; k < 8; k++) c[k] *= sc;
-            }
+            for (int q = 0; q < 8; q++) cc[q] = a.norm_w ? __fmul_rn(__fmul_rn(nw[k][q], c[k][q]), f) : c[k][q] * scv;
             if (lay == 0) {
                 float psum = 0.0f;
 #pragma unroll
-                for (int k = 0; k < 8; k++) psum += c[k];
-                P[((v * nsb + sb) * 4 + tt) * 8 + w] = psum;
+                for (int q = 0; q < 8; q++) psum += cc[q];
+                // S_j: the partials of w = 4 (j & 1) .. + 3 sit NV lanes apart in this warp
+                const float p1 = __shfl_down_sync(0xffffffffu, psum, NV), p2 = __shfl_down_sync(0xffffffffu, psum, 2 * NV),
+                            p3 = __shfl_down_sync(0xffffffffu, psum, 3 * NV);
+                if ((w & 3) == 0) S[(v * nsb + sb) * 8 + 2 * tt + (w >> 2)] = ((psum + p1) + p2) + p3;
             }
             float o[8];
 #pragma unroll
-            for (int k = 0; k < 8; k++) o[k] = lay == 0 ? c[(k >> 1) + 4 * (k & 1)] : c[k];
+            for (int q = 0; q < 8; q++) o[q] = lay == 0 ? cc[(q >> 1) + 4 * (q & 1)] : cc[q];
             uint32_t hi[4], lo[4];
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                __half2 hh = __floats2half2_rn(o[2 * k], o[2 * k + 1]);
+            for (int q = 0; q < 4; q++) {
+                __half2 hh = __floats2half2_rn(o[2 * q], o[2 * q + 1]);
                 float2 hf = __half22float2(hh);
-                hi[k] = *reinterpret_cast<uint32_t *>(&hh);
-                lo[k] = pack_half2(o[2 * k] - hf.x, o[2 * k + 1] - hf.y);
+                hi[q] = *reinterpret_cast<uint32_t *>(&hh);
+                lo[q] = pack_half2(o[2 * q] - hf.x, o[2 * q + 1] - hf.y);
             }
+            uint4 *xs = lay == 0 ? xs4 : xs6;
             xs[xunit<NV>(sb, tt, w, v, 0)] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             xs[xunit<NV>(sb, tt, w, v, 1)] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
-    }
-    if (a.need_q4) {
-        __syncthreads();
-        // pass C: sub-block sums S_j = sum of its four 8-weight partials, fixed order
-        for (int it = tid; it < NV * nsb * 8; it += NT) {
-            const int v = it / (nsb * 8), jj = it % (nsb * 8), sb = jj >> 3, j = jj & 7;
-            const float *pp = P + ((v * nsb + sb) * 4 + (j >> 1)) * 8 + 4 * (j & 1);
-            S[it] = ((pp[0] + pp[1]) + pp[2]) + pp[3];
+    } else {
+        // ---- prologue pass A: sum of squares (norm) and max |x| per vector, all threads
+        {
+            float ss[NV], mx[NV];
+    #pragma unroll
+            for (int v = 0; v < NV; v++) ss[v] = mx[v] = 0.0f;
+            for (int i = tid; i < cols; i += NT) {
+                const float wn = a.norm_w ? a.norm_w[i] : 1.0f;
+    #pragma unroll
+                for (int v = 0; v < NV; v++) {
+                    const float h = a.x[(size_t)v * a.ldx + i];
+                    ss[v] = fmaf(h, h, ss[v]);
+                    const float ax = fabsf(a.norm_w ? __fmul_rn(wn, h) : h);
+                    mx[v] = fmaxf(mx[v], ax);
+                    if (I8 && a.need_q4) {  // the warp's 32 consecutive elements share a super-block
+                        const float wm = warp_max(ax);
+                        if (lane == 0) atomicMax((unsigned *)xsc + v * nsb + (i >> 8), __float_as_uint(wm));
+                    }
+                }
+            }
+    #pragma unroll
+            for (int v = 0; v < NV; v++) {
+                ss[v] = warp_sum(ss[v]);
+                mx[v] = warp_max(mx[v]);
+            }
+            if (lane == 0)
+    #pragma unroll
+                for (int v = 0; v < NV; v++) {
+                    wred[warp * 2 * NV + v] = ss[v];
+                    wred[warp * 2 * NV + NV + v] = mx[v];
+                }
+            __syncthreads();
+            if (tid < NV) {
+                float s = 0.0f, m = 0.0f;
+                for (int w = 0; w < GEMV_WARPS; w++) {
+                    s += wred[w * 2 * NV + tid];
+                    m = fmaxf(m, wred[w * 2 * NV + NV + tid]);
+                }
+                float inv = 1.0f;
+                if (a.norm_w) {  // VectorMath.RmsNorm: 1 / sqrt(ss/n + eps); x = (w*h)*inv
+                    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)cols), a.eps)));
+                    m = __fmul_rn(m, inv);  // rounding is monotone: max of the products
+                }
+                float sc = 1.0f;  // exact power of two putting max|x|*sc in [2^14, 2^15)
+                if (m > 0.0f && m < INFINITY) {
+                    int e;
+                    frexpf(m, &e);
+                    sc = ldexpf(1.0f, 15 - e);
+                }
+                stat[tid] = inv;
+                stat[NV + tid] = sc;
+            }
+            __syncthreads();
+            if (I8 && a.need_q4)  // X = x * 2^k with the super-block's max |x| * 2^k in [2^29, 2^30)
+                for (int i = tid; i < NV * nsb; i += NT) {
+                    float m = __uint_as_float(((const unsigned *)xsc)[i]);
+                    if (a.norm_w) m = __fmul_rn(m, stat[i / nsb]);
+                    int e = 0;
+                    if (m > 0.0f && m < INFINITY) frexpf(m, &e);
+                    e = max(e, -90);
+                    xsc[i] = ldexpf(1.0f, 30 - e);
+                    xinv[i] = ldexpf(1.0f, e - 30);
+                }
+        }
+        // ---- pass B: fp16 hi/lo fragments of the scaled x for the layouts in use
+        if (I8 && a.need_q4) {
+            __syncthreads();
+            // int8 form: item (v, sb, j, t) = elements 32j + 4t + b and 32j + 16 + 4t + b (b = 0..3) of
+            // super-block sb, as four signed digits of X (one 8-byte unit per digit); P gets the sum
+            // of the 8 normed values for the sub-block sums S
+            uint2 *xs8 = (uint2 *)xs4;
+            for (int it = tid; it < NV * nsb * 32; it += NT) {
+                const int tt = it & 3, j = (it >> 2) & 7, sb = (it >> 5) % nsb, v = it / (nsb * 32);
+                const int e0 = sb * 256 + 32 * j + 4 * tt;
+                const float *h = a.x + (size_t)v * a.ldx;
+                const float4 p0 = *(const float4 *)(h + e0), p1 = *(const float4 *)(h + e0 + 16);
+                float c[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+                if (a.norm_w) {
+                    const float inv = stat[v];
+                    const float4 n0 = *(const float4 *)(a.norm_w + e0), n1 = *(const float4 *)(a.norm_w + e0 + 16);
+                    const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+    #pragma unroll
+                    for (int k = 0; k < 8; k++) c[k] = __fmul_rn(__fmul_rn(nw[k], c[k]), inv);
+                }
+                float psum = 0.0f;
+    #pragma unroll
+                for (int k = 0; k < 8; k++) psum += c[k];
+                P[((v * nsb + sb) * 4 + (j >> 1)) * 8 + 4 * (j & 1) + tt] = psum;
+                const float scale = xsc[v * nsb + sb];
+                uint32_t dg[4][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}};
+    #pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    int X = __float2int_rn(c[k] * scale);
+    #pragma unroll
+                    for (int dd = 0; dd < 4; dd++) {  // balanced base-256 digits
+                        const int dgt = dd < 3 ? (int)(int8_t)(X & 0xFF) : X;
+                        X = (X - dgt) >> 8;
+                        dg[dd][k >> 2] |= ((uint32_t)dgt & 0xFFu) << (8 * (k & 3));
+                    }
+                }
+    #pragma unroll
+                for (int dd = 0; dd < 4; dd++) xs8[x8unit<NV>(sb, j, tt, 4 * v + dd)] = make_uint2(dg[dd][0], dg[dd][1]);
+            }
+        }
+        for (int lay = 0; lay < 2; lay++) {
+            if ((lay == 0 && (I8 || !a.need_q4)) || (lay == 1 && !a.need_q6)) continue;
+            uint4 *xs = lay == 0 ? xs4 : xs6;
+            for (int it = tid; it < nsb * 32 * NV; it += NT) {
+                const int v = it % NV, r = it / NV, w = r & 7, tt = (r >> 3) & 3, sb = r >> 5;
+                // Q4_K: 8 consecutive weights 64t+8w.. in slot order {0,4,1,5,2,6,3,7};
+                // Q6_K: 4 at 32w+4t.. and 4 at 32w+16+4t.. in order
+                const int e0 = lay == 0 ? sb * 256 + 64 * tt + 8 * w : sb * 256 + 32 * w + 4 * tt;
+                const int e1 = lay == 0 ? e0 + 4 : e0 + 16;
+                const float *h = a.x + (size_t)v * a.ldx;
+                float4 p0 = *(const float4 *)(h + e0), p1 = *(const float4 *)(h + e1);
+                float c[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+                const float sc = stat[NV + v];
+                if (a.norm_w) {
+                    // ((w*h)*inv)*sc == (w*h)*(inv*sc): sc is a power of two
+                    const float f = stat[v] * sc;
+                    const float4 n0 = *(const float4 *)(a.norm_w + e0), n1 = *(const float4 *)(a.norm_w + e1);
+                    const float nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+    #pragma unroll
+                    for (int k = 0; k < 8; k++) c[k] = __fmul_rn(__fmul_rn(nw[k], c[k]), f);
+                } else {
+    #pragma unroll
+                    for (int k = 0; k < 8; k++) c[k] *= sc;
+                }
+                if (lay == 0) {
+                    float psum = 0.0f;
+    #pragma unroll
+                    for (int k = 0; k < 8; k++) psum += c[k];
+                    P[((v * nsb + sb) * 4 + tt) * 8 + w] = psum;
+                }
+                float o[8];
+    #pragma unroll
+                for (int k = 0; k < 8; k++) o[k] = lay == 0 ? c[(k >> 1) + 4 * (k & 1)] : c[k];
+                uint32_t hi[4], lo[4];
+    #pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    __half2 hh = __floats2half2_rn(o[2 * k], o[2 * k + 1]);
+                    float2 hf = __half22float2(hh);
+                    hi[k] = *reinterpret_cast<uint32_t *>(&hh);
+                    lo[k] = pack_half2(o[2 * k] - hf.x, o[2 * k + 1] - hf.y);
+                }
+                xs[xunit<NV>(sb, tt, w, v, 0)] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                xs[xunit<NV>(sb, tt, w, v, 1)] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+        }
+        if (a.need_q4) {
+            __syncthreads();
+            // pass C: sub-block sums S_j = sum of its four 8-weight partials, fixed order
+            for (int it = tid; it < NV * nsb * 8; it += NT) {
+                const int v = it / (nsb * 8), jj = it % (nsb * 8), sb = jj >> 3, j = jj & 7;
+                const float *pp = P + ((v * nsb + sb) * 4 + (j >> 1)) * 8 + 4 * (j & 1);
+                S[it] = ((pp[0] + pp[1]) + pp[2]) + pp[3];
+            }
         }
     }
     __syncthreads();

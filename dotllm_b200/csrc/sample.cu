@@ -14,9 +14,25 @@
 // Temperature <= 0 is the greedy argmax of the softcapped row (lowest index on ties).  Equal values
 // at the k-th place are taken lowest index first and equal winners are ordered by index; the
 // reference orders them by its replacement scan instead (FindTopK :83-127), which only matters for
-// exactly tied logits.  The top-p-only path (top_k <= 0 or >= n) is not on the device.
+// exactly tied logits.
+//
+// top_k <= 0 or top_k >= n (Sampler.cs:42-61): VectorMath.Softmax over the whole row (the FindMax
+// lane rule, ExpApprox in the 8-wide lanes with the lanes' running sums, exp in the tail), then
+//   * top_p >= 1: the first index whose running sum reaches r;
+//   * top_p < 1: FindNucleus (:129-151) -- the selection sort by probability, the prefix whose
+//     running sum first reaches top_p, renormalised, and the pick inside it.  The reference passes
+//     one buffer as both the probabilities and the nucleus values (:48-50), so the value written at
+//     sorted position i is the probability of token idx[i] unless that token's slot was already
+//     overwritten (idx[i] < i), in which case it is the value written there; when the nucleus is
+//     the whole row the pick then runs over the overwritten row and returns a position.  The device
+//     sorts (value, index) pairs with a stable radix sort; while no two of the prefix's values tie,
+//     that is the selection sort's order, and the aliased values follow the chain
+//     i -> idx[i] while idx[i] < i.  A tie inside the prefix replays the selection sort's swaps on
+//     one thread (each tie group ordered by its members' current positions).
+// The running sums are sequential fp32 adds in the reference's order, on one thread.
 #include "sample.cuh"
 
+#include <cub/device/device_radix_sort.cuh>
 #include <string>
 
 namespace llmdot {
@@ -52,6 +68,93 @@ __host__ __device__ inline SampleSmem sample_layout(int n, int window, int k2)
     return L;
 }
 
+// The row's values as the sampler sees them: softcap (vector-lane rule), repeat penalty, 1/T.
+struct RowValues {
+    const float *x;
+    int nvec, has_cap, np;
+    float cap, inv_cap, inv_temp;
+    const uint32_t *bitmap;
+    const int *ptok;
+    const float *pval;
+    __device__ __forceinline__ float capped(int i) const
+    {
+        const float v = x[i];
+        return has_cap ? softcap_ref(v, cap, inv_cap, i < nvec) : v;
+    }
+    // the scaled value of token i (VectorMath.Scale: x * (1/T) in every lane)
+    __device__ __forceinline__ float value(int i) const
+    {
+        float v;
+        if (np && ((bitmap[i >> 5] >> (i & 31)) & 1u)) {
+            int j = 0;
+            while (ptok[j] != i) j++;
+            v = pval[j];
+        } else {
+            v = capped(i);
+        }
+        return __fmul_rn(v, inv_temp);
+    }
+};
+
+// Repeat penalty (ApplyRepeatPenalty :64-81), by the whole block: the last `window` history tokens
+// in order, each occurrence applied once (a token that appears twice is divided twice).  The
+// window's values are loaded in parallel into wval; one thread then applies the penalty.  Fills
+// the bitmap and (ptok, pval) of the distinct penalised tokens and returns their number.
+__device__ int penalty_setup(const SampleArgs &a, int row, RowValues &rv, uint32_t *bitmap, int *ptok, float *pval,
+                             float *wval, int *np_slot)
+{
+    const int tid = threadIdx.x, n = a.n, window = a.window;
+    for (int i = tid; i < (n + 31) / 32; i += blockDim.x) bitmap[i] = 0u;
+    const bool pen = a.penalty != 1.0f && window > 0 && a.recent;
+    const int plen = pen ? a.recent_len[row] : 0, p0 = max(0, plen - window);
+    const int32_t *rec = pen ? a.recent + (size_t)row * a.recent_ld : nullptr;
+    for (int i = p0 + tid; i < plen; i += blockDim.x) {
+        const int t = rec[i];
+        wval[i - p0] = (t >= 0 && t < n) ? rv.capped(t) : 0.0f;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int np = 0;
+        for (int i = p0; i < plen; i++) {
+            const int t = rec[i];
+            if (t < 0 || t >= n) continue;
+            int j = 0;
+            while (j < np && ptok[j] != t) j++;
+            if (j == np) {
+                ptok[np] = t;
+                pval[np] = wval[i - p0];
+                np++;
+                bitmap[t >> 5] |= 1u << (t & 31);
+            }
+            pval[j] = pval[j] > 0.0f ? __fdiv_rn(pval[j], a.penalty) : __fmul_rn(pval[j], a.penalty);
+        }
+        *np_slot = np;
+    }
+    __syncthreads();
+    const int np = *np_slot;
+    rv.bitmap = bitmap;
+    rv.ptok = ptok;
+    rv.pval = pval;
+    rv.np = np;
+    return np;
+}
+
+__device__ __forceinline__ RowValues row_values(const SampleArgs &a, int row)
+{
+    RowValues rv;
+    rv.x = a.logits + (size_t)row * a.ld;
+    rv.nvec = a.n - a.n % 8;
+    rv.has_cap = a.has_cap;
+    rv.cap = a.cap;
+    rv.inv_cap = a.inv_cap;
+    rv.inv_temp = a.inv_temp;
+    rv.np = 0;
+    rv.bitmap = nullptr;
+    rv.ptok = nullptr;
+    rv.pval = nullptr;
+    return rv;
+}
+
 __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k2)
 {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -65,12 +168,8 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
     unsigned long long *cand = (unsigned long long *)(smem + L.cand);
     uint32_t *skey = (uint32_t *)(smem + L.skey);
     float *prob = (float *)(smem + L.prob);
-    const float *x = a.logits + (size_t)row * a.ld;
-    const int nvec = n - n % 8;
-    auto capped = [&](int i) {
-        const float v = x[i];
-        return a.has_cap ? softcap_ref(v, a.cap, a.inv_cap, i < nvec) : v;
-    };
+    RowValues rv = row_values(a, row);
+    auto capped = [&](int i) { return rv.capped(i); };
 
     if (a.temperature <= 0.0f) {  // Temperature <= 0: ArgMax (Sampler.cs:26-27)
         unsigned long long best = 0;
@@ -104,50 +203,9 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
         return;
     }
 
-    // ---- repeat penalty (ApplyRepeatPenalty :64-81): the last `window` tokens, in order.  The
-    // window's values are loaded in parallel (into the candidate buffer, not yet in use);
-    // one thread then applies the penalty occurrence by occurrence.
-    for (int i = tid; i < (n + 31) / 32; i += SMP_THREADS) bitmap[i] = 0u;
-    const bool pen = a.penalty != 1.0f && window > 0 && a.recent;
-    const int plen = pen ? a.recent_len[row] : 0, p0 = max(0, plen - window);
-    const int32_t *rec = pen ? a.recent + (size_t)row * a.recent_ld : nullptr;
-    float *wval = (float *)cand;  // window values, index i - p0 (the candidates come later)
-    for (int i = p0 + tid; i < plen; i += SMP_THREADS) {
-        const int t = rec[i];
-        wval[i - p0] = (t >= 0 && t < n) ? capped(t) : 0.0f;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        int np = 0;
-        for (int i = p0; i < plen; i++) {
-            const int t = rec[i];
-            if (t < 0 || t >= n) continue;
-            int j = 0;
-            while (j < np && ptok[j] != t) j++;
-            if (j == np) {
-                ptok[np] = t;
-                pval[np] = wval[i - p0];
-                np++;
-                bitmap[t >> 5] |= 1u << (t & 31);
-            }
-            pval[j] = pval[j] > 0.0f ? __fdiv_rn(pval[j], a.penalty) : __fmul_rn(pval[j], a.penalty);
-        }
-        hist[256] = np;
-    }
-    __syncthreads();
-    const int np = hist[256];
-    // the scaled value of token i (VectorMath.Scale: x * (1/T) in every lane)
-    auto value = [&](int i) {
-        float v;
-        if (np && ((bitmap[i >> 5] >> (i & 31)) & 1u)) {
-            int j = 0;
-            while (ptok[j] != i) j++;
-            v = pval[j];
-        } else {
-            v = capped(i);
-        }
-        return __fmul_rn(v, a.inv_temp);
-    };
+    // ---- repeat penalty (the window's values are staged in the candidate buffer, not yet in use)
+    penalty_setup(a, row, rv, bitmap, ptok, pval, (float *)cand, &hist[256]);
+    auto value = [&](int i) { return rv.value(i); };
 
     const int k = a.top_k;
     int sort_n = k2;  // entries of cand to sort
@@ -343,6 +401,371 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
     }
 }
 
+// ---------------------------------------------------------------- full-row path (top_k <= 0 or >= n)
+constexpr int SF_CHUNK = 8192;    // values staged in shared memory per step of a sequential scan
+constexpr int SF_GROUP = 8192;    // largest tie group the selection-sort replay orders in shared memory
+constexpr int SF_TIE_GROUP_TOO_LARGE = -2;  // written as the sampled id when SF_GROUP is exceeded
+
+static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+static size_t cub_sort_bytes(int n)
+{
+    size_t tb = 0;
+    cub::DeviceRadixSort::SortPairsDescending(nullptr, tb, (const uint32_t *)nullptr, (uint32_t *)nullptr,
+                                              (const int32_t *)nullptr, (int32_t *)nullptr, n);
+    return tb;
+}
+
+size_t sample_work_bytes(int n)
+{
+    return 8 * align256(sizeof(float) * (size_t)n) + align256(cub_sort_bytes(n));
+}
+
+static SampleWork work_carve(void *base, int n)
+{
+    SampleWork w;
+    uint8_t *p = (uint8_t *)base;
+    const size_t a = align256(sizeof(float) * (size_t)n);
+    w.p = (float *)p;
+    w.val = (float *)(p + a);
+    w.kin = (uint32_t *)(p + 2 * a);
+    w.kout = (uint32_t *)(p + 3 * a);
+    w.iin = (int32_t *)(p + 4 * a);
+    w.iout = (int32_t *)(p + 5 * a);
+    w.pos = (int32_t *)(p + 6 * a);
+    w.at = (int32_t *)(p + 7 * a);
+    w.cub = p + 8 * a;
+    w.cub_bytes = cub_sort_bytes(n);
+    return w;
+}
+
+struct SampleFullSmem {
+    int bitmap, ptok, pval, wval, misc, chunk, group, total;  // byte offsets
+};
+__host__ __device__ inline SampleFullSmem sample_full_layout(int n, int window, bool probs)
+{
+    SampleFullSmem L;
+    int o = 0;
+    L.bitmap = o;
+    o += probs ? ((n + 31) / 32 * 4 + 15) / 16 * 16 : 0;
+    L.ptok = o;
+    o += probs ? (window * 4 + 15) / 16 * 16 : 0;
+    L.pval = o;
+    o += probs ? (window * 4 + 15) / 16 * 16 : 0;
+    L.wval = o;
+    o += probs ? (window * 4 + 15) / 16 * 16 : 0;
+    L.misc = o;  // 32 floats / ints of block reductions and broadcasts
+    o += 32 * 4 + 16 * 4;
+    L.chunk = o;
+    o += SF_CHUNK * 4;
+    L.group = o;  // (position << 32 | token) keys of one tie group
+    o += probs ? 0 : SF_GROUP * 8;
+    L.total = o;
+    return L;
+}
+
+// The first i in [0, len) at which the running fp32 sum of v[0..i] (each times `scale` first when
+// `scaled`) reaches thr, or -1.  One thread adds in index order (the reference's loops); the block
+// stages the values in shared memory.  *sum_out (thread 0): the running sum where the scan stopped.
+__device__ int seq_reach(const float *v, int len, bool scaled, float scale, float thr, float *chunk, int *flag,
+                         float *sum_out)
+{
+    float cum = 0.0f;
+    int hit = -1;
+    for (int base = 0; base < len; base += SF_CHUNK) {
+        const int m = min(SF_CHUNK, len - base);
+        for (int j = threadIdx.x; j < m; j += blockDim.x) chunk[j] = v[base + j];
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int j = 0; j < m; j++) {
+                cum = __fadd_rn(cum, scaled ? __fmul_rn(chunk[j], scale) : chunk[j]);
+                if (cum >= thr) {  // SampleFromProbabilities: r <= cum; FindNucleus: cum >= top_p
+                    hit = base + j;
+                    break;
+                }
+            }
+            *flag = hit;
+        }
+        __syncthreads();
+        hit = *flag;
+        __syncthreads();
+        if (hit >= 0) break;
+    }
+    if (threadIdx.x == 0 && sum_out) *sum_out = cum;
+    return hit;
+}
+
+// Softmax of the whole row into w.p (and the sort keys when the nucleus follows); without the
+// nucleus, also the pick.
+__global__ void __launch_bounds__(SMP_THREADS) sample_probs_kernel(SampleArgs a, SampleWork w, int nucleus)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int n = a.n, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const SampleFullSmem L = sample_full_layout(n, a.window, true);
+    float *misc = (float *)(smem + L.misc), *chunk = (float *)(smem + L.chunk);
+    int *imisc = (int *)(misc + 32);
+    RowValues rv = row_values(a, 0);
+    penalty_setup(a, 0, rv, (uint32_t *)(smem + L.bitmap), (int *)(smem + L.ptok), (float *)(smem + L.pval),
+                  (float *)(smem + L.wval), &imisc[0]);
+    // ---- values, and FindMax (:260-284): with n >= 8, lane l of the 8-wide loop starts from
+    // element l and keeps it if it is NaN (no later element compares greater); NaN never wins; so
+    // the max is over the non-NaN elements outside NaN-started lanes.  With n < 8: x[0], then `>`.
+    const int nv8 = n - n % 8;
+    uint32_t nan_lanes = 0;
+    if (n >= 8)
+        for (int l = 0; l < 8; l++) nan_lanes |= (uint32_t)(rv.value(l) != rv.value(l)) << l;
+    float mx = -INFINITY;
+    for (int i = tid; i < n; i += SMP_THREADS) {
+        const float v = rv.value(i);
+        w.p[i] = v;
+        const bool ok = v == v && !(i < nv8 && ((nan_lanes >> (i & 7)) & 1u));
+        if (ok) mx = fmaxf(mx, v);
+    }
+    mx = warp_max(mx);
+    if (lane == 0) misc[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float m = -INFINITY;
+        for (int q = 0; q < SMP_THREADS / 32; q++) m = fmaxf(m, misc[q]);
+        if (n < 8) {
+            m = w.p[0];
+            for (int i = 1; i < n; i++)
+                if (w.p[i] > m) m = w.p[i];
+        }
+        misc[0] = m;
+    }
+    __syncthreads();
+    const float M = misc[0];
+    // ---- e = ExpApprox(x - max) in the 8-wide lanes, exp in the tail (Softmax :215-258)
+    for (int i = tid; i < n; i += SMP_THREADS) {
+        const float d = __fsub_rn(w.p[i], M);
+        w.p[i] = i < nv8 ? exp_approx(d) : expf(d);
+    }
+    __syncthreads();
+    // ---- the lanes' running sums (lane l adds elements l, l + 8, ... in order), staged in chunks
+    float acc = 0.0f;
+    for (int base = 0; base < nv8; base += SF_CHUNK) {
+        const int m = min(SF_CHUNK, nv8 - base);
+        for (int j = tid; j < m; j += SMP_THREADS) chunk[j] = w.p[base + j];
+        __syncthreads();
+        if (tid < 8)
+            for (int j = tid; j < m; j += 8) acc = __fadd_rn(acc, chunk[j]);
+        __syncthreads();
+    }
+    if (warp == 0) {
+        // ((l0 + l1) + (l2 + l3)) + ((l4 + l5) + (l6 + l7)), then the tail in order
+        if (lane >= 8) acc = 0.0f;
+        const float s1 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+        const float s2 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 2));
+        const float s4 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 4));
+        if (lane == 0) {
+            float sum = n >= 8 ? s4 : 0.0f;
+            for (int j = nv8; j < n; j++) sum = __fadd_rn(sum, w.p[j]);
+            misc[1] = __fdiv_rn(1.0f, sum);
+        }
+    }
+    __syncthreads();
+    const float inv = misc[1];
+    for (int i = tid; i < n; i += SMP_THREADS) {
+        const float pr = __fmul_rn(w.p[i], inv);
+        w.p[i] = pr;
+        if (nucleus) {
+            w.kin[i] = float_key(pr);
+            w.iin[i] = i;
+        }
+    }
+    __syncthreads();
+    if (nucleus) return;
+    // ---- SampleFromProbabilities (:153-165) over the whole row
+    const int hit = seq_reach(w.p, n, false, 1.0f, a.r[0], chunk, &imisc[1], nullptr);
+    if (tid == 0) {
+        const int idx = hit >= 0 ? hit : n - 1;
+        a.out[0] = idx;
+        if (a.next) a.next[0] = idx;
+    }
+}
+
+// FindNucleus on the sorted (probability, token) pairs, then the pick.
+__global__ void __launch_bounds__(SMP_THREADS) sample_nucleus_kernel(SampleArgs a, SampleWork w)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int n = a.n, tid = threadIdx.x;
+    const SampleFullSmem L = sample_full_layout(n, a.window, false);
+    float *misc = (float *)(smem + L.misc), *chunk = (float *)(smem + L.chunk);
+    int *imisc = (int *)(misc + 32);
+    unsigned long long *grp = (unsigned long long *)(smem + L.group);
+    const float top_p = a.top_p;
+    // first sorted position i whose value equals the next one's
+    if (tid == 0) imisc[0] = n;
+    __syncthreads();
+    for (int i = tid; i + 1 < n; i += SMP_THREADS)
+        if (w.kout[i] == w.kout[i + 1]) atomicMin(&imisc[0], i);
+    // values written at each sorted position (the aliased buffer): follow i -> idx[i] while idx[i] < i
+    for (int i = tid; i < n; i += SMP_THREADS) {
+        int j = i, sel = w.iout[i];
+        while (sel < j) {
+            j = sel;
+            sel = w.iout[j];
+        }
+        w.val[i] = w.p[sel];
+    }
+    __syncthreads();
+    const int t0 = imisc[0];
+    const int hit = seq_reach(w.val, n, false, 1.0f, top_p, chunk, &imisc[1], &misc[0]);
+    int count = hit >= 0 ? hit + 1 : n;
+    const float *vals = w.val;
+    const int32_t *idx = w.iout;
+    if (t0 <= count - 1) {
+        // ---- a tie inside the prefix: replay the selection sort.  pos / at: current position of
+        // each token / token at each position; the aliased writes go to w.p in place.
+        int32_t *nidx = (int32_t *)w.kin;  // the sorted order this replay produces
+        for (int e = tid; e < n; e += SMP_THREADS) {
+            w.pos[e] = e;
+            w.at[e] = e;
+        }
+        __syncthreads();
+        // thread 0's state: pass i, group start g, running sum, done (count found), group size
+        int i = 0, g = 0;
+        float cum = 0.0f;
+        if (tid == 0) imisc[2] = 0;  // done
+        for (;;) {
+            if (tid == 0) {
+                int done = 0, m = 0;
+                auto take = [&](int sel) {  // one pass of the selection sort selects token sel
+                    const int o = w.at[i];
+                    if (o != sel) {
+                        const int ps = w.pos[sel];
+                        w.at[ps] = o;
+                        w.pos[o] = ps;
+                        w.at[i] = sel;
+                        w.pos[sel] = i;
+                    }
+                    nidx[i] = sel;
+                    const float v = w.p[sel];  // slot sel holds a written value when sel < i
+                    w.p[i] = v;
+                    cum = __fadd_rn(cum, v);
+                    i++;
+                    if (cum >= top_p) done = 1;
+                };
+                while (!done && g < n) {
+                    int ge = g + 1;
+                    while (ge < n && w.kout[ge] == w.kout[g]) ge++;
+                    if (ge - g == 1) {
+                        take(w.iout[g]);
+                        g = ge;
+                    } else {
+                        m = ge - g;
+                        break;
+                    }
+                }
+                imisc[2] = done || g >= n ? 1 : 0;
+                imisc[3] = g;
+                imisc[4] = m;
+                misc[0] = cum;
+            }
+            __syncthreads();
+            if (imisc[2]) break;
+            const int gs = imisc[3], m = imisc[4];
+            if (m > SF_GROUP) {
+                if (tid == 0) a.out[0] = SF_TIE_GROUP_TOO_LARGE;
+                return;
+            }
+            // the group's members ordered by their current positions (bitonic sort, ascending)
+            int m2 = 2;
+            while (m2 < m) m2 <<= 1;
+            for (int k = tid; k < m2; k += SMP_THREADS) {
+                const int e = k < m ? w.iout[gs + k] : 0;
+                grp[k] = k < m ? ((unsigned long long)(uint32_t)w.pos[e] << 32) | (uint32_t)e : ~0ull;
+            }
+            __syncthreads();
+            for (int size = 2; size <= m2; size <<= 1)
+                for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                    for (int q = tid; q < m2 / 2; q += SMP_THREADS) {
+                        const int lo = 2 * q - (q & (stride - 1)), hi = lo + stride;
+                        const bool asc = (lo & size) == 0;
+                        const unsigned long long A = grp[lo], B = grp[hi];
+                        if ((A > B) == asc) {
+                            grp[lo] = B;
+                            grp[hi] = A;
+                        }
+                    }
+                    __syncthreads();
+                }
+            if (tid == 0) {
+                int done = 0;
+                for (int k = 0; k < m && !done; k++) {
+                    const int sel = (int)(uint32_t)grp[k];
+                    const int o = w.at[i];
+                    if (o != sel) {
+                        const int ps = w.pos[sel];
+                        w.at[ps] = o;
+                        w.pos[o] = ps;
+                        w.at[i] = sel;
+                        w.pos[sel] = i;
+                    }
+                    nidx[i] = sel;
+                    const float v = w.p[sel];
+                    w.p[i] = v;
+                    cum = __fadd_rn(cum, v);
+                    i++;
+                    if (cum >= top_p) done = 1;
+                }
+                g = gs + m;
+                imisc[2] = done || g >= n ? 1 : 0;
+                misc[0] = cum;
+            }
+            __syncthreads();
+            if (imisc[2]) break;
+        }
+        if (tid == 0) imisc[5] = i;  // passes run: the count (n when the sum never reached top_p)
+        __syncthreads();
+        count = imisc[5];
+        vals = w.p;
+        idx = nidx;
+    }
+    __syncthreads();
+    // ---- Sample :51-61: the nucleus renormalised (its sum is the running sum where it stopped),
+    // or, when it is the whole row, the pick over the overwritten row (a position)
+    const float sum = misc[0];
+    __syncthreads();
+    int out;
+    if (count < n) {
+        const float inv = __fdiv_rn(1.0f, sum);
+        const int h2 = seq_reach(vals, count, true, inv, a.r[0], chunk, &imisc[1], nullptr);
+        out = idx[h2 >= 0 ? h2 : count - 1];
+    } else {
+        const int h2 = seq_reach(vals, n, false, 1.0f, a.r[0], chunk, &imisc[1], nullptr);
+        out = h2 >= 0 ? h2 : n - 1;
+    }
+    if (tid == 0) {
+        a.out[0] = out;
+        if (a.next) a.next[0] = out;
+    }
+}
+
+static int launch_sample_full(const SampleArgs &a, int rows, cudaStream_t st)
+{
+    if (rows != 1) return fail(LLMDOT_E_UNSUPPORTED, "sample: the full-row path takes one row");
+    if (!a.work) return fail(LLMDOT_E_INVALID, "sample: the full-row path needs its work buffer");
+    if (a.n > (1 << 30) / 8) return fail(LLMDOT_E_UNSUPPORTED, "sample: vocabulary too large for the full-row path");
+    const SampleWork w = work_carve(a.work, a.n);
+    const bool nucleus = a.top_p < 1.0f;
+    const size_t s1 = sample_full_layout(a.n, a.window, true).total, s2 = sample_full_layout(a.n, a.window, false).total;
+    if (s1 > 200 * 1024 || s2 > 200 * 1024)
+        return fail(LLMDOT_E_UNSUPPORTED, "sample: vocabulary too large for the token bitmap");
+    static std::atomic<unsigned long long> attr1{0}, attr2{0};
+    LLMDOT_CUDA_TRY(smem_attr_once(attr1, sample_probs_kernel, 200 * 1024));
+    LLMDOT_CUDA_TRY(smem_attr_once(attr2, sample_nucleus_kernel, 200 * 1024));
+    sample_probs_kernel<<<1, SMP_THREADS, s1, st>>>(a, w, nucleus ? 1 : 0);
+    LLMDOT_CUDA_TRY(cudaGetLastError());
+    if (!nucleus) return LLMDOT_OK;
+    size_t tb = w.cub_bytes;
+    LLMDOT_CUDA_TRY(cub::DeviceRadixSort::SortPairsDescending(w.cub, tb, w.kin, w.kout, w.iin, w.iout, a.n, 0, 32, st));
+    sample_nucleus_kernel<<<1, SMP_THREADS, s2, st>>>(a, w);
+    LLMDOT_CUDA_TRY(cudaGetLastError());
+    return LLMDOT_OK;
+}
+
 // candidates, a power of two: at least one per warp (the greedy path parks warp maxima there)
 static int k2_for(int k)
 {
@@ -360,11 +783,12 @@ int launch_sample(const SampleArgs &a, int rows, cudaStream_t st)
 {
     if (rows < 1 || a.n < 1 || !a.logits || !a.out || !a.r)
         return fail(LLMDOT_E_INVALID, "sample: bad arguments");
-    if (a.temperature > 0.0f && (a.top_k <= 0 || a.top_k >= a.n || a.top_k > SAMPLE_MAX_TOP_K))
-        return fail(LLMDOT_E_UNSUPPORTED, "sample: temperature > 0 needs 0 < top_k < vocabulary and top_k <= " +
-                                              std::to_string(SAMPLE_MAX_TOP_K) + " on the device");
     if (a.window < 0 || a.window > SAMPLE_MAX_WINDOW)
         return fail(LLMDOT_E_UNSUPPORTED, "sample: repeat window above " + std::to_string(SAMPLE_MAX_WINDOW));
+    if (sample_full_row(a.temperature, a.top_k, a.n)) return launch_sample_full(a, rows, st);
+    if (a.temperature > 0.0f && a.top_k > SAMPLE_MAX_TOP_K)
+        return fail(LLMDOT_E_UNSUPPORTED, "sample: top_k above " + std::to_string(SAMPLE_MAX_TOP_K) +
+                                              " (and below the vocabulary) is not on the device");
     const int k2 = k2_for(a.top_k > 0 ? a.top_k : 1);
     const size_t sm = sample_smem(a.n, a.window, a.top_k);
     if (sm > 200 * 1024) return fail(LLMDOT_E_UNSUPPORTED, "sample: vocabulary too large for the token bitmap");

@@ -259,11 +259,16 @@ LLMDOT_API float llmdot_cuda_sampling_seeded_draw(int32_t seed);
 
 /* Sampler.Sample (Sampler.cs:24-62) for one row of host logits (vocabulary n), on the device:
  * repeat penalty over the last repeat_window entries of recent (oldest first), scaling by
- * 1/temperature, top-k, softmax, and the first index whose running probability reaches r (the
- * uniform draw in [0, 1)).  temperature <= 0 is the argmax.  With temperature > 0 the device
- * needs 0 < top_k < n and top_k <= 1024 (the top-p-only path, top_k <= 0, is
- * LLMDOT_E_UNSUPPORTED); repeat_window <= 1024.  Exactly tied logits at the k-th place are taken
- * lowest index first. */
+ * 1/temperature, then
+ *   0 < top_k < n: top-k, softmax over the k, and the first index whose running probability
+ *                  reaches r (the uniform draw in [0, 1)); top_k <= 1024 on the device;
+ *   otherwise:     softmax over the whole row, then with top_p < 1 the nucleus (FindNucleus,
+ *                  including the reference's aliased value buffer: a nucleus that is the whole
+ *                  row returns a position of the sorted order, as the reference does), else the
+ *                  pick over the whole row.
+ * temperature <= 0 is the argmax.  repeat_window <= 1024.  Exactly tied logits at the k-th place
+ * are taken lowest index first.  LLMDOT_E_UNSUPPORTED: top_k in (1024, n), or a tie group of
+ * more than 8192 equal probabilities inside the nucleus. */
 LLMDOT_API int llmdot_cuda_sample(llmdot_backend *h, const float *logits, int n, const llmdot_sampling *opt,
                                   const int32_t *recent, int n_recent, float r, int32_t *index);
 

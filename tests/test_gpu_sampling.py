@@ -5,7 +5,8 @@ Logits are continuous random values, so no two tie; the sampled index must be id
 softmax's 8-wide ExpApprox lanes are bit-exact on the device; only its MathF.Exp tail (the last
 k mod 8 entries) may differ by an ulp, so a draw within an ulp of a cumulative-probability
 boundary could in principle pick the neighbour.  The seeds and draws are fixed, and none of them
-lands that close.
+lands that close.  The full-row path (top_k <= 0 or >= n) is also checked on rows with many exactly
+tied probabilities, where the nucleus replays the reference's selection sort.
 """
 import numpy as np
 import pytest
@@ -32,6 +33,12 @@ CASES = [
     dict(top_k=200, top_p=1.0, temperature=1.5, repeat_penalty=1.3, repeat_window=64),
     dict(top_k=1024, top_p=1.0, temperature=2.0, repeat_penalty=1.0, repeat_window=64),
     dict(top_k=3, top_p=1.0, temperature=0.0, repeat_penalty=1.5, repeat_window=64),  # greedy
+    # the whole row (Sampler.cs:42-61): top-p nucleus, plain softmax, top_k at or above the vocabulary
+    dict(top_k=0, top_p=0.95, temperature=0.8, repeat_penalty=1.1, repeat_window=64),
+    dict(top_k=0, top_p=1.0, temperature=1.0, repeat_penalty=1.0, repeat_window=0),
+    dict(top_k=-1, top_p=0.5, temperature=0.7, repeat_penalty=1.3, repeat_window=16),
+    dict(top_k=1 << 20, top_p=0.9, temperature=1.2, repeat_penalty=1.1, repeat_window=64),
+    dict(top_k=0, top_p=0.05, temperature=2.0, repeat_penalty=1.0, repeat_window=0),
 ]
 
 
@@ -40,8 +47,8 @@ CASES = [
 def test_sample_matches_oracle(backend, vocab, case):
     rng = np.random.default_rng(1000 * case + vocab)
     o = _opts(**CASES[case])
-    if o.top_k >= vocab:
-        pytest.skip("top_k beyond the vocabulary")
+    if 1024 < o.top_k < vocab:
+        pytest.skip("top_k above the device's top-k limit")
     for trial in range(4):
         logits = (rng.standard_normal(vocab) * 3.0).astype(np.float32)
         # a history with repeats and negative logits among the penalised tokens
@@ -59,10 +66,26 @@ def test_sample_seeded_draw_and_errors(backend):
     o = _opts(seed=42)
     want = O.sample(logits, _oracle_opts(o), [])
     assert backend.sample(logits, o, []) == want
-    with pytest.raises(CudaBackendError):  # top-p only: not on the device
-        backend.sample(logits, _opts(top_k=0, top_p=0.9, temperature=1.0), [], 0.5)
-    with pytest.raises(CudaBackendError):  # top_k must stay below the vocabulary
-        backend.sample(logits, _opts(top_k=5000, temperature=1.0), [], 0.5)
+    with pytest.raises(CudaBackendError):  # top_k between the device's 1024 and the vocabulary
+        backend.sample(logits, _opts(top_k=2000, temperature=1.0), [], 0.5)
+
+
+@pytest.mark.parametrize("vocab", [7, 8, 1000, 32000])
+def test_sample_full_row_ties(backend, vocab):
+    """Whole-row softmax and nucleus on rows whose logits take a few values only, so equal
+    probabilities fill the nucleus and the selection sort's replay decides the order; also rows
+    shorter than the 8-wide lanes, NaN-free infinities, and nuclei that cover the whole row."""
+    rng = np.random.default_rng(vocab)
+    for trial in range(6):
+        logits = rng.integers(-3, 4, size=vocab).astype(np.float32) * 0.5
+        if trial == 1:
+            logits[rng.integers(0, vocab, size=max(1, vocab // 10))] = -np.inf
+        recent = rng.integers(0, vocab, size=12).astype(np.int32)
+        for top_p, r in [(0.9, 0.37), (0.5, 0.81), (0.999999, 0.55), (1.0, 0.93), (0.2, 0.05)]:
+            o = _opts(top_k=0, top_p=top_p, temperature=0.9, repeat_penalty=1.2, repeat_window=8)
+            want = O.sample(logits, _oracle_opts(o), recent, r)
+            got = backend.sample(logits, o, recent, r)
+            assert got == want, (vocab, trial, top_p, r, got, want)
 
 
 @pytest.mark.parametrize("name", ["micro", "micro-gemma", "tiny"])
@@ -98,6 +121,25 @@ def test_generate_sampled_matches_oracle(gpu, name):
             os_.close()
             om.close()
         assert list(s.generate_sampled(prompt, 8, seeded)) == want7
+        # the whole-row path: softmax over the vocabulary, then the top-p nucleus.  A nucleus of
+        # thousands of nearly equal probabilities (the random-weight "tiny" model) orders them by
+        # differences far below the logits' fp32 tolerance, so there the draw is checked on the
+        # device's own logits; the micro models' nuclei are small enough for the whole sequence.
+        top_p = _opts(top_k=0, top_p=0.9, temperature=0.9, repeat_penalty=1.1, repeat_window=16)
+        got_p = list(s.generate_sampled(prompt, steps, top_p, draws))
+        if name == "tiny":
+            s2 = m.session(kv="f32")
+            _, lg = s2.prefill(prompt, want_logits=True)
+            s2.close()
+            assert got_p[0] == O.sample(lg, _oracle_opts(top_p), prompt, float(draws[0]))
+        else:
+            os_ = O.Session(om := O.Model(path))
+            try:
+                want_p = list(os_.generate_sampled(prompt, steps, _oracle_opts(top_p), draws))
+            finally:
+                os_.close()
+                om.close()
+            assert got_p == want_p
         s.close()
     finally:
         m.close()
