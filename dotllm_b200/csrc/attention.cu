@@ -264,16 +264,20 @@ __global__ void append_kv_kernel(const float *__restrict__ k, const float *__res
 // shared-memory slots with cp.async (rows padded by 16 bytes: 16-byte reads of 8 consecutive
 // rows hit distinct bank groups), keeping the scores of all its positions in shared memory.
 // The window max (the reference's softmax subtracts the GLOBAL max before ExpApprox) and the
-// final sums cross the cluster through distributed shared memory; the output is reduced over
-// the ranks in rank order, so the result does not depend on scheduling.  No global scratch,
+// final sums cross the cluster through distributed shared memory: every rank pushes its per-head
+// maxima into every rank's shared memory and its partial P.V slices to the rank that finishes
+// them, each exchange closed by one cluster barrier (release / acquire); the output is reduced
+// over the ranks in rank order, so the result does not depend on scheduling.  No global scratch,
 // no atomics, one launch per layer.
 constexpr int AC_THREADS = 256;
 constexpr int AC_SBUF = 32 * 1024;  // bytes of scores per CTA (G heads x pages x 64 positions)
 
 struct AcLayout {
-    int rstride, mbar, ring, sbuf, qs, kn, pv, lo, stat, total;  // rstride: bytes per staged row; the rest byte offsets
+    int rstride, mbar, ring, sbuf, qs, kn, pv, lo, stat, xmax, xsum, xpart, total;  // rstride: bytes per staged row
 };
-__host__ __device__ inline AcLayout ac_layout(int hd, int esz, int G, int maxp, int slots)
+// slice of the G * hd outputs that rank q of a C-CTA cluster finishes
+__host__ __device__ inline int ac_slice(int G, int hd, int C) { return (G * hd + C - 1) / C; }
+__host__ __device__ inline AcLayout ac_layout(int hd, int esz, int G, int maxp, int slots, int C)
 {
     AcLayout L;
     int o = 0;
@@ -294,6 +298,12 @@ __host__ __device__ inline AcLayout ac_layout(int hd, int esz, int G, int maxp, 
     o += G * hd * 4;
     L.stat = o;  // lmax[G], M[G], lsum[G]
     o += (3 * G * 4 + 15) / 16 * 16;
+    L.xmax = o;  // [C][G] every rank's per-head maxima (pushed by the ranks)
+    o += (C * G * 4 + 15) / 16 * 16;
+    L.xsum = o;  // [C][G] every rank's per-head sums
+    o += (C * G * 4 + 15) / 16 * 16;
+    L.xpart = o;  // [C][slice] every rank's P.V partials of this rank's output slice
+    o += (C * ac_slice(G, hd, C) * 4 + 15) / 16 * 16;
     L.total = o;
     return L;
 }
@@ -363,13 +373,17 @@ __global__ void __launch_bounds__(AC_THREADS) attn_cluster_kernel(const float *_
     const int C = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
     const int kvh = blockIdx.y, b = blockIdx.z, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int hd = sh.head_dim, half = sh.rope_half, G = sh.heads / sh.heads_kv, cpr = hd / E;
-    const AcLayout L = ac_layout(hd, (int)sizeof(T), G, maxp, slots);
+    const AcLayout L = ac_layout(hd, (int)sizeof(T), G, maxp, slots, C);
     uint8_t *ring = smem + L.ring;
     uint64_t *mbar = (uint64_t *)(smem + L.mbar);
     if (tid < slots)
         asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(mbar + tid)), "r"(AC_THREADS) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
+    // cluster barrier 0: every rank has started (its shared memory may receive pushes); waited
+    // on just before the first push
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     float *sbuf = (float *)(smem + L.sbuf), *qs = (float *)(smem + L.qs), *pv = (float *)(smem + L.pv);
     float *lo = (float *)(smem + L.lo), *lmax = (float *)(smem + L.stat), *Ms = lmax + G, *lsum = lmax + 2 * G;
     T *kn = (T *)(smem + L.kn), *vn = (T *)(smem + L.kn + (hd * sizeof(T) + 15) / 16 * 16);
@@ -484,47 +498,36 @@ __global__ void __launch_bounds__(AC_THREADS) attn_cluster_kernel(const float *_
         __syncthreads();  // the slot is free again
         if (f + slots < 2 * n) issue(f + slots);
     }
-    // this CTA's max per head (all threads: a head's positions are spread over the block, the
-    // warp maxima meet in pv), then the window max over the cluster
+    // this CTA's max per head: warp hg reduces head hg's positions, and lane r pushes it into
+    // rank r's exchange slots; after the barrier every rank holds all ranks' maxima
     const int plo = max(start - pg_lo * KV_PAGE, 0), phi = min(seq_len - pg_lo * KV_PAGE, n * KV_PAGE);  // CTA's positions
-    for (int hg = 0; hg < G; hg++) {
+    float *xmax = (float *)(smem + L.xmax), *xsum = (float *)(smem + L.xsum), *xpart = (float *)(smem + L.xpart);
+    __syncwarp();
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // barrier 0
+    for (int hg = warp; hg < G; hg += AC_THREADS / 32) {
         float m = -INFINITY;
-        for (int j = plo + tid; j < phi; j += AC_THREADS) m = fmaxf(m, sbuf[hg * sstride + j]);
+        for (int j = plo + lane; j < phi; j += 32) m = fmaxf(m, sbuf[hg * sstride + j]);
         m = warp_max(m);
-        if (lane == 0) pv[hg * 8 + warp] = m;
+        if (lane < C) *cluster.map_shared_rank(xmax + rank * G + hg, lane) = m;
     }
-    __syncthreads();
-    for (int hg = tid; hg < G; hg += AC_THREADS) {
-        float m = -INFINITY;
-        for (int w2 = 0; w2 < AC_THREADS / 32; w2++) m = fmaxf(m, pv[hg * 8 + w2]);
-        lmax[hg] = m;
-    }
-    cluster.sync();
-    for (int hg = tid; hg < G; hg += AC_THREADS) {
-        float m = -INFINITY;
-        for (int r = 0; r < C; r++) m = fmaxf(m, *cluster.map_shared_rank(lmax + hg, r));
-        Ms[hg] = m;
-    }
-    __syncthreads();
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // barrier 1
     // p = exp(s - M) in place (ExpApprox in the reference's 8-wide lanes, MathF.Exp in the tail);
-    // per-head sums: thread partials, warp sums, then the 8 warps in order
-    for (int hg = 0; hg < G; hg++) {
+    // warp hg takes head hg: the window max over the ranks, the exponentials, this CTA's sum
+    for (int hg = warp; hg < G; hg += AC_THREADS / 32) {
+        float M = -INFINITY;
+        for (int r = 0; r < C; r++) M = fmaxf(M, xmax[r * G + hg]);
         float sum = 0.0f;
-        for (int j = plo + tid; j < phi; j += AC_THREADS) {
+        for (int j = plo + lane; j < phi; j += 32) {
             float *sp = sbuf + hg * sstride + j;
-            const float d = __fsub_rn(*sp, Ms[hg]);
+            const float d = __fsub_rn(*sp, M);
             const float pr = (pg_lo * KV_PAGE + j - start) < nvec ? exp_approx(d) : expf(d);
             *sp = pr;
             sum += pr;
         }
         sum = warp_sum(sum);
-        if (lane == 0) pv[hg * 8 + warp] = sum;
-    }
-    __syncthreads();
-    for (int hg = tid; hg < G; hg += AC_THREADS) {
-        float sum = 0.0f;
-        for (int w2 = 0; w2 < AC_THREADS / 32; w2++) sum += pv[hg * 8 + w2];
-        lsum[hg] = sum;
+        if (lane == 0) lsum[hg] = sum;
     }
     __syncthreads();
     // ---- pass 2: P.V.  A set of G*hd/E threads covers every (head, 16-byte chunk) once; the NG
@@ -556,23 +559,33 @@ __global__ void __launch_bounds__(AC_THREADS) attn_cluster_kernel(const float *_
 #pragma unroll
         for (int e = 0; e < E; e++) pv[gi * G * hd + hg * hd + ch * E + e] = acc[e];
     __syncthreads();
+    // this CTA's P.V partials go to the rank finishing their slice, its sums to every rank
+    const int SL = ac_slice(G, hd, C);
     for (int o = tid; o < G * hd; o += AC_THREADS) {
-        float s = 0.0f;
-        for (int g2 = 0; g2 < NG; g2++) s += pv[g2 * G * hd + o];
-        lo[o] = s;
+        float sacc = 0.0f;
+        for (int g2 = 0; g2 < NG; g2++) sacc += pv[g2 * G * hd + o];
+        const int q = o / SL;
+        *cluster.map_shared_rank(xpart + rank * SL + (o - q * SL), q) = sacc;
     }
-    cluster.sync();
-    // each rank finishes a slice of the (head, dim) outputs, summing the ranks in rank order
-    for (int o = rank * AC_THREADS + tid; o < G * hd; o += C * AC_THREADS) {
+    for (int i = tid; i < C * G; i += AC_THREADS) {
+        const int r = i / G, hg = i % G;
+        *cluster.map_shared_rank(xsum + rank * G + hg, r) = lsum[hg];
+    }
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // barrier 2: no access to a peer after it
+    // this rank's slice of the (head, dim) outputs, the ranks summed in rank order
+    for (int ol = tid; ol < SL; ol += AC_THREADS) {
+        const int o = rank * SL + ol;
+        if (o >= G * hd) break;
         const int h = o / hd;
         float tot = 0.0f, ssum = 0.0f;
         for (int r = 0; r < C; r++) {
-            tot += *cluster.map_shared_rank(lo + o, r);
-            ssum += *cluster.map_shared_rank(lsum + h, r);
+            tot += xpart[r * SL + ol];
+            ssum += xsum[r * G + h];
         }
         out[(size_t)b * ldo + (size_t)kvh * G * hd + o] = __fmul_rn(tot, __fdiv_rn(1.0f, ssum));
     }
-    cluster.sync();  // peers may still read this CTA's shared memory
 }
 
 // Cluster size and pages per CTA for a shape, or false when the cluster kernel does not apply
@@ -611,8 +624,8 @@ static bool cluster_plan(const AttnShape &sh, int batch, size_t esz, int *C_out,
         return e ? std::max(2, atoi(e)) : 1 << 20;
     }();
     slots = std::min(slots, slots_cap);
-    while (slots > 2 && ac_layout(sh.head_dim, (int)esz, G, maxp, slots).total > budget) slots--;
-    const AcLayout L = ac_layout(sh.head_dim, (int)esz, G, maxp, slots);
+    while (slots > 2 && ac_layout(sh.head_dim, (int)esz, G, maxp, slots, C).total > budget) slots--;
+    const AcLayout L = ac_layout(sh.head_dim, (int)esz, G, maxp, slots, C);
     if (L.total > 200 * 1024) return false;
     static const int min_smem = [] {  // LLMDOT_ATTN_MIN_SMEM: shared-memory floor per CTA in KB (tuning)
         const char *e = getenv("LLMDOT_ATTN_MIN_SMEM");
