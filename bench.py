@@ -262,13 +262,17 @@ def gpu_ids(local):
 
 
 def windows_for(ctx, used, steps, want):
-    """Timed windows of `steps` steps that still fit the sessions' context after `used` positions."""
-    return max(1, min(want, (ctx - used - 1) // max(steps, 1)))
+    """Timed windows: each restarts from the prompt, so all of them fit when one does (`used`
+    positions: prompt, warm-up and one window)."""
+    if used >= ctx:
+        raise SystemExit(f"bench: {used} positions per window exceed the context of {ctx}")
+    return max(1, want)
 
 
 def measure(m, cfg, args, B, n_prompt, ctx, rank, steps, dist, local, windows=1, clocks=False, sid0=None):
     """Prefill B sessions, warm up, then time `windows` windows of `steps` device-resident greedy
-    steps of all of them (each window bracketed by a barrier and synchronize; max over ranks).
+    steps of all of them (each window bracketed by a barrier and synchronize; max over ranks; every
+    window starts from the same prefilled prompt and warm-up).
     Returns the sessions, the last tokens, the per-window device ms, kernels per step, prefill
     seconds and the clock record."""
     import torch
@@ -296,7 +300,15 @@ def measure(m, cfg, args, B, n_prompt, ctx, rank, steps, dist, local, windows=1,
     kps = 0
     region = getattr(args, "profile_region", False)
     with clk:
-        for _ in range(windows):
+        for wi in range(windows):
+            if wi > 0:
+                # every window decodes from the same context: the prompt again, then the warm-up
+                # steps (untimed), so the windows time the same positions
+                for s in sessions:
+                    s.reset()
+                first = [s.prefill(p)[0] for s, p in zip(sessions, prompts)]
+                toks, _, _ = decode_steps(sessions, first, args.warmup)
+                cur = toks[-1]
             if dist:
                 dist.barrier()
             torch.cuda.synchronize()
@@ -419,7 +431,7 @@ def matvec_only(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--steps", type=int, default=64, help="timed steps per window (C2 generates 64 tokens)")
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="llama1b")
@@ -493,13 +505,21 @@ def main():
     ctx = min(cfg.context, 4096) if args.config == "llama1b" else cfg.context
     B = args.batch
     K = args.steps
-    nwin = windows_for(ctx, n_prompt + args.warmup + 2 * K + 8, K, args.windows)
+    nwin = windows_for(ctx, n_prompt + args.warmup + K + 8, K, args.windows)
     sessions, cur, wins, kps, prefill_s, clk = measure(m, cfg, args, B, n_prompt, ctx, rank, K, dist, local,
                                                        windows=nwin, clocks=True,
                                                        sid0=0 if args.tp else None)
     dev_ms = statistics.median(wins)
 
-    # end to end through the public per-step API: host tokens in, host ids out, every step
+    # end to end through the public per-step API: host tokens in, host ids out, every step, from
+    # the same context as the timed windows
+    from dotllm_b200.engine import decode_steps
+    e2e_prompts = [synth.prompt_tokens(cfg, n_prompt, session=(0 if args.tp else rank * B) + i) for i in range(B)]
+    for s in sessions:
+        s.reset()
+    first = [s.prefill(p)[0] for s, p in zip(sessions, e2e_prompts)]
+    toks, _, _ = decode_steps(sessions, first, args.warmup)
+    cur = toks[-1]
     if dist:
         dist.barrier()
     e2e_steps = K
@@ -526,7 +546,7 @@ def main():
     achieved = (layer_b + head_b) / (mv_ms * 1e-3) / 1e9  # weights are read once per step for all rows
     kv_elem = 2 if args.kv == "f16" else 4
     kv_dim = c["heads_kv"] * c["head_dim"] // (world if args.tp else 1)
-    mean_pos = n_prompt + args.warmup + K * (nwin + 0.5)
+    mean_pos = n_prompt + args.warmup + K * 0.5
     kv_read = kv_read_bytes(c, B, c["layers"], kv_dim, kv_elem, mean_pos)
     attn_ms = fam["attention"]["ms_per_step"]
 
@@ -598,7 +618,8 @@ def main():
         "windows": {"n": len(wins), "steps_each": K, "ms_per_step": [w / K for w in wins],
                     "median_ms_per_step": step_ms, "min_ms_per_step": min(wins) / K, "max_ms_per_step": max(wins) / K,
                     "note": "value = the median window; each window is K device-resident steps between a barrier "
-                            "and a synchronize, timed with CUDA events, max over ranks"},
+                            "and a synchronize, timed with CUDA events, max over ranks; every window starts from "
+                            "the prompt (sessions reset and prefilled again, untimed) and the warm-up steps"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": (layer_b + head_b) * DRAM_PER_ALGORITHMIC_BYTE,
                      "traffic_note": "DRAM bytes (read + write) per step of the matvec launches from an ncu capture "

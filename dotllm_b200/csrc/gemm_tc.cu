@@ -67,7 +67,7 @@ constexpr uint32_t A_COL = 192;
 constexpr float S_FAC = 1.0f / 64.0f;  // sub-block sums (< 2^20) scaled into fp16 range
 constexpr float C_FAC = 256.0f;        // offset coefficients scaled up (their lo half stays normal)
 constexpr unsigned long long TC_WAIT_NS = 2000000000ull;
-constexpr int TC_DEFAULT_REPLICAS = 8;
+constexpr int TC_DEFAULT_REPLICAS = 1;
 
 enum {
     B_B_FULL = 0, B_B_EMPTY = B_B_FULL + NB, B_RAW_FULL = B_B_EMPTY + NB, B_RAW_EMPTY = B_RAW_FULL + 8 * NRAW,
@@ -598,9 +598,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
 }
 
 // ------------------------------------------------------------------ input operands
-// One CTA per input row v: RMSNorm statistics (optional), an exact power-of-two scale putting
-// max |x| in [2^14, 2^15), then fp16 hi (column v) and lo (column 32 + v) of every element, in the
-// K order of each weight layout; for Q4_K also the sub-block sums as the offset term's B operand.
+// CTA (v, c) for input row v and chunk c of the super-blocks: RMSNorm statistics of the whole row
+// (optional), an exact power-of-two scale putting max |x| in [2^14, 2^15), then fp16 hi (column v)
+// and lo (column 32 + v) of the chunk's elements, in the K order of each weight layout; for Q4_K
+// also the sub-block sums as the offset term's B operand.
 __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ x, int ldx, int nsb,
                                                       const float *__restrict__ norm_w, float eps, int q4, int q6,
                                                       uint8_t *__restrict__ b4, uint8_t *__restrict__ b6,
@@ -609,6 +610,7 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
     __shared__ float red[2][8];
     __shared__ float stat[2];
     const int v = blockIdx.x, tid = threadIdx.x, cols = nsb * 256;
+    const int sb_lo = (int)((long long)blockIdx.y * nsb / gridDim.y), sb_n = (int)((long long)(blockIdx.y + 1) * nsb / gridDim.y) - sb_lo;
     const float *xv = x + (size_t)v * ldx;
     float ss = 0.0f, mx = 0.0f;
     for (int i = tid; i < cols; i += 256) {
@@ -642,7 +644,7 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
         }
         stat[0] = iv;
         stat[1] = sc;
-        isc[v] = 1.0f / sc;
+        if (blockIdx.y == 0) isc[v] = 1.0f / sc;
     }
     __syncthreads();
     // ((w*h)*inv)*sc == (w*h)*(inv*sc): sc is a power of two
@@ -651,8 +653,8 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
     const int n_hi = v, n_lo = v + 32;
     const int off_hi = (n_hi >> 3) * 1024 + (n_hi & 7) * 16, off_lo = (n_lo >> 3) * 1024 + (n_lo & 7) * 16;
     // one core row (8 weights, 16 bytes) per item: (super-block, quarter qt, core row kc of the quarter)
-    for (int it = tid; it < nsb * 32; it += 256) {
-        const int sb = it >> 5, kc32 = it & 31, qt = kc32 >> 3, kc = kc32 & 7;
+    for (int it = tid; it < sb_n * 32; it += 256) {
+        const int sb = sb_lo + (it >> 5), kc32 = it & 31, qt = kc32 >> 3, kc = kc32 & 7;
         float c[8];
         if (q4) {  // elements 32 (kc / 4) + 8 (kc % 4) + {0,4,1,5,2,6,3,7} of the quarter
             const int e0 = sb * 256 + qt * 64 + 32 * (kc >> 2) + 8 * (kc & 3);
@@ -700,8 +702,8 @@ __global__ void __launch_bounds__(256) tc_prep_kernel(const float *__restrict__ 
     }
     if (q4) {
         // sub-block sums S_j (fixed order: four 8-element partials), hi and lo, at K = 2j and 2j + 1
-        for (int it = tid; it < nsb * 8; it += 256) {
-            const int sb = it >> 3, j = it & 7;
+        for (int it = tid; it < sb_n * 8; it += 256) {
+            const int sb = sb_lo + (it >> 3), j = it & 7;
             float p[4];
 #pragma unroll
             for (int q = 0; q < 4; q++) {
@@ -749,8 +751,8 @@ int tc_scratch_alloc(TcScratch &s, int cols_max, int tiles_max, std::vector<void
         allocs.push_back(*p);
         return LLMDOT_OK;
     };
-    // replicas of the prepared operands: every CTA reads all of one input's B, so a single copy
-    // concentrates 148 readers on the same L2 lines; CTA c reads replica c % reps
+    // replicas of the prepared operands (CTA c reads replica c % reps): every CTA reads all of one
+    // input's B from L2; spreading the readers over copies measured no faster, so one by default
     static const int reps_env = [] {
         const char *e = getenv("LLMDOT_TC_REPLICAS");
         return e ? std::max(1, std::min(16, atoi(e))) : TC_DEFAULT_REPLICAS;
@@ -784,8 +786,10 @@ int tc_prepare(const float *x, int ldx, int nv, int cols, const float *norm_w, f
 {
     if (!s.ready() || nv < 1 || nv > TC_MAX_ROWS || cols % 256 || cols > s.cols_max)
         return fail(LLMDOT_E_INVALID, "tensor-core matmul: bad input shape");
-    tc_prep_kernel<<<nv, 256, 0, st>>>(x, ldx, cols / 256, norm_w, eps, q4 ? 1 : 0, q6 ? 1 : 0, s.b4, s.b6, s.isc,
-                                       s.reps, s.b4s, s.b6s);
+    // about four super-blocks per CTA: the statistics are re-read per chunk, the conversion spreads
+    const int chunks = std::max(1, std::min(16, cols / 1024));
+    tc_prep_kernel<<<dim3(nv, chunks), 256, 0, st>>>(x, ldx, cols / 256, norm_w, eps, q4 ? 1 : 0, q6 ? 1 : 0, s.b4,
+                                                      s.b6, s.isc, s.reps, s.b4s, s.b6s);
     LLMDOT_CUDA_TRY(cudaGetLastError());
     return LLMDOT_OK;
 }
