@@ -239,8 +239,10 @@ def run_reference(args, rank):
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per quantised weight byte of the matvec
-# launches of one decode step, from an ncu capture of this benchmark's default command
-DRAM_PER_ALGORITHMIC_BYTE = 1.008
+# launches of one decode step, from an ncu capture of this benchmark's batch-1 command: the
+# gate+up and down launches of one layer read 48.48 MB for their own 32.63 MB plus the 17.57 MB
+# of the next operations' weights they prefetch into L2 (each weight byte once per step)
+DRAM_PER_ALGORITHMIC_BYTE = 0.966
 
 
 def gpu_ids(local):
