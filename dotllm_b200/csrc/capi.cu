@@ -519,6 +519,12 @@ struct ModelExtra {
     int32_t *h_pinned = nullptr;  // pinned staging: tokens | pos | next  (3 * cap)
     KvView *h_views = nullptr;
     int cap = 0;
+    // the sampled Generate's buffers, kept across calls: history | length | out | draw (pinned and
+    // device copies), and the sampler's whole-row work
+    int32_t *h_samp = nullptr, *d_samp = nullptr;
+    size_t samp_n = 0;
+    void *d_work = nullptr;
+    size_t work_bytes = 0;
 };
 
 static std::mutex g_extra_mu;
@@ -619,6 +625,9 @@ static void drop_graphs(llmdot_model *m)
     for (auto &g : it->second.graphs) cudaGraphExecDestroy(g.exec);
     if (it->second.h_pinned) cudaFreeHost(it->second.h_pinned);
     if (it->second.h_views) cudaFreeHost(it->second.h_views);
+    if (it->second.h_samp) cudaFreeHost(it->second.h_samp);
+    if (it->second.d_samp) cudaFree(it->second.d_samp);
+    if (it->second.d_work) cudaFree(it->second.d_work);
     g_extra.erase(it);
 }
 
@@ -1045,8 +1054,7 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
     cudaStream_t st = m->stream;
     cudaGraphExec_t g = nullptr;
     LLMDOT_TRY(step_graph(m, 1, s->kv_type, &g));
-    // the decode step's position and KV view, set before the history buffers exist so that an
-    // early return leaks nothing
+    // the decode step's position and KV view
     ModelExtra &x = extra(m);
     LLMDOT_TRY(ensure_pinned(m, 1));
     x.h_pinned[x.cap] = s->pos;
@@ -1056,21 +1064,33 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
     const int keep = a.window + 1;
     std::vector<int32_t> recent(prompt, prompt + n_prompt);
     // device: [history (keep)] [length] [out] [r]
-    int32_t *dbuf = nullptr;
-    LLMDOT_CUDA_TRY(cudaMallocAsync(&dbuf, sizeof(int32_t) * (keep + 3), st));
-    if (full_row && cudaMallocAsync(&a.work, sample_work_bytes(c.vocab), st) != cudaSuccess) {
-        cudaGetLastError();
-        cudaFreeAsync(dbuf, st);
-        return fail(LLMDOT_E_NOMEM, "generate_sampled: sampler work allocation failed");
+    // kept by the model across calls (a per-call pinned allocation cost more than a short
+    // generation); pinned, so the per-token upload is a plain DMA
+    const size_t need = (size_t)keep + 3;
+    if (x.samp_n < need) {
+        if (x.h_samp) cudaFreeHost(x.h_samp);
+        if (x.d_samp) cudaFree(x.d_samp);
+        x.h_samp = x.d_samp = nullptr;
+        x.samp_n = 0;
+        if (cudaMallocHost(&x.h_samp, sizeof(int32_t) * need) != cudaSuccess ||
+            cudaMalloc(&x.d_samp, sizeof(int32_t) * need) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(LLMDOT_E_NOMEM, "generate_sampled: staging allocation failed");
+        }
+        x.samp_n = need;
     }
-    // pinned: the per-token upload is then a plain DMA instead of the driver's pageable staging
-    int32_t *hbuf = nullptr;
-    if (cudaMallocHost(&hbuf, sizeof(int32_t) * (keep + 3)) != cudaSuccess) {
-        cudaGetLastError();
-        cudaFreeAsync(dbuf, st);
-        if (a.work) cudaFreeAsync(a.work, st);
-        return fail(LLMDOT_E_NOMEM, "generate_sampled: pinned staging allocation failed");
+    if (full_row && x.work_bytes < sample_work_bytes(c.vocab)) {
+        if (x.d_work) cudaFree(x.d_work);
+        x.d_work = nullptr;
+        x.work_bytes = 0;
+        if (cudaMalloc(&x.d_work, sample_work_bytes(c.vocab)) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(LLMDOT_E_NOMEM, "generate_sampled: sampler work allocation failed");
+        }
+        x.work_bytes = sample_work_bytes(c.vocab);
     }
+    int32_t *dbuf = x.d_samp, *hbuf = x.h_samp;
+    if (full_row) a.work = x.d_work;
     std::mt19937 rng(std::random_device{}());
     const float seeded = opt->seed >= 0 ? llmdot_cuda_sampling_seeded_draw(opt->seed) : 0.0f;
     a.has_cap = c.has_final_cap;
@@ -1122,10 +1142,7 @@ extern "C" int llmdot_cuda_generate_sampled(llmdot_session *s, const int32_t *pr
         }
         s->pos += 1;
     }
-    cudaFreeAsync(dbuf, st);
-    if (a.work) cudaFreeAsync(a.work, st);
     cudaStreamSynchronize(st);
-    cudaFreeHost(hbuf);
     if (rc == LLMDOT_OK) rc = check_err_flag(m);
     *n_out = produced;
     return rc;
