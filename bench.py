@@ -398,7 +398,8 @@ def tensor_parallel(args, world, rank, dist, local, name, n_prompt, batches, ste
     else:
         m = CudaModel.load(path, device=local)
     out = {"model": name, "tp": world, "prompt": n_prompt, "steps": steps, "batches": {}}
-    try:
+
+    def run(into):
         for B in batches:
             ctx = n_prompt + args.warmup + 3 * steps + 16
             ss, cur, wins, _, pre, _ = measure(m, cfg, args, B, n_prompt, ctx, rank, steps, dist, local, windows=3,
@@ -407,10 +408,21 @@ def tensor_parallel(args, world, rank, dist, local, name, n_prompt, batches, ste
             for s in ss:
                 s.close()
             ms = statistics.median(wins)
-            out["batches"][str(B)] = {"value": B * steps / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms / steps,
-                                      "prefill_tok_s": B * n_prompt / pre,
-                                      "families_ms_per_step": {f: v["ms_per_step"] for f, v in fam.items()},
-                                      "collectives_per_step": fam["collective"]["launches_per_step"]}
+            into[str(B)] = {"value": B * steps / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms / steps,
+                            "prefill_tok_s": B * n_prompt / pre,
+                            "families_ms_per_step": {f: v["ms_per_step"] for f, v in fam.items()},
+                            "collectives_per_step": fam["collective"]["launches_per_step"]}
+
+    try:
+        run(out["batches"])
+        if world > 1 and not args.no_peer:
+            # the same batches with the step's residual sums on the peer-memory all-reduce (one kernel
+            # over NVLink, CUDA IPC handles exchanged through the process group) instead of NCCL's
+            handles = [None] * world
+            dist.all_gather_object(handles, m.tp_exchange_handle())
+            m.tp_exchange_open(handles)
+            out["peer_allreduce"] = {}
+            run(out["peer_allreduce"])
     finally:
         m.close()
     return out
@@ -446,6 +458,10 @@ def main():
     ap.add_argument("--no-batch32", action="store_true", help="skip the sharded batch-32 measurement")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the Phi-3 sharded-sessions and Llama-3-8B tensor-parallel workloads")
+    ap.add_argument("--no-peer", action="store_true",
+                    help="tensor-parallel workloads: skip the peer-memory all-reduce measurement")
+    ap.add_argument("--tp-config", default=None,
+                    help="run only the tensor-parallel workload over all ranks on this config, B=1 and B=16")
     ap.add_argument("--matvec", default=None, help="time one matvec over this tensor only (profiling)")
     ap.add_argument("--profile-region", action="store_true",
                     help="bracket the timed decode windows with cudaProfilerStart/Stop (ncu --profile-from-start off)")
@@ -474,6 +490,21 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    if args.tp_config:
+        # one tensor-parallel workload alone (NCCL and peer-memory residual sums), rank 0 prints it
+        tcfg = synth.get(args.tp_config)
+        if rank == 0:
+            synth.build_model(tcfg)
+        if dist:
+            dist.barrier()
+        res = tensor_parallel(args, world, rank, dist, local, args.tp_config,
+                              args.prompt if args.prompt is not None else tcfg.prompt_len, [1, 16], args.steps)
+        if rank == 0:
+            print(json.dumps({"tp_workload": res}), flush=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     extras = not args.no_extras and not args.tp and args.config == "llama1b"
     # rank 0 writes the synthetic GGUFs (spawned workers, before any CUDA work), the others reuse them
     if rank == 0:

@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(AC_THREADS) attn_cluster_kernel(const float *_
     __syncwarp();
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     float *sbuf = (float *)(smem + L.sbuf), *qs = (float *)(smem + L.qs), *pv = (float *)(smem + L.pv);
-    float *lo = (float *)(smem + L.lo), *lmax = (float *)(smem + L.stat), *Ms = lmax + G, *lsum = lmax + 2 * G;
+    float *lmax = (float *)(smem + L.stat), *lsum = lmax + 2 * G;
     T *kn = (T *)(smem + L.kn), *vn = (T *)(smem + L.kn + (hd * sizeof(T) + 15) / 16 * 16);
     const int sstride = maxp * KV_PAGE;  // scores per head in sbuf
 

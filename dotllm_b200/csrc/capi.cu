@@ -710,6 +710,21 @@ extern "C" int llmdot_cuda_tp_init(llmdot_model *m, const uint8_t *id128)
     return tp_comm_init(m, id128);
 }
 
+extern "C" int llmdot_cuda_tp_exchange_handle(llmdot_model *m, uint8_t *out128)
+{
+    if (!m || !out128) return fail(LLMDOT_E_INVALID, "null argument");
+    if (!m->nccl) return fail(LLMDOT_E_INVALID, "tp_exchange_handle: call llmdot_cuda_tp_init first");
+    return tp_exchange_handle(m, out128);
+}
+
+extern "C" int llmdot_cuda_tp_exchange_open(llmdot_model *m, const uint8_t *handles)
+{
+    if (!m || !handles) return fail(LLMDOT_E_INVALID, "null argument");
+    LLMDOT_TRY(tp_exchange_open(m, handles));
+    drop_graphs(m);  // steps captured before use NCCL's all-reduce; the next capture uses the exchange
+    return LLMDOT_OK;
+}
+
 extern "C" int llmdot_cuda_model_config(const llmdot_model *m, llmdot_config *out)
 {
     if (!m || !out) return fail(LLMDOT_E_INVALID, "null argument");
@@ -856,6 +871,7 @@ static int check_err_flag(llmdot_model *m)
         cudaMemset(m->ws.err, 0, sizeof(int));
         if (e == 1) return fail(LLMDOT_E_INVALID, "token id outside the vocabulary");
         if (e == 5) return fail(LLMDOT_E_TIMEOUT, "tensor-core matmul: a bounded wait gave up");
+        if (e == 6) return fail(LLMDOT_E_TIMEOUT, "tensor parallel: a peer exchange wait gave up");
         return fail(LLMDOT_E_CUDA, "device error flag " + std::to_string(e));
     }
     return LLMDOT_OK;

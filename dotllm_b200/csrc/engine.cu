@@ -293,6 +293,7 @@ void model_destroy(llmdot_model *m)
     if (!m) return;
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    tp_exchange_close(m);
     tp_comm_destroy(m);
     for (void *p : m->ws.allocs) cudaFree(p);
     for (void *p : m->allocs) cudaFree(p);

@@ -86,6 +86,12 @@ struct llmdot_model {
     int tp = 1, tp_rank = 0, head_lo = 0, head_rows = 0;
     llmdot_config full_cfg{};
     void *nccl = nullptr;  // ncclComm_t once llmdot_cuda_tp_init ran
+    // peer-memory all-reduce (tp.cu): this rank's exchange buffer, every rank's mapped into this
+    // process (own included), floats per slot row, and whether the step uses it
+    uint8_t *tpx = nullptr;
+    uint8_t *tpx_peer[8] = {};
+    size_t tpx_cap = 0;
+    bool tpx_open = false;
     llmdot::StepTimer *timer = nullptr;  // attached only while llmdot_cuda_profile_step runs
 };
 

@@ -106,10 +106,6 @@ __device__ __forceinline__ void bar_arrive(uint64_t *b)
 {
     asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
 }
-__device__ __forceinline__ void bar_expect_tx(uint64_t *b, uint32_t bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
-}
 __device__ __forceinline__ bool bar_try(uint64_t *b, uint32_t parity)
 {
     uint32_t ok;
@@ -128,13 +124,6 @@ __device__ __forceinline__ void cp16(void *dst, const void *src)
 __device__ __forceinline__ void cp_arrive(uint64_t *b)
 {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(su32(b)) : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *b)
-{
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     su32(dst)),
-                 "l"(src), "r"(bytes), "r"(su32(b))
-                 : "memory");
 }
 // shared-memory matrix descriptor: no swizzle, K-major core matrices of 8 rows x 16 bytes; lbo =
 // byte distance of K-adjacent core matrices, sbo = of 8-row groups; bit 46 = descriptor version 1
@@ -480,11 +469,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             }
             cp_arrive(bars + B_RAW_FULL + (k % NRAW) * 8 + my_tile);
         };
-        int own_issued = 0;
-        for (int k = 0; k < NRAW && k < n; k++) {
-            issue_tile(k);
-            own_issued = k + 1;
-        }
+        for (int k = 0; k < NRAW && k < n; k++) issue_tile(k);
         bool ok = true;
         for (int i = 0; i < n && ok; i++) {
             const Unit U = unit(i);
@@ -583,11 +568,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
                 // refill this warp's tile of the slot once both readers of it are done with unit i
                 if (!(ok = wait(B_RAW_EMPTY + slot * 8 + my_tile, (i / NRAW) & 1))) break;
                 issue_tile(i + NRAW);
-                own_issued = i + NRAW + 1;
             }
         }
         asm volatile("cp.async.wait_all;" ::: "memory");  // no copy may land after the CTA exits
-        (void)own_issued;
     }
 
     tc_fence_before();

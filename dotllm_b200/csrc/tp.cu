@@ -2,6 +2,7 @@
 #include <dlfcn.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -114,9 +115,269 @@ void tp_comm_destroy(llmdot_model *m)
     m->nccl = nullptr;
 }
 
+// ------------------------------------------------------------------ peer-memory all-reduce
+// Exchange buffer of one rank (device memory, exported with CUDA IPC):
+//   u32 [0]  sequence number of the last finished all-reduce (advanced by its last CTA)
+//   u32 [1]  CTAs of the running all-reduce that finished
+//   u32 [2]  set once a wait of this rank gave up (later waits give up at once)
+//   u32 [3]  set by the close barrier when it gave up
+//   u32 [16 + q]  set by rank q when it reached its close barrier
+//   byte TPX_DATA: u64 slots [2 parities][tp source ranks][cap elements]
+// One all-reduce, generation g = sequence + 1: every rank stores each element of its partial as a
+// word (g << 32 | float bits) into every peer's slot [g & 1][own rank][element], then polls its own
+// slots for the other ranks' words tagged g.  A 64-bit store is single-copy atomic, so the tag and
+// the value arrive together and no flag or fence is needed.  Two parities make reuse safe: a rank
+// starts generation g + 2 only after finishing g + 1, which needed every peer's g + 1 words, which
+// each peer stores only after its generation g kernel (and all its reads of parity g & 1) ended.
+namespace {
+
+constexpr size_t TPX_DATA = 4096;
+constexpr int TPX_THREADS = 256;
+constexpr int TPX_MAX_CTAS = 148;  // at most one CTA per SM: every CTA resident, none waits on a queued one
+constexpr unsigned long long TPX_WAIT_NS = 10ull * 1000 * 1000 * 1000;
+constexpr unsigned long long TPX_CLOSE_NS = 5ull * 1000 * 1000 * 1000;
+constexpr int TPX_ERR_TIMEOUT = 6;  // device error flag value the host maps to LLMDOT_E_TIMEOUT
+
+struct TpxArgs {
+    uint8_t *peer[TPX_MAX_RANKS];  // every rank's exchange buffer as mapped here (own included)
+    uint8_t *own;
+    float *buf;
+    long long n, cap;
+    int tp, rank;
+    int *err;
+};
+
+__device__ __forceinline__ unsigned long long tpx_now()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void tpx_store2(uint8_t *p, unsigned long long a, unsigned long long b)
+{
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+
+__device__ __forceinline__ void tpx_load2(const uint8_t *p, unsigned long long &a, unsigned long long &b)
+{
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Polls the four words at p until all carry tag gen; false (and the error flag) once the wait ran
+// past its deadline or an earlier wait of this rank already gave up.
+__device__ bool tpx_wait4(const uint8_t *p, unsigned gen, float4 &v, volatile unsigned *hdr, int *err)
+{
+    unsigned long long w0, w1, w2, w3, t0 = 0;
+    for (unsigned it = 0;; it++) {
+        tpx_load2(p, w0, w1);
+        tpx_load2(p + 16, w2, w3);
+        if ((unsigned)(w0 >> 32) == gen && (unsigned)(w1 >> 32) == gen && (unsigned)(w2 >> 32) == gen &&
+            (unsigned)(w3 >> 32) == gen)
+            break;
+        if ((it & 255) == 0) {
+            const unsigned long long t = tpx_now();
+            if (it == 0) t0 = t;
+            if (hdr[2] || t - t0 > TPX_WAIT_NS) {
+                hdr[2] = 1;
+                atomicCAS(err, 0, TPX_ERR_TIMEOUT);
+                v = make_float4(0.f, 0.f, 0.f, 0.f);
+                return false;
+            }
+        }
+    }
+    v = make_float4(__uint_as_float((unsigned)w0), __uint_as_float((unsigned)w1), __uint_as_float((unsigned)w2),
+                    __uint_as_float((unsigned)w3));
+    return true;
+}
+
+__device__ __forceinline__ unsigned long long tpx_word(unsigned gen, float x)
+{
+    return ((unsigned long long)gen << 32) | __float_as_uint(x);
+}
+
+__global__ void __launch_bounds__(TPX_THREADS) tpx_allreduce_kernel(TpxArgs a)
+{
+    volatile unsigned *hdr = (volatile unsigned *)a.own;
+    const unsigned gen = hdr[0] + 1;
+    const long long par = gen & 1;
+    const long long stride = (long long)gridDim.x * TPX_THREADS * 4;
+    const long long e0 = ((long long)blockIdx.x * TPX_THREADS + threadIdx.x) * 4;
+    const size_t src_off = TPX_DATA + (size_t)((par * a.tp + a.rank) * a.cap) * 8;
+    // push: this rank's partial into every peer's slot row [par][rank]
+    for (long long e = e0; e < a.n; e += stride) {
+        const float4 v = *(const float4 *)(a.buf + e);
+        const unsigned long long w0 = tpx_word(gen, v.x), w1 = tpx_word(gen, v.y), w2 = tpx_word(gen, v.z),
+                                 w3 = tpx_word(gen, v.w);
+        for (int q = 0; q < a.tp; q++) {
+            if (q == a.rank) continue;
+            uint8_t *d = a.peer[q] + src_off + (size_t)e * 8;
+            tpx_store2(d, w0, w1);
+            tpx_store2(d + 16, w2, w3);
+        }
+    }
+    // gather: every rank's partial, summed in rank order (the same order on every rank)
+    for (long long e = e0; e < a.n; e += stride) {
+        const float4 mine = *(const float4 *)(a.buf + e);
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < a.tp; q++) {
+            float4 v = mine;
+            if (q != a.rank)
+                tpx_wait4(a.own + TPX_DATA + (size_t)((par * a.tp + q) * a.cap + e) * 8, gen, v, hdr, a.err);
+            if (q == 0) {
+                s = v;
+            } else {
+                s.x += v.x;
+                s.y += v.y;
+                s.z += v.z;
+                s.w += v.w;
+            }
+        }
+        *(float4 *)(a.buf + e) = s;
+    }
+    // the last CTA to finish publishes the generation (every CTA read the old one before arriving)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd((unsigned *)(a.own + 4), 1u) == gridDim.x - 1) {
+            hdr[1] = 0;
+            hdr[0] = gen;
+            __threadfence();
+        }
+    }
+}
+
+// Close barrier: every rank marks its arrival in every peer's header and waits (bounded) for the
+// others' marks, so that no rank frees its buffer while a peer may still store into it.
+__global__ void tpx_close_kernel(TpxArgs a)
+{
+    volatile unsigned *hdr = (volatile unsigned *)a.own;
+    const int q = threadIdx.x;
+    if (q < a.tp && q != a.rank) {
+        volatile unsigned *peer_hdr = (volatile unsigned *)a.peer[q];
+        peer_hdr[16 + a.rank] = 1;
+        __threadfence_system();
+        const unsigned long long t0 = tpx_now();
+        while (hdr[16 + q] == 0) {
+            if (tpx_now() - t0 > TPX_CLOSE_NS) {
+                hdr[3] = 1;
+                break;
+            }
+        }
+    }
+}
+
+TpxArgs tpx_args(llmdot_model *m, float *buf, long long n)
+{
+    TpxArgs a{};
+    for (int q = 0; q < m->tp && q < TPX_MAX_RANKS; q++) a.peer[q] = m->tpx_peer[q];
+    a.own = m->tpx;
+    a.buf = buf;
+    a.n = n;
+    a.cap = (long long)m->tpx_cap;
+    a.tp = m->tp;
+    a.rank = m->tp_rank;
+    a.err = m->ws.err;
+    return a;
+}
+
+}  // namespace
+
+int tp_exchange_handle(llmdot_model *m, void *out128)
+{
+    if (m->tp < 2 || m->tp > TPX_MAX_RANKS)
+        return fail(LLMDOT_E_UNSUPPORTED, "peer all-reduce: needs 2 to 8 tensor-parallel ranks");
+    if (m->tpx_open) return fail(LLMDOT_E_INVALID, "peer all-reduce: already open");
+    LLMDOT_CUDA_TRY(cudaSetDevice(m->device));
+    if (!m->tpx) {
+        // the step's residual sums of up to 64 rows of the hidden state
+        const size_t cap = (size_t)64 * ((m->cfg.hidden + 3) / 4 * 4);
+        const size_t bytes = TPX_DATA + 2 * (size_t)m->tp * cap * 8;
+        LLMDOT_CUDA_TRY(cudaMalloc((void **)&m->tpx, bytes));
+        LLMDOT_CUDA_TRY(cudaMemset(m->tpx, 0, bytes));
+        LLMDOT_CUDA_TRY(cudaDeviceSynchronize());
+        m->tpx_cap = cap;
+    }
+    cudaIpcMemHandle_t h;
+    LLMDOT_CUDA_TRY(cudaIpcGetMemHandle(&h, m->tpx));
+    cudaDeviceProp prop;
+    LLMDOT_CUDA_TRY(cudaGetDeviceProperties(&prop, m->device));
+    static_assert(sizeof(h) + sizeof(prop.uuid) <= TPX_HANDLE_BYTES, "handle layout");
+    memset(out128, 0, TPX_HANDLE_BYTES);
+    memcpy(out128, &h, sizeof(h));
+    memcpy((uint8_t *)out128 + 64, &prop.uuid, sizeof(prop.uuid));
+    return LLMDOT_OK;
+}
+
+int tp_exchange_open(llmdot_model *m, const void *handles)
+{
+    if (!m->tpx) return fail(LLMDOT_E_INVALID, "peer all-reduce: call tp_exchange_handle first");
+    if (m->tpx_open) return fail(LLMDOT_E_INVALID, "peer all-reduce: already open");
+    const uint8_t *hb = (const uint8_t *)handles;
+    LLMDOT_CUDA_TRY(cudaSetDevice(m->device));
+    cudaDeviceProp prop;
+    LLMDOT_CUDA_TRY(cudaGetDeviceProperties(&prop, m->device));
+    if (memcmp(hb + (size_t)m->tp_rank * TPX_HANDLE_BYTES + 64, &prop.uuid, sizeof(prop.uuid)))
+        return fail(LLMDOT_E_INVALID, "peer all-reduce: this rank's handle is not at its rank's position");
+    // ranks that wait on one another must not share a GPU (nothing makes their kernels co-resident)
+    for (int p = 0; p < m->tp; p++)
+        for (int q = p + 1; q < m->tp; q++)
+            if (!memcmp(hb + (size_t)p * TPX_HANDLE_BYTES + 64, hb + (size_t)q * TPX_HANDLE_BYTES + 64, 16))
+                return fail(LLMDOT_E_UNSUPPORTED, "peer all-reduce: two ranks share one GPU");
+    uint8_t *peer[TPX_MAX_RANKS] = {};
+    for (int q = 0; q < m->tp; q++) {
+        if (q == m->tp_rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hb + (size_t)q * TPX_HANDLE_BYTES, sizeof(h));
+        void *p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int r = 0; r < q; r++)
+                if (peer[r]) cudaIpcCloseMemHandle(peer[r]);
+            return fail(LLMDOT_E_CUDA, std::string("peer all-reduce: cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+        }
+        peer[q] = (uint8_t *)p;
+    }
+    peer[m->tp_rank] = m->tpx;
+    for (int q = 0; q < TPX_MAX_RANKS; q++) m->tpx_peer[q] = peer[q];
+    m->tpx_open = true;
+    return LLMDOT_OK;
+}
+
+void tp_exchange_close(llmdot_model *m)
+{
+    if (!m->tpx) return;
+    cudaSetDevice(m->device);
+    bool safe = false;  // whether no peer can store into this rank's buffer any more
+    if (m->tpx_open) {
+        TpxArgs a = tpx_args(m, nullptr, 0);
+        tpx_close_kernel<<<1, 32, 0, m->stream>>>(a);
+        unsigned gave_up = 1;
+        if (cudaGetLastError() == cudaSuccess && cudaStreamSynchronize(m->stream) == cudaSuccess &&
+            cudaMemcpy(&gave_up, m->tpx + 12, sizeof(gave_up), cudaMemcpyDeviceToHost) == cudaSuccess)
+            safe = gave_up == 0;
+        for (int q = 0; q < m->tp && q < TPX_MAX_RANKS; q++)
+            if (q != m->tp_rank && m->tpx_peer[q]) cudaIpcCloseMemHandle(m->tpx_peer[q]);
+    }
+    // A buffer whose handle went out but whose close barrier did not complete stays allocated: a
+    // peer that opened it may still store into it.
+    if (safe) cudaFree(m->tpx);
+    m->tpx = nullptr;
+    for (int q = 0; q < TPX_MAX_RANKS; q++) m->tpx_peer[q] = nullptr;
+    m->tpx_cap = 0;
+    m->tpx_open = false;
+}
+
 int tp_allreduce_sum(llmdot_model *m, float *buf, size_t n, cudaStream_t st)
 {
     if (!m->nccl) return fail(LLMDOT_E_INVALID, "tensor parallel: call llmdot_cuda_tp_init first");
+    if (m->tpx_open && n <= m->tpx_cap && n % 4 == 0 && ((uintptr_t)buf & 15) == 0) {
+        const long long G = std::min<long long>(TPX_MAX_CTAS, ((long long)n + TPX_THREADS * 4 - 1) / (TPX_THREADS * 4));
+        if (n == 0) return LLMDOT_OK;
+        tpx_allreduce_kernel<<<(unsigned)G, TPX_THREADS, 0, st>>>(tpx_args(m, buf, (long long)n));
+        LLMDOT_CUDA_TRY(cudaGetLastError());
+        return LLMDOT_OK;
+    }
     const int r = nccl().allReduce(buf, buf, n, NCCL_FLOAT, NCCL_SUM, (NcclComm)m->nccl, st);
     return r ? nccl_fail(r, "ncclAllReduce") : LLMDOT_OK;
 }

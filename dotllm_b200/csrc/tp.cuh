@@ -33,4 +33,14 @@ int tp_allreduce_max_u64(llmdot_model *m, unsigned long long *buf, size_t n, cud
 // All-gather of `n` floats per rank: recv holds rank r's block at r*n.
 int tp_allgather(llmdot_model *m, const float *send, float *recv, size_t n, cudaStream_t st);
 
+// Peer-memory one-shot all-reduce: each rank's exchange buffer (a sequence counter and two receive
+// slots) is exported with CUDA IPC; once every rank opened every handle, tp_allreduce_sum runs as
+// one kernel that pushes this rank's partial into every peer's slot and sums the ranks' values in
+// rank order (the same order on every rank, so every rank ends with identical values).
+constexpr int TPX_HANDLE_BYTES = 128;  // cudaIpcMemHandle_t (64) + device UUID (16), zero padded
+constexpr int TPX_MAX_RANKS = 8;
+int tp_exchange_handle(llmdot_model *m, void *out128);
+int tp_exchange_open(llmdot_model *m, const void *handles);  // tp x TPX_HANDLE_BYTES, rank order
+void tp_exchange_close(llmdot_model *m);
+
 }  // namespace llmdot

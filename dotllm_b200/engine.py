@@ -45,6 +45,20 @@ class CudaModel:
         buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
         check(lib().llmdot_cuda_tp_init(self._h, buf))
 
+    def tp_exchange_handle(self) -> bytes:
+        """This rank's 128-byte exchange-buffer handle (CUDA IPC handle + GPU UUID) for the
+        peer-memory all-reduce."""
+        buf = (C.c_uint8 * 128)()
+        check(lib().llmdot_cuda_tp_exchange_handle(self._h, buf))
+        return bytes(buf)
+
+    def tp_exchange_open(self, handles) -> None:
+        """Open every rank's handle (rank order); the step's residual sums then run over peer
+        memory instead of NCCL."""
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check(lib().llmdot_cuda_tp_exchange_open(self._h, buf))
+
     @classmethod
     def from_tensors(cls, cfg: dict, tensors: Sequence[Tuple[str, int, Sequence[int], np.ndarray]],
                      device: int = 0) -> "CudaModel":

@@ -316,6 +316,17 @@ LLMDOT_API int llmdot_cuda_model_load_gguf_tp(int device, const char *path, int 
 LLMDOT_API int llmdot_cuda_tp_unique_id(uint8_t *out128);
 /* Attaches the NCCL communicator (ncclCommInitRank on the model's device). */
 LLMDOT_API int llmdot_cuda_tp_init(llmdot_model *m, const uint8_t *id128);
+/* Peer-memory all-reduce for the step's two residual sums (one kernel over NVLink instead of
+ * NCCL's all-reduce), after llmdot_cuda_tp_init: every rank exports a 128-byte handle (the CUDA IPC
+ * handle of its exchange buffer and its GPU's UUID) into out128, the host hands all ranks' handles
+ * to every rank in rank order (tp x 128 bytes), and every rank opens them; two ranks on one GPU
+ * are refused (LLMDOT_E_UNSUPPORTED).  Each sum then adds the ranks' partials in rank order on every rank (identical
+ * results everywhere); sums larger than 64 rows of the hidden state stay on NCCL, as does the
+ * argmax max-reduce.  Every wait is bounded (LLMDOT_E_TIMEOUT).  Needs at most 8 ranks whose
+ * GPUs can map each other's memory.  Once open, llmdot_cuda_model_free is collective too (it
+ * waits for every rank's last exchange before releasing the buffer): every rank frees its model. */
+LLMDOT_API int llmdot_cuda_tp_exchange_handle(llmdot_model *m, uint8_t *out128);
+LLMDOT_API int llmdot_cuda_tp_exchange_open(llmdot_model *m, const uint8_t *handles);
 /* Shard geometry of rank tp_rank (host only, no device needed): out8 = {q_lo, q_n, kv_lo, kv_n,
  * ffn_lo, ffn_n, vocab_lo, vocab_n} in rows / columns of the full matrices. */
 LLMDOT_API int llmdot_cuda_tp_shard(const llmdot_config *cfg, int tp_size, int tp_rank, int32_t *out8);

@@ -4,11 +4,15 @@ CPU part: two `gloo` ranks each ask the library (host-only entry point, no devic
 shard of several BASELINE shapes and all-gather them; the shards must tile every split
 dimension exactly once.  GPU part (skipped with fewer than two GPUs): two spawned processes
 load their shards of the tiny config, join one NCCL group and must reproduce the single-GPU
-greedy tokens and logits.
+greedy tokens and logits, once with NCCL's all-reduce for the residual sums and once with the
+peer-memory all-reduce (CUDA IPC handles exchanged through files), whose results must also equal
+the NCCL run's bit for bit (with two ranks both add the same two partials).
 """
 import json
 import os
 import socket
+import tempfile
+import time
 
 import numpy as np
 import pytest
@@ -88,7 +92,25 @@ def test_tp_shard_rejects_uneven():
         tp_shard(cfg, 4, 0)  # 128-column attn_output shards are not whole super-blocks
 
 
-def _tp_rank(rank, world, path, prompt, steps, q_in, q_out):
+def _exchange_files(m, rank, world, xdir):
+    """Every rank writes its peer all-reduce handle to a file and opens all ranks' handles."""
+    h = m.tp_exchange_handle()
+    tmp = os.path.join(xdir, f"h{rank}.tmp")
+    with open(tmp, "wb") as f:
+        f.write(h)
+    os.replace(tmp, os.path.join(xdir, f"h{rank}"))
+    handles = []
+    for r in range(world):
+        fn = os.path.join(xdir, f"h{r}")
+        t0 = time.time()
+        while not os.path.exists(fn):
+            assert time.time() - t0 < 120, "peer handle never arrived"
+            time.sleep(0.05)
+        handles.append(open(fn, "rb").read())
+    m.tp_exchange_open(handles)
+
+
+def _tp_rank(rank, world, path, prompt, steps, q_in, q_out, xdir=None):
     from dotllm_b200.engine import CudaModel, tp_unique_id
 
     m = CudaModel.load_tp(path, world, rank, device=rank)
@@ -99,6 +121,8 @@ def _tp_rank(rank, world, path, prompt, steps, q_in, q_out):
     else:
         uid = q_in.get(timeout=120)
     m.tp_init(uid)
+    if xdir is not None:
+        _exchange_files(m, rank, world, xdir)
     s = m.session(kv="f32")
     _, lg = s.prefill(prompt, want_logits=True)
     toks = s.generate(prompt, steps)
@@ -115,8 +139,12 @@ def _tp_rank(rank, world, path, prompt, steps, q_in, q_out):
     m.close()
 
 
+_NCCL_RUN = {}
+
+
 @pytest.mark.gpu
-def test_tp2_matches_single_gpu(gpu):
+@pytest.mark.parametrize("allreduce", ["nccl", "peer"])
+def test_tp2_matches_single_gpu(gpu, allreduce):
     import torch
 
     if torch.cuda.device_count() < 2:
@@ -137,7 +165,8 @@ def test_tp2_matches_single_gpu(gpu):
     ref_nxt, ref_blg = decode_batch(rss, rf, want_logits=True)
     ctx = mp.get_context("spawn")
     q_in, q_out = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_tp_rank, args=(r, 2, path, prompt, steps, q_in, q_out)) for r in range(2)]
+    xdir = tempfile.mkdtemp(prefix="tpx") if allreduce == "peer" else None
+    procs = [ctx.Process(target=_tp_rank, args=(r, 2, path, prompt, steps, q_in, q_out, xdir)) for r in range(2)]
     for p in procs:
         p.start()
     toks, lg, firsts, nxt, blg = q_out.get(timeout=300)
@@ -151,3 +180,7 @@ def test_tp2_matches_single_gpu(gpu):
     assert nxt == list(map(int, ref_nxt))
     golden = json.load(open(os.path.join(HERE, "golden", "greedy_tokens.json")))["tiny"]["tokens"]
     assert toks == golden[:steps]
+    _NCCL_RUN.setdefault(allreduce, (lg, blg))
+    if allreduce == "peer" and "nccl" in _NCCL_RUN:
+        assert np.array_equal(lg, _NCCL_RUN["nccl"][0])
+        assert np.array_equal(blg, _NCCL_RUN["nccl"][1])
