@@ -412,17 +412,38 @@ def tensor_parallel(args, world, rank, dist, local, name, n_prompt, batches, ste
                             "prefill_tok_s": B * n_prompt / pre,
                             "families_ms_per_step": {f: v["ms_per_step"] for f, v in fam.items()},
                             "collectives_per_step": fam["collective"]["launches_per_step"]}
+        # 16 greedy tokens of the first session's prompt: both all-reduce forms must agree
+        s = m.session(max_ctx=n_prompt + 32, kv=args.kv)
+        into["greedy16"] = list(map(int, s.generate(synth.prompt_tokens(cfg, n_prompt, session=0), 16)))
+        s.close()
 
     try:
         run(out["batches"])
         if world > 1 and not args.no_peer:
             # the same batches with the step's residual sums on the peer-memory all-reduce (one kernel
-            # over NVLink, CUDA IPC handles exchanged through the process group) instead of NCCL's
+            # over NVLink, CUDA IPC handles exchanged through the process group) instead of NCCL's;
+            # every rank learns whether all ranks opened it before any of them uses it
+            why = None
+            try:
+                h = m.tp_exchange_handle()
+            except Exception as e:
+                h, why = None, str(e)[:200]
             handles = [None] * world
-            dist.all_gather_object(handles, m.tp_exchange_handle())
-            m.tp_exchange_open(handles)
-            out["peer_allreduce"] = {}
-            run(out["peer_allreduce"])
+            dist.all_gather_object(handles, h)
+            if why is None and all(handles):
+                try:
+                    m.tp_exchange_open(handles)
+                except Exception as e:
+                    why = str(e)[:200]
+            elif why is None:
+                why = "a peer could not export its exchange buffer"
+            whys = [None] * world
+            dist.all_gather_object(whys, why)
+            if any(whys):
+                out["peer_allreduce"] = {"error": next(w for w in whys if w)}
+            else:
+                out["peer_allreduce"] = {}
+                run(out["peer_allreduce"])
     finally:
         m.close()
     return out
