@@ -320,11 +320,13 @@ LLMDOT_API int llmdot_cuda_tp_init(llmdot_model *m, const uint8_t *id128);
  * NCCL's all-reduce), after llmdot_cuda_tp_init: every rank exports a 128-byte handle (the CUDA IPC
  * handle of its exchange buffer and its GPU's UUID) into out128, the host hands all ranks' handles
  * to every rank in rank order (tp x 128 bytes), and every rank opens them; two ranks on one GPU
- * are refused (LLMDOT_E_UNSUPPORTED).  Each sum then adds the ranks' partials in rank order on every rank (identical
- * results everywhere); sums larger than 64 rows of the hidden state stay on NCCL, as does the
- * argmax max-reduce.  Every wait is bounded (LLMDOT_E_TIMEOUT).  Needs at most 8 ranks whose
- * GPUs can map each other's memory.  Once open, llmdot_cuda_model_free is collective too (it
- * waits for every rank's last exchange before releasing the buffer): every rank frees its model. */
+ * are refused (LLMDOT_E_UNSUPPORTED).  Each sum then adds the ranks' partials in rank order on
+ * every rank (identical results everywhere); sums larger than 64 rows of the hidden state stay on
+ * NCCL, as does the argmax max-reduce.  Every wait is bounded (10 s, then LLMDOT_E_TIMEOUT).
+ * Needs 2 to 8 ranks whose GPUs can map each other's memory.  Once open, llmdot_cuda_model_free
+ * is collective too: it waits (at most 5 s) for every rank to reach its own free before releasing
+ * the buffer, and leaves the buffer allocated if a rank never does.  Replaces no reference
+ * interface: the reference has no multi-GPU path; this is the NVLink form of the NCCL sum above. */
 LLMDOT_API int llmdot_cuda_tp_exchange_handle(llmdot_model *m, uint8_t *out128);
 LLMDOT_API int llmdot_cuda_tp_exchange_open(llmdot_model *m, const uint8_t *handles);
 /* Shard geometry of rank tp_rank (host only, no device needed): out8 = {q_lo, q_n, kv_lo, kv_n,
