@@ -423,24 +423,16 @@ def tensor_parallel(args, world, rank, dist, local, name, n_prompt, batches, ste
             # the same batches with the step's residual sums on the peer-memory all-reduce (one kernel
             # over NVLink, CUDA IPC handles exchanged through the process group) instead of NCCL's;
             # every rank learns whether all ranks opened it before any of them uses it
-            why = None
-            try:
-                h = m.tp_exchange_handle()
-            except Exception as e:
-                h, why = None, str(e)[:200]
-            handles = [None] * world
-            dist.all_gather_object(handles, h)
-            if why is None and all(handles):
-                try:
-                    m.tp_exchange_open(handles)
-                except Exception as e:
-                    why = str(e)[:200]
-            elif why is None:
-                why = "a peer could not export its exchange buffer"
-            whys = [None] * world
-            dist.all_gather_object(whys, why)
-            if any(whys):
-                out["peer_allreduce"] = {"error": next(w for w in whys if w)}
+            from dotllm_b200.engine import tp_open_peer
+
+            def gather(obj):
+                got = [None] * world
+                dist.all_gather_object(got, obj)
+                return got
+
+            why = tp_open_peer(m, gather)
+            if why:
+                out["peer_allreduce"] = {"error": why}
             else:
                 out["peer_allreduce"] = {}
                 try:

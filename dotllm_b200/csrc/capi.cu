@@ -725,6 +725,14 @@ extern "C" int llmdot_cuda_tp_exchange_open(llmdot_model *m, const uint8_t *hand
     return LLMDOT_OK;
 }
 
+extern "C" int llmdot_cuda_tp_exchange_use(llmdot_model *m, int on)
+{
+    if (!m) return fail(LLMDOT_E_INVALID, "null argument");
+    LLMDOT_TRY(tp_exchange_use(m, on != 0));
+    drop_graphs(m);  // captured steps hold the other all-reduce form
+    return LLMDOT_OK;
+}
+
 extern "C" int llmdot_cuda_model_config(const llmdot_model *m, llmdot_config *out)
 {
     if (!m || !out) return fail(LLMDOT_E_INVALID, "null argument");

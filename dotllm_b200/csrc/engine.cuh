@@ -91,7 +91,7 @@ struct llmdot_model {
     uint8_t *tpx = nullptr;
     uint8_t *tpx_peer[8] = {};
     size_t tpx_cap = 0;
-    bool tpx_open = false;
+    bool tpx_open = false, tpx_use = false;
     llmdot::StepTimer *timer = nullptr;  // attached only while llmdot_cuda_profile_step runs
 };
 

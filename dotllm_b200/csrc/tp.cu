@@ -340,7 +340,14 @@ int tp_exchange_open(llmdot_model *m, const void *handles)
     }
     peer[m->tp_rank] = m->tpx;
     for (int q = 0; q < TPX_MAX_RANKS; q++) m->tpx_peer[q] = peer[q];
-    m->tpx_open = true;
+    m->tpx_open = m->tpx_use = true;
+    return LLMDOT_OK;
+}
+
+int tp_exchange_use(llmdot_model *m, bool on)
+{
+    if (on && !m->tpx_open) return fail(LLMDOT_E_INVALID, "peer all-reduce: not open");
+    m->tpx_use = on;
     return LLMDOT_OK;
 }
 
@@ -365,13 +372,13 @@ void tp_exchange_close(llmdot_model *m)
     m->tpx = nullptr;
     for (int q = 0; q < TPX_MAX_RANKS; q++) m->tpx_peer[q] = nullptr;
     m->tpx_cap = 0;
-    m->tpx_open = false;
+    m->tpx_open = m->tpx_use = false;
 }
 
 int tp_allreduce_sum(llmdot_model *m, float *buf, size_t n, cudaStream_t st)
 {
     if (!m->nccl) return fail(LLMDOT_E_INVALID, "tensor parallel: call llmdot_cuda_tp_init first");
-    if (m->tpx_open && n <= m->tpx_cap && n % 4 == 0 && ((uintptr_t)buf & 15) == 0) {
+    if (m->tpx_use && n <= m->tpx_cap && n % 4 == 0 && ((uintptr_t)buf & 15) == 0) {
         const long long G = std::min<long long>(TPX_MAX_CTAS, ((long long)n + TPX_THREADS * 4 - 1) / (TPX_THREADS * 4));
         if (n == 0) return LLMDOT_OK;
         tpx_allreduce_kernel<<<(unsigned)G, TPX_THREADS, 0, st>>>(tpx_args(m, buf, (long long)n));

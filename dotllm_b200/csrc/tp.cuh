@@ -41,6 +41,7 @@ constexpr int TPX_HANDLE_BYTES = 128;  // cudaIpcMemHandle_t (64) + device UUID 
 constexpr int TPX_MAX_RANKS = 8;
 int tp_exchange_handle(llmdot_model *m, void *out128);
 int tp_exchange_open(llmdot_model *m, const void *handles);  // tp x TPX_HANDLE_BYTES, rank order
+int tp_exchange_use(llmdot_model *m, bool on);  // whether the step's sums use it (after open)
 void tp_exchange_close(llmdot_model *m);
 
 }  // namespace llmdot

@@ -59,6 +59,10 @@ class CudaModel:
         buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
         check(lib().llmdot_cuda_tp_exchange_open(self._h, buf))
 
+    def tp_exchange_use(self, on: bool) -> None:
+        """Residual sums on the opened peer-memory all-reduce (True) or on NCCL (False)."""
+        check(lib().llmdot_cuda_tp_exchange_use(self._h, 1 if on else 0))
+
     @classmethod
     def from_tensors(cls, cfg: dict, tensors: Sequence[Tuple[str, int, Sequence[int], np.ndarray]],
                      device: int = 0) -> "CudaModel":
@@ -249,6 +253,38 @@ def gguf_config(path: str) -> dict:
     c = LlmdotConfig()
     check(lib().llmdot_cuda_gguf_config(path.encode(), C.byref(c)))
     return c.as_dict()
+
+
+def tp_open_peer(model, all_gather) -> Optional[str]:
+    """Collective switch of a tensor-parallel group's residual sums to the peer-memory all-reduce.
+
+    Every rank calls it with its model and `all_gather(obj) -> [obj of rank 0, .., rank tp-1]`
+    (e.g. torch.distributed.all_gather_object).  Each rank exports its handle, the handles are
+    gathered, each rank opens them, and the ranks then agree: the peer form is used only if every
+    rank opened it; otherwise the ranks that did open turn it off again, so that all ranks keep
+    NCCL.  Returns None on success, else the first failing rank's reason.
+    """
+    why = None
+    try:
+        h = model.tp_exchange_handle()
+    except Exception as e:  # CudaBackendError: unsupported TP size, no device memory, ...
+        h, why = None, str(e)[:300]
+    handles = all_gather(h)
+    opened = False
+    if why is None:
+        if all(x is not None for x in handles):
+            try:
+                model.tp_exchange_open(list(handles))
+                opened = True
+            except Exception as e:
+                why = str(e)[:300]
+        else:
+            why = "a peer could not export its exchange buffer"
+    whys = all_gather(why)
+    first = next((w for w in whys if w), None)
+    if first is not None and opened:
+        model.tp_exchange_use(False)
+    return first
 
 
 def tp_unique_id() -> bytes:

@@ -113,6 +113,7 @@ _SIGS = {
     "llmdot_cuda_tp_init": (C.c_int, [VP, C.POINTER(C.c_uint8)]),
     "llmdot_cuda_tp_exchange_handle": (C.c_int, [VP, C.POINTER(C.c_uint8)]),
     "llmdot_cuda_tp_exchange_open": (C.c_int, [VP, C.POINTER(C.c_uint8)]),
+    "llmdot_cuda_tp_exchange_use": (C.c_int, [VP, C.c_int]),
     "llmdot_cuda_tp_shard": (C.c_int, [C.POINTER(LlmdotConfig), C.c_int, C.c_int, I32P]),
     "llmdot_cuda_profile_step": (C.c_int, [C.POINTER(VP), C.c_int, I32P, I32P, C.c_int, F32P, C.POINTER(C.c_int)]),
     "llmdot_cuda_profile_matvec": (C.c_int, [VP, C.c_char_p, C.c_int, C.c_int, F32P, C.POINTER(C.c_uint64)]),

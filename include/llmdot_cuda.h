@@ -329,6 +329,10 @@ LLMDOT_API int llmdot_cuda_tp_init(llmdot_model *m, const uint8_t *id128);
  * interface: the reference has no multi-GPU path; this is the NVLink form of the NCCL sum above. */
 LLMDOT_API int llmdot_cuda_tp_exchange_handle(llmdot_model *m, uint8_t *out128);
 LLMDOT_API int llmdot_cuda_tp_exchange_open(llmdot_model *m, const uint8_t *handles);
+/* Whether the step's residual sums use the opened peer-memory all-reduce (on = 1, the state after
+ * open) or NCCL's (on = 0).  Every rank must make the same choice before its next step: a rank
+ * whose open succeeded turns it off when another rank's open failed. */
+LLMDOT_API int llmdot_cuda_tp_exchange_use(llmdot_model *m, int on);
 /* Shard geometry of rank tp_rank (host only, no device needed): out8 = {q_lo, q_n, kv_lo, kv_n,
  * ffn_lo, ffn_n, vocab_lo, vocab_n} in rows / columns of the full matrices. */
 LLMDOT_API int llmdot_cuda_tp_shard(const llmdot_config *cfg, int tp_size, int tp_rank, int32_t *out8);

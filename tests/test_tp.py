@@ -110,6 +110,83 @@ def _exchange_files(m, rank, world, xdir):
     m.tp_exchange_open(handles)
 
 
+class _FakeExchange:
+    """Stands in for a model's exchange entry points on CPU; `fail` names the call that raises."""
+
+    def __init__(self, rank, fail=None):
+        self.rank, self.fail, self.calls = rank, fail, []
+
+    def tp_exchange_handle(self):
+        self.calls.append("handle")
+        if self.fail == "handle":
+            raise RuntimeError(f"rank {self.rank}: export refused")
+        return bytes([self.rank]) * 128
+
+    def tp_exchange_open(self, handles):
+        self.calls.append(("open", tuple(h[0] for h in handles)))
+        if self.fail == "open":
+            raise RuntimeError(f"rank {self.rank}: open refused")
+
+    def tp_exchange_use(self, on):
+        self.calls.append(("use", on))
+
+
+def _open_peer_rank(rank, world, port, fail_rank, fail_call, q):
+    import torch.distributed as dist
+
+    from dotllm_b200.engine import tp_open_peer
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        m = _FakeExchange(rank, fail_call if rank == fail_rank else None)
+
+        def gather(obj):
+            got = [None] * world
+            dist.all_gather_object(got, obj)
+            return got
+
+        why = tp_open_peer(m, gather)
+        q.put((rank, why, m.calls))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_rank,fail_call", [(-1, None), (1, "handle"), (0, "open"), (2, "open")])
+def test_tp_open_peer_agreement_gloo(fail_rank, fail_call):
+    """Every rank ends with the same answer: the peer all-reduce on everywhere, or off everywhere
+    (ranks whose own open succeeded turn it off again when another rank failed)."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_open_peer_rank, args=(r, world, port, fail_rank, fail_call, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    whys = {why for _, why, _ in got}
+    assert len(whys) == 1
+    why = whys.pop()
+    if fail_rank < 0:
+        assert why is None
+        for rank, _, calls in got:
+            assert calls == ["handle", ("open", (0, 1, 2))]
+        return
+    assert f"rank {fail_rank}" in why or "could not export" in why
+    for rank, _, calls in got:
+        opened = any(c[0] == "open" for c in calls if isinstance(c, tuple))
+        if fail_call == "handle":
+            assert not opened  # nobody opens an incomplete set of handles
+            assert ("use", False) not in calls
+        elif rank == fail_rank:
+            assert calls[-1] == ("open", (0, 1, 2))  # its open raised: nothing to turn off
+        else:
+            assert calls[-1] == ("use", False)
+
+
 def _tp_rank(rank, world, path, prompt, steps, q_in, q_out, xdir=None):
     from dotllm_b200.engine import CudaModel, tp_unique_id
 
