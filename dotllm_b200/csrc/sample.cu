@@ -11,10 +11,11 @@
 //   3. VectorMath.Softmax over the k sorted values (ExpApprox in the 8-wide lanes, exp in the tail,
 //      the 8 lane sums added as ((0+1)+(2+3))+((4+5)+(6+7))), then the first index whose running
 //      sum of probabilities reaches the draw r (SampleFromProbabilities).
-// Temperature <= 0 is the greedy argmax of the softcapped row (lowest index on ties).  Equal values
-// at the k-th place are taken lowest index first and equal winners are ordered by index; the
-// reference orders them by its replacement scan instead (FindTopK :83-127), which only matters for
-// exactly tied logits.
+// Temperature <= 0 is the greedy argmax of the softcapped row (lowest index on ties).  When two of
+// the k winners have equal values, or equal values straddle the k-th place, which of them win and
+// their order come from FindTopK's replacement scan (:83-127), so such rows replay it exactly
+// (topk_replay: one warp scanning the row in index order); rows without ties skip the replay, as
+// their winners and order are then unique.
 //
 // top_k <= 0 or top_k >= n (Sampler.cs:42-61): VectorMath.Softmax over the whole row (the FindMax
 // lane rule, ExpApprox in the 8-wide lanes with the lanes' running sums, exp in the tail), then
@@ -155,6 +156,105 @@ __device__ __forceinline__ RowValues row_values(const SampleArgs &a, int row)
     return rv;
 }
 
+// First slot holding the smallest of tv[0..k) (FindTopK's minIdx scan, :93-98: a later slot
+// replaces the current one only when strictly smaller, so equal values keep the lowest slot),
+// reduced over the calling warp; every lane gets the same (value, slot).
+__device__ __forceinline__ void topk_min(const float *tv, int k, int lane, float &minv, int &mins)
+{
+    float bv = 0.0f;
+    int bs = INT_MAX;
+    for (int j = lane; j < k; j += 32) {
+        const float t = tv[j];
+        if (bs == INT_MAX || t < bv) {
+            bv = t;
+            bs = j;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int os = __shfl_xor_sync(0xffffffffu, bs, o);
+        if (os != INT_MAX && (bs == INT_MAX || ov < bv || (ov == bv && os < bs))) {
+            bv = ov;
+            bs = os;
+        }
+    }
+    minv = bv;
+    mins = bs;
+}
+
+// FindTopK (Sampler.cs:83-127) replayed exactly, for rows whose winners tie: slots 0..k-1 start
+// as tokens 0..k-1; each later token, in index order, replaces the first slot holding the minimum
+// when it is strictly larger; the slots are then ordered by value, equal values by slot (the
+// insertion sort is stable).  Warp 0 scans the row 32 tokens at a time and handles the tokens
+// above the current minimum lane by lane in index order (re-testing them after each replacement);
+// the whole block then sorts (value, slot) pairs.  Leaves the k winners in cand as
+// (key << 32 | ~token), sorted.  Rows are taken NaN-free (a NaN never enters, as in the reference,
+// but one among the first k slots is ordered differently).
+__device__ void topk_replay(const RowValues &rv, int n, int k, int k2, unsigned long long *cand, int *tix,
+                            float *tv)
+{
+    const int tid = threadIdx.x;
+    if (tid < 32) {
+        const int lane = tid;
+        for (int j = lane; j < k; j += 32) {
+            tix[j] = j;
+            tv[j] = rv.value(j);
+        }
+        __syncwarp();
+        float minv;
+        int mins;
+        topk_min(tv, k, lane, minv, mins);
+        for (int base = k; base < n; base += 4 * 32) {
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = base + u * 32 + lane;
+                v[u] = i < n ? rv.value(i) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int b = base + u * 32;
+                unsigned m = __ballot_sync(0xffffffffu, b + lane < n && v[u] > minv);
+                while (m) {
+                    const int l = __ffs(m) - 1;
+                    const float vl = __shfl_sync(0xffffffffu, v[u], l);
+                    if (lane == 0) {
+                        tix[mins] = b + l;
+                        tv[mins] = vl;
+                    }
+                    __syncwarp();
+                    topk_min(tv, k, lane, minv, mins);
+                    m &= ~(1u << l);
+                    m &= __ballot_sync(0xffffffffu, b + lane < n && v[u] > minv);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    // (value, slot) pairs: descending value (-0 as +0), then ascending slot
+    for (int j = tid; j < k2; j += SMP_THREADS)
+        cand[j] = j < k ? ((unsigned long long)float_key(tv[j] == 0.0f ? 0.0f : tv[j]) << 32) | (uint32_t)~j : 0ull;
+    __syncthreads();
+    for (int size = 2; size <= k2; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < k2 / 2; i += SMP_THREADS) {
+                const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+                const bool desc = (lo & size) == 0;
+                const unsigned long long A = cand[lo], B = cand[hi];
+                if ((A < B) == desc) {
+                    cand[lo] = B;
+                    cand[hi] = A;
+                }
+            }
+            __syncthreads();
+        }
+    for (int j = tid; j < k; j += SMP_THREADS) {
+        const int slot = (int)~(uint32_t)cand[j];
+        cand[j] = ((unsigned long long)float_key(tv[slot]) << 32) | (uint32_t)~tix[slot];
+    }
+    __syncthreads();
+}
+
 __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k2)
 {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -210,6 +310,8 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
     const int k = a.top_k;
     int sort_n = k2;  // entries of cand to sort
     bool fast = false;
+    int ncand = 0;         // fast path: candidates collected (sorted, so cand[k] is the (k+1)-th largest)
+    bool thr_tie = false;  // radix path: more keys equal the k-th than places are left for them
     // ---- fast path: a threshold tau from a strided sample, then one pass collecting every key
     // >= tau.  When at least k keys reach tau, the k largest (ties included) are all among them,
     // so sorting the candidates gives exactly the radix select's answer; otherwise (tau above
@@ -258,6 +360,7 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
         __syncthreads();
         const int got = hist[0];
         __syncthreads();
+        ncand = got;
         if (got >= k && got <= SMP_CAND) {
             int c2 = k2;
             while (c2 < got) c2 <<= 1;
@@ -313,6 +416,7 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
     }
     const uint32_t thr = prefix;
     const int eq_total = hist[259], eq_take = need;  // keys equal to thr: all of them / how many to take
+    thr_tie = eq_take < eq_total;
     // ---- the k winners: every key above thr, and the eq_take lowest indices with key == thr
     if (tid == 0) hist[0] = 0;
     for (int i = tid; i < k2; i += SMP_THREADS) cand[i] = 0ull;
@@ -360,6 +464,18 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(SampleArgs a, int k
             }
             __syncthreads();
         }
+    // ---- exactly equal values among the winners or across the k-th place: FindTopK's order
+    if (tid == 0) {
+        const float kth = key_float((uint32_t)(cand[k - 1] >> 32));
+        // -0 and +0 compare equal in the reference but have distinct keys: a zero k-th value
+        // may hide a tie across the k-th place, so it is treated as one
+        hist[0] = thr_tie || kth == 0.0f || (fast && ncand > k && key_float((uint32_t)(cand[k] >> 32)) == kth);
+    }
+    __syncthreads();
+    for (int j = 1 + tid; j < k; j += SMP_THREADS)  // sorted: equal values are neighbours
+        if (key_float((uint32_t)(cand[j - 1] >> 32)) == key_float((uint32_t)(cand[j] >> 32))) hist[0] = 1;
+    __syncthreads();
+    if (hist[0]) topk_replay(rv, n, k, k2, cand, (int *)skey, prob);
     // ---- VectorMath.Softmax over the k values (Sampler.cs:39), then the pick (:153-165)
     if (tid < 32) {
         const int lane = tid;

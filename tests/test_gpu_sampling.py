@@ -6,7 +6,8 @@ softmax's 8-wide ExpApprox lanes are bit-exact on the device; only its MathF.Exp
 k mod 8 entries) may differ by an ulp, so a draw within an ulp of a cumulative-probability
 boundary could in principle pick the neighbour.  The seeds and draws are fixed, and none of them
 lands that close.  The full-row path (top_k <= 0 or >= n) is also checked on rows with many exactly
-tied probabilities, where the nucleus replays the reference's selection sort.
+tied probabilities, where the nucleus replays the reference's selection sort, and the top-k path on
+rows with tied winners, where the device replays FindTopK's replacement scan.
 """
 import numpy as np
 import pytest
@@ -86,6 +87,24 @@ def test_sample_full_row_ties(backend, vocab):
             want = O.sample(logits, _oracle_opts(o), recent, r)
             got = backend.sample(logits, o, recent, r)
             assert got == want, (vocab, trial, top_p, r, got, want)
+
+
+@pytest.mark.parametrize("vocab", [1000, 32064, 128256])
+@pytest.mark.parametrize("top_k", [2, 5, 40, 200, 1024])
+def test_sample_top_k_ties(backend, vocab, top_k):
+    """Top-k on rows whose values repeat (a few levels, signed zeros among them): the winners tie,
+    within the top k and across the k-th place, and the device replays FindTopK's replacement scan
+    (Sampler.cs:83-127), so both which equal values win and their order are the reference's."""
+    rng = np.random.default_rng(7 * vocab + top_k)
+    for trial, (levels, temp) in enumerate([(3, 0.7), (8, 1.0), (60, 1.3)]):
+        logits = (rng.integers(-levels, levels + 1, size=vocab) * 0.25).astype(np.float32)
+        logits[rng.integers(0, vocab, size=20)] = -0.0
+        recent = rng.integers(0, vocab, size=24).astype(np.int32)
+        o = _opts(top_k=top_k, top_p=1.0, temperature=temp, repeat_penalty=1.1, repeat_window=32)
+        for r in (0.03, 0.5, 0.97):
+            want = O.sample(logits, _oracle_opts(o), recent, r)
+            got = backend.sample(logits, o, recent, r)
+            assert got == want, (vocab, top_k, trial, r, got, want)
 
 
 @pytest.mark.parametrize("name", ["micro", "micro-gemma", "tiny"])
