@@ -191,6 +191,45 @@ __device__ bool tpx_wait4(const uint8_t *p, unsigned gen, float4 &v, volatile un
     return true;
 }
 
+// Polls the two words at p until both carry tag gen; their low halves, or false as above.
+__device__ bool tpx_wait2(const uint8_t *p, unsigned gen, unsigned &lo0, unsigned &lo1, volatile unsigned *hdr,
+                          int *err)
+{
+    unsigned long long w0, w1, t0 = 0;
+    for (unsigned it = 0;; it++) {
+        tpx_load2(p, w0, w1);
+        if ((unsigned)(w0 >> 32) == gen && (unsigned)(w1 >> 32) == gen) break;
+        if ((it & 255) == 0) {
+            const unsigned long long t = tpx_now();
+            if (it == 0) t0 = t;
+            if (hdr[2] || t - t0 > TPX_WAIT_NS) {
+                hdr[2] = 1;
+                atomicCAS(err, 0, TPX_ERR_TIMEOUT);
+                lo0 = lo1 = 0;
+                return false;
+            }
+        }
+    }
+    lo0 = (unsigned)w0;
+    lo1 = (unsigned)w1;
+    return true;
+}
+
+// The last CTA of an exchange to finish publishes its generation (every CTA read the old one
+// before arriving).
+__device__ __forceinline__ void tpx_finish(uint8_t *own, volatile unsigned *hdr, unsigned gen)
+{
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd((unsigned *)(own + 4), 1u) == gridDim.x - 1) {
+            hdr[1] = 0;
+            hdr[0] = gen;
+            __threadfence();
+        }
+    }
+}
+
 __device__ __forceinline__ unsigned long long tpx_word(unsigned gen, float x)
 {
     return ((unsigned long long)gen << 32) | __float_as_uint(x);
@@ -235,16 +274,36 @@ __global__ void __launch_bounds__(TPX_THREADS) tpx_allreduce_kernel(TpxArgs a)
         }
         *(float4 *)(a.buf + e) = s;
     }
-    // the last CTA to finish publishes the generation (every CTA read the old one before arriving)
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        if (atomicAdd((unsigned *)(a.own + 4), 1u) == gridDim.x - 1) {
-            hdr[1] = 0;
-            hdr[0] = gen;
-            __threadfence();
+    tpx_finish(a.own, hdr, gen);
+}
+
+// Max of n packed argmax keys (value key << 32 | ~index) across the ranks: one exchange of the
+// same protocol, each key sent as two tagged words (high half, low half) in slot elements 2j, 2j+1.
+__global__ void __launch_bounds__(TPX_THREADS) tpx_allmax_u64_kernel(TpxArgs a, unsigned long long *keys, int n)
+{
+    volatile unsigned *hdr = (volatile unsigned *)a.own;
+    const unsigned gen = hdr[0] + 1;
+    const long long par = gen & 1;
+    const int j = blockIdx.x * TPX_THREADS + threadIdx.x;
+    if (j < n) {
+        const unsigned long long k = keys[j];
+        const unsigned long long w0 = ((unsigned long long)gen << 32) | (unsigned)(k >> 32),
+                                 w1 = ((unsigned long long)gen << 32) | (unsigned)k;
+        const size_t src_off = TPX_DATA + (size_t)((par * a.tp + a.rank) * a.cap + 2 * (long long)j) * 8;
+        for (int q = 0; q < a.tp; q++)
+            if (q != a.rank) tpx_store2(a.peer[q] + src_off, w0, w1);
+        unsigned long long best = k;
+        for (int q = 0; q < a.tp; q++) {
+            if (q == a.rank) continue;
+            unsigned hi, lo;
+            tpx_wait2(a.own + TPX_DATA + (size_t)((par * a.tp + q) * a.cap + 2 * (long long)j) * 8, gen, hi, lo, hdr,
+                      a.err);
+            const unsigned long long kq = ((unsigned long long)hi << 32) | lo;
+            best = kq > best ? kq : best;
         }
+        keys[j] = best;
     }
+    tpx_finish(a.own, hdr, gen);
 }
 
 // Close barrier: every rank marks its arrival in every peer's header and waits (bounded) for the
@@ -392,6 +451,14 @@ int tp_allreduce_sum(llmdot_model *m, float *buf, size_t n, cudaStream_t st)
 int tp_allreduce_max_u64(llmdot_model *m, unsigned long long *buf, size_t n, cudaStream_t st)
 {
     if (!m->nccl) return fail(LLMDOT_E_INVALID, "tensor parallel: call llmdot_cuda_tp_init first");
+    // one key per thread, at most one CTA per SM (every CTA resident, as for the sums)
+    if (m->tpx_use && 2 * n <= m->tpx_cap && n <= (size_t)TPX_MAX_CTAS * TPX_THREADS) {
+        if (n == 0) return LLMDOT_OK;
+        const unsigned G = (unsigned)((n + TPX_THREADS - 1) / TPX_THREADS);
+        tpx_allmax_u64_kernel<<<G, TPX_THREADS, 0, st>>>(tpx_args(m, nullptr, 0), buf, (int)n);
+        LLMDOT_CUDA_TRY(cudaGetLastError());
+        return LLMDOT_OK;
+    }
     const int r = nccl().allReduce(buf, buf, n, NCCL_UINT64, NCCL_MAX, (NcclComm)m->nccl, st);
     return r ? nccl_fail(r, "ncclAllReduce") : LLMDOT_OK;
 }

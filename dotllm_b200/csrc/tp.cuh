@@ -36,7 +36,8 @@ int tp_allgather(llmdot_model *m, const float *send, float *recv, size_t n, cuda
 // Peer-memory one-shot all-reduce: each rank's exchange buffer (a sequence counter and two receive
 // slots) is exported with CUDA IPC; once every rank opened every handle, tp_allreduce_sum runs as
 // one kernel that pushes this rank's partial into every peer's slot and sums the ranks' values in
-// rank order (the same order on every rank, so every rank ends with identical values).
+// rank order (the same order on every rank, so every rank ends with identical values);
+// tp_allreduce_max_u64 runs over the same buffers.
 constexpr int TPX_HANDLE_BYTES = 128;  // cudaIpcMemHandle_t (64) + device UUID (16), zero padded
 constexpr int TPX_MAX_RANKS = 8;
 int tp_exchange_handle(llmdot_model *m, void *out128);

@@ -321,8 +321,9 @@ LLMDOT_API int llmdot_cuda_tp_init(llmdot_model *m, const uint8_t *id128);
  * handle of its exchange buffer and its GPU's UUID) into out128, the host hands all ranks' handles
  * to every rank in rank order (tp x 128 bytes), and every rank opens them; two ranks on one GPU
  * are refused (LLMDOT_E_UNSUPPORTED).  Each sum then adds the ranks' partials in rank order on
- * every rank (identical results everywhere); sums larger than 64 rows of the hidden state stay on
- * NCCL, as does the argmax max-reduce.  Every wait is bounded (10 s, then LLMDOT_E_TIMEOUT).
+ * every rank (identical results everywhere), and the greedy argmax's max-reduce of the ranks' keys
+ * runs over the same buffers; sums larger than 64 rows of the hidden state stay on NCCL, as do the
+ * logits all-gathers.  Every wait is bounded (10 s, then LLMDOT_E_TIMEOUT).
  * Needs 2 to 8 ranks whose GPUs can map each other's memory.  Once open, llmdot_cuda_model_free
  * is collective too: it waits (at most 5 s) for every rank to reach its own free before releasing
  * the buffer, and leaves the buffer allocated if a rank never does.  Replaces no reference
