@@ -300,13 +300,13 @@ LLMDOT_API int llmdot_cuda_model_matvec(llmdot_model *m, const char *tensor, con
                                         int mode, const float *norm_w, float *y);
 
 /* ---- tensor parallelism (Megatron-style, one process per GPU) ---------------------------
- * The one-process-per-GPU form of the survey's `_tp_init(model, tpSize, devices)`: every rank
- * loads ITS shard of the model, rank 0 creates an NCCL unique id that the host distributes
+ * One process per GPU (in place of a single-process `tp_init(model, tpSize, devices)`): every
+ * rank loads ITS shard of the model, rank 0 creates an NCCL unique id that the host distributes
  * (e.g. with torch.distributed), and every rank attaches it.  Shards: attn_q/k/v and
  * ffn_gate/up by output rows (whole heads), attn_output and ffn_down by input columns, the
  * logits head by vocabulary rows; the embedding and norms stay whole.  Each decode step then
- * does one in-place NCCL all-reduce of the residual after attn_output and one after ffn_down,
- * and a max all-reduce of the packed argmax keys.  All ranks must make the same prefill /
+ * does one in-place all-reduce of the residual after attn_output and one after ffn_down, and a
+ * max all-reduce of the packed argmax keys (NCCL's, or the peer exchange's once it is open).  All ranks must make the same prefill /
  * decode / generate calls in the same order (they contain collectives); logits read back under
  * TP are gathered from every rank (needs vocab % tp_size == 0).  llmdot_cuda_model_config
  * returns the full model's configuration. */
