@@ -1,5 +1,6 @@
 """Host-side pieces of bench.py that need no GPU: the clock sampler's NVML polling and its
-summary, against a fake NVML module (read-only queries only; nothing is set)."""
+summary, against a fake NVML module (read-only queries only; nothing is set), and the reference
+arm's JSON line (the CPU restatement on the tiny config), alone and under torchrun."""
 import sys
 import time
 import types
@@ -97,3 +98,56 @@ def test_nvml_device_found_by_uuid(monkeypatch):
     with bench.ClockSampler(1, uuid="not-present") as c:
         time.sleep(0.03)
     assert set(seen) == {("dev", 1)}
+
+
+def _json_lines(out):
+    import json
+    return [json.loads(line) for line in out.splitlines() if line.startswith("{")]
+
+
+def _check_reference_line(line, n_gpus):
+    assert line["impl"] == "reference"
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["n_gpus"] == n_gpus and line["steps"] == 2 and line["warmup"] == 3
+    assert line["value"] > 0 and line["higher_is_better"] is True
+    assert line["cpu_baseline"]["kind"] in ("port", "reference") and line["cpu_baseline"]["cores"] >= 1
+    assert line["cpu_baseline"]["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+    assert line["config"]["model"] == "tiny"
+
+
+def test_reference_arm_line_one_process():
+    """`bench.py --impl reference` times the CPU restatement and prints one contract line."""
+    import os
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", "tiny", "--steps", "2",
+                        "--warmup", "3"], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = _json_lines(r.stdout)
+    assert len(lines) == 1
+    _check_reference_line(lines[0], 1)
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    """Launched as the driver launches it for N > 1: rank 0 alone runs and prints, the other rank
+    exits 0 without work."""
+    import os
+    import socket
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(port), "bench.py", "--impl", "reference",
+                        "--config", "tiny", "--gpus", "2", "--steps", "2", "--warmup", "3"],
+                       cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = _json_lines(r.stdout)
+    assert len(lines) == 1
+    _check_reference_line(lines[0], 2)
